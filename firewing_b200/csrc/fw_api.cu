@@ -1,0 +1,545 @@
+// fw_api.cu -- the C ABI of include/fwmoe.h.
+//
+// Host-side runtime around the kernels: handle lifetime, device weight
+// ownership, scratch sizing, the bf16 SiLU/sigmoid tables, status mapping.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "fw_kernels.h"
+#include "fwmoe.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define FW_CUDA(call)                                                                    \
+  do {                                                                                   \
+    const cudaError_t e_ = (call);                                                       \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(e_ == cudaErrorMemoryAllocation ? FW_ENOMEM : FW_ECUDA,                \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                   \
+  } while (0)
+
+// bf16 helpers with the reference arithmetic (src/expert.rs:315-322).
+uint16_t host_to_bf16(float v) {
+  uint32_t b;
+  std::memcpy(&b, &v, sizeof b);
+  return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+}
+float host_from_bf16(uint16_t v) {
+  const uint32_t b = static_cast<uint32_t>(v) << 16;
+  float f;
+  std::memcpy(&f, &b, sizeof f);
+  return f;
+}
+
+// The two 65,536-entry tables, built with the host libm exactly as the
+// reference builds its SiLU table (src/metal_moe.rs:385-392) and as
+// sigmoid_bf16 rounds (src/expert.rs:573-576).
+void build_tables(std::vector<uint16_t>& silu, std::vector<uint16_t>& sigmoid) {
+  silu.resize(65536);
+  sigmoid.resize(65536);
+  for (uint32_t bits = 0; bits < 65536u; ++bits) {
+    const float g = host_from_bf16(static_cast<uint16_t>(bits));
+    silu[bits] = host_to_bf16(g / (1.0f + std::exp(-g)));
+    sigmoid[bits] = host_to_bf16(1.0f / (1.0f + std::exp(-g)));
+  }
+}
+
+// Per-device tables and status word for the handle-free primitives.
+struct DeviceCommon {
+  uint16_t* silu = nullptr;
+  uint16_t* sigmoid = nullptr;
+  int* err = nullptr;
+};
+std::mutex g_common_mu;
+std::map<int, DeviceCommon> g_common;
+
+int device_common(int device, DeviceCommon** out) {
+  std::lock_guard<std::mutex> lock(g_common_mu);
+  auto it = g_common.find(device);
+  if (it == g_common.end()) {
+    std::vector<uint16_t> silu, sig;
+    build_tables(silu, sig);
+    DeviceCommon c;
+    FW_CUDA(cudaMalloc(&c.silu, 65536 * sizeof(uint16_t)));
+    FW_CUDA(cudaMalloc(&c.sigmoid, 65536 * sizeof(uint16_t)));
+    FW_CUDA(cudaMalloc(&c.err, sizeof(int)));
+    FW_CUDA(cudaMemcpy(c.silu, silu.data(), 65536 * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    FW_CUDA(cudaMemcpy(c.sigmoid, sig.data(), 65536 * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    FW_CUDA(cudaMemset(c.err, 0, sizeof(int)));
+    it = g_common.emplace(device, c).first;
+  }
+  *out = &it->second;
+  return FW_OK;
+}
+
+int map_device_error(int code) {
+  switch (code) {
+    case fw::kErrNone: return FW_OK;
+    case fw::kErrNanLogits: return fail(FW_ENAN, "router received NaN logits");
+    case fw::kErrTimeout: return fail(FW_ETIMEOUT, "a bounded device wait timed out");
+    case fw::kErrBadIndex: return fail(FW_EINVAL, "expert index out of range on device");
+    case fw::kErrCapacity: return fail(FW_EINVAL, "token/expert pairs exceeded scratch capacity");
+    default: return fail(FW_ECUDA, "unknown device status " + std::to_string(code));
+  }
+}
+
+// SplitMix64 keyed stream (Steele, Lea, Flood 2014); the device kernel
+// applies the same finaliser per element.
+uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+constexpr uint64_t kGamma = 0x9E3779B97F4A7C15ull;
+uint64_t synth_key(uint64_t seed, uint32_t tensor) {
+  return mix64(mix64(seed + kGamma) + static_cast<uint64_t>(tensor) * kGamma + kGamma);
+}
+float synth_scale(float std_dev) {
+  const double sd = std::sqrt((65536.0 * 65536.0 - 1.0) / 3.0);
+  return static_cast<float>(static_cast<double>(std_dev) / sd);
+}
+
+struct OwnedLayer {
+  fw::LayerWeights w;
+  std::vector<void*> owned;
+  bool loaded = false;
+};
+
+}  // namespace
+
+struct fw_moe {
+  fw_moe_config cfg{};
+  int device = 0;
+  fw::Shape shape{};
+  std::vector<OwnedLayer> layers;
+  fw::Luts luts{};
+  uint16_t* silu = nullptr;
+  uint16_t* sigmoid = nullptr;
+  fw::Scratch sc{};
+  std::vector<void*> scratch_owned;
+  uint16_t* x_dev = nullptr;
+  uint16_t* y_dev = nullptr;
+  int32_t* idx_dev = nullptr;
+  uint16_t* score_dev = nullptr;
+  cudaStream_t stream = nullptr;
+  uint64_t bytes = 0;
+  bool profile = false;
+  cudaEvent_t stage_ev[fw::kStages + 1] = {};
+};
+
+namespace {
+
+template <typename T>
+int alloc(fw_moe* h, T** p, size_t count, std::vector<void*>& owned) {
+  void* v = nullptr;
+  FW_CUDA(cudaMalloc(&v, count * sizeof(T) > 0 ? count * sizeof(T) : 16));
+  owned.push_back(v);
+  h->bytes += count * sizeof(T);
+  *p = static_cast<T*>(v);
+  return FW_OK;
+}
+
+#define FW_TRY(call)            \
+  do {                          \
+    const int rc_ = (call);     \
+    if (rc_ != FW_OK) return rc_; \
+  } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+int check_config(const fw_moe_config* c) {
+  if (c == nullptr) return fail(FW_EINVAL, "config is null");
+  if (c->hidden <= 0 || c->hidden % 64 != 0 || c->hidden > 8192)
+    return fail(FW_EINVAL, "hidden must be a positive multiple of 64, at most 8192");
+  if (c->intermediate <= 0 || c->intermediate % 64 != 0 || c->shared_intermediate <= 0 ||
+      c->shared_intermediate % 64 != 0)
+    return fail(FW_EINVAL, "intermediate sizes must be positive multiples of 64");
+  if (c->experts <= 0 || c->experts % 32 != 0 || c->experts > 1024)
+    return fail(FW_EINVAL, "experts must be a multiple of 32, at most 1024");
+  if (c->top_k < 1 || c->top_k > 32 || c->top_k > c->experts)
+    return fail(FW_EINVAL, "top_k must be in [1, min(32, experts)]");
+  if (c->max_tokens < 1 || c->max_tokens > 256)
+    return fail(FW_EINVAL, "max_tokens must be in [1, 256]");
+  if (c->layers < 1) return fail(FW_EINVAL, "layers must be >= 1");
+  // shared memory of the GEMV stages: 8 tokens x cols x f32
+  if (8ull * c->hidden * 4 > 200 * 1024) return fail(FW_EINVAL, "hidden too large for staging");
+  return FW_OK;
+}
+
+int check_handle(const fw_moe* h, int32_t layer) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  if (layer < 0 || layer >= h->cfg.layers) return fail(FW_EINVAL, "layer out of range");
+  if (!h->layers[layer].loaded) return fail(FW_EINVAL, "layer not loaded");
+  return FW_OK;
+}
+
+int free_layer(OwnedLayer& L) {
+  for (void* p : L.owned) cudaFree(p);
+  L.owned.clear();
+  L.w = fw::LayerWeights{};
+  L.loaded = false;
+  return FW_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fw_last_error(void) { return g_last_error.c_str(); }
+
+int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
+  if (out == nullptr) return fail(FW_EINVAL, "out is null");
+  *out = nullptr;
+  FW_TRY(check_config(config));
+  int ndev = 0;
+  FW_CUDA(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(FW_EINVAL, "device out of range");
+  FW_CUDA(cudaSetDevice(device));
+  fw_moe* h = new fw_moe();
+  h->cfg = *config;
+  h->device = device;
+  h->shape = fw::Shape{config->hidden, config->intermediate, config->shared_intermediate,
+                       config->experts, config->top_k};
+  h->layers.resize(config->layers);
+  const int M = config->max_tokens, K = config->top_k, E = config->experts;
+  const int H = config->hidden, I = config->intermediate, Is = config->shared_intermediate;
+  auto& o = h->scratch_owned;
+  int rc = FW_OK;
+  do {
+    std::vector<uint16_t> silu, sig;
+    build_tables(silu, sig);
+    if ((rc = alloc(h, &h->silu, 65536, o)) != FW_OK) break;
+    if ((rc = alloc(h, &h->sigmoid, 65536, o)) != FW_OK) break;
+    if (cudaMemcpy(h->silu, silu.data(), 65536 * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(h->sigmoid, sig.data(), 65536 * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+      rc = fail(FW_ECUDA, "table upload failed");
+      break;
+    }
+    h->luts = fw::Luts{h->silu, h->sigmoid};
+    fw::Scratch& s = h->sc;
+    s.max_T = M;
+    if ((rc = alloc(h, &s.logits, static_cast<size_t>(M) * E, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.sh_logit, M, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.sh_sig, M, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.sorted_slot, static_cast<size_t>(M) * K, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.sched, fw::sched_words(E, M, K), o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.act, static_cast<size_t>(M) * K * I, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.act_sh, static_cast<size_t>(M) * Is, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.weighted, static_cast<size_t>(M) * K * H, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.gated_sh, static_cast<size_t>(M) * H, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.err, 1, o)) != FW_OK) break;
+    if ((rc = alloc(h, &h->x_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
+    if ((rc = alloc(h, &h->y_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
+    if ((rc = alloc(h, &h->idx_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
+    if ((rc = alloc(h, &h->score_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
+    if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess) {
+      rc = fail(FW_ECUDA, "status reset failed");
+      break;
+    }
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      rc = fail(FW_ECUDA, "stream creation failed");
+      break;
+    }
+  } while (false);
+  if (rc != FW_OK) {
+    fw_moe_destroy(h);
+    return rc;
+  }
+  *out = h;
+  return FW_OK;
+}
+
+int fw_moe_destroy(fw_moe* h) {
+  if (h == nullptr) return FW_OK;
+  cudaSetDevice(h->device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  for (auto& L : h->layers) free_layer(L);
+  for (void* p : h->scratch_owned) cudaFree(p);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  for (auto& ev : h->stage_ev)
+    if (ev) cudaEventDestroy(ev);
+  delete h;
+  return FW_OK;
+}
+
+int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const uint16_t* gate_up,
+                      const uint16_t* down, const uint16_t* shared_gate, const uint16_t* shared_up,
+                      const uint16_t* shared_down, const uint16_t* shared_gate_w,
+                      const float* logit_bias) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  if (layer < 0 || layer >= h->cfg.layers) return fail(FW_EINVAL, "layer out of range");
+  if (!router || !gate_up || !down || !shared_gate || !shared_up || !shared_down || !shared_gate_w)
+    return fail(FW_EINVAL, "a weight pointer is null");
+  FW_CUDA(cudaSetDevice(h->device));
+  OwnedLayer& L = h->layers[layer];
+  free_layer(L);
+  const size_t H = h->cfg.hidden, I = h->cfg.intermediate, Is = h->cfg.shared_intermediate;
+  const size_t E = h->cfg.experts;
+  struct Item {
+    const void* src;
+    size_t count;
+    const uint16_t** dst;
+  } items[] = {
+      {router, E * H, &L.w.router},          {gate_up, E * 2 * I * H, &L.w.gate_up},
+      {down, E * H * I, &L.w.down},          {shared_gate, Is * H, &L.w.sh_gate},
+      {shared_up, Is * H, &L.w.sh_up},       {shared_down, H * Is, &L.w.sh_down},
+      {shared_gate_w, H, &L.w.sh_gate_w},
+  };
+  for (auto& it : items) {
+    uint16_t* d = nullptr;
+    const int rc = alloc(h, &d, it.count, L.owned);
+    if (rc != FW_OK) {
+      free_layer(L);
+      return rc;
+    }
+    const cudaError_t e = cudaMemcpy(d, it.src, it.count * 2, cudaMemcpyDefault);
+    if (e != cudaSuccess) {
+      free_layer(L);
+      return fail(FW_ECUDA, std::string("weight copy: ") + cudaGetErrorString(e));
+    }
+    *it.dst = d;
+  }
+  if (logit_bias != nullptr) {
+    float* d = nullptr;
+    const int rc = alloc(h, &d, E, L.owned);
+    if (rc != FW_OK) {
+      free_layer(L);
+      return rc;
+    }
+    if (cudaMemcpy(d, logit_bias, E * 4, cudaMemcpyDefault) != cudaSuccess) {
+      free_layer(L);
+      return fail(FW_ECUDA, "bias copy failed");
+    }
+    L.w.bias = d;
+  }
+  L.w.expert_base = 0;
+  L.w.expert_count = static_cast<int>(E);
+  L.loaded = true;
+  return FW_OK;
+}
+
+int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, int32_t zipf_bias) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  if (layer < 0 || layer >= h->cfg.layers) return fail(FW_EINVAL, "layer out of range");
+  if (!(std_dev > 0.0f)) return fail(FW_EINVAL, "std must be positive");
+  FW_CUDA(cudaSetDevice(h->device));
+  OwnedLayer& L = h->layers[layer];
+  free_layer(L);
+  const size_t H = h->cfg.hidden, I = h->cfg.intermediate, Is = h->cfg.shared_intermediate;
+  const size_t E = h->cfg.experts;
+  const float scale = synth_scale(std_dev);
+  struct Item {
+    uint32_t id;
+    size_t count;
+    const uint16_t** dst;
+  } items[] = {
+      {0, E * H, &L.w.router},  {1, E * 2 * I * H, &L.w.gate_up}, {2, E * H * I, &L.w.down},
+      {3, Is * H, &L.w.sh_gate}, {4, Is * H, &L.w.sh_up},          {5, H * Is, &L.w.sh_down},
+      {6, H, &L.w.sh_gate_w},
+  };
+  for (auto& it : items) {
+    uint16_t* d = nullptr;
+    const int rc = alloc(h, &d, it.count, L.owned);
+    if (rc != FW_OK) {
+      free_layer(L);
+      return rc;
+    }
+    const cudaError_t e = fw::launch_synth(synth_key(seed, it.id), it.id, 0, it.count, scale, d, h->stream);
+    if (e != cudaSuccess) {
+      free_layer(L);
+      return fail(FW_ECUDA, std::string("synth launch: ") + cudaGetErrorString(e));
+    }
+    *it.dst = d;
+  }
+  if (zipf_bias) {
+    std::vector<float> bias(E);
+    for (size_t e = 0; e < E; ++e)
+      bias[e] = static_cast<float>(0.5 * std::log(std::pow(static_cast<double>(e + 1), -1.1)));
+    float* d = nullptr;
+    const int rc = alloc(h, &d, E, L.owned);
+    if (rc != FW_OK) {
+      free_layer(L);
+      return rc;
+    }
+    if (cudaMemcpy(d, bias.data(), E * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+      free_layer(L);
+      return fail(FW_ECUDA, "bias copy failed");
+    }
+    L.w.bias = d;
+  }
+  const cudaError_t e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    return fail(FW_ECUDA, std::string("synth: ") + cudaGetErrorString(e));
+  }
+  L.w.expert_base = 0;
+  L.w.expert_count = static_cast<int>(E);
+  L.loaded = true;
+  return FW_OK;
+}
+
+int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t tokens, uint16_t* y,
+                         int32_t* topk_idx, uint16_t* topk_scores, void* stream) {
+  FW_TRY(check_handle(h, layer));
+  if (tokens < 0 || tokens > h->cfg.max_tokens) return fail(FW_EINVAL, "tokens out of range");
+  if (tokens == 0) return FW_OK;
+  if (x == nullptr || y == nullptr) return fail(FW_EINVAL, "x / y is null");
+  if (!aligned16(x) || !aligned16(y)) return fail(FW_EINVAL, "x / y must be 16-byte aligned");
+  if (!aligned4(topk_idx) || !aligned4(topk_scores))
+    return fail(FW_EINVAL, "topk buffers must be 4-byte aligned");
+  FW_CUDA(cudaSetDevice(h->device));
+  const cudaError_t e = fw::launch_block(h->shape, h->layers[layer].w, h->luts, h->sc, x, tokens, y,
+                                         topk_idx ? topk_idx : h->idx_dev,
+                                         topk_scores ? topk_scores : h->score_dev,
+                                         static_cast<cudaStream_t>(stream),
+                                         h->profile ? h->stage_ev : nullptr);
+  if (e != cudaSuccess) return fail(FW_ECUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return FW_OK;
+}
+
+int fw_moe_sync(fw_moe* h, void* stream) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  FW_CUDA(cudaSetDevice(h->device));
+  FW_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int code = 0;
+  FW_CUDA(cudaMemcpy(&code, h->sc.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    FW_CUDA(cudaMemset(h->sc.err, 0, sizeof(int)));
+    return map_device_error(code);
+  }
+  return FW_OK;
+}
+
+int fw_moe_forward(fw_moe* h, int32_t layer, const uint16_t* x, int32_t tokens, uint16_t* y,
+                   int32_t* topk_idx, uint16_t* topk_scores) {
+  FW_TRY(check_handle(h, layer));
+  if (tokens < 0 || tokens > h->cfg.max_tokens) return fail(FW_EINVAL, "tokens out of range");
+  if (tokens == 0) return FW_OK;
+  if (x == nullptr || y == nullptr) return fail(FW_EINVAL, "x / y is null");
+  FW_CUDA(cudaSetDevice(h->device));
+  const size_t H = h->cfg.hidden, K = h->cfg.top_k;
+  FW_CUDA(cudaMemcpyAsync(h->x_dev, x, tokens * H * 2, cudaMemcpyDefault, h->stream));
+  FW_TRY(fw_moe_forward_async(h, layer, h->x_dev, tokens, h->y_dev, h->idx_dev, h->score_dev,
+                              h->stream));
+  FW_CUDA(cudaMemcpyAsync(y, h->y_dev, tokens * H * 2, cudaMemcpyDefault, h->stream));
+  if (topk_idx)
+    FW_CUDA(cudaMemcpyAsync(topk_idx, h->idx_dev, tokens * K * 4, cudaMemcpyDefault, h->stream));
+  if (topk_scores)
+    FW_CUDA(cudaMemcpyAsync(topk_scores, h->score_dev, tokens * K * 2, cudaMemcpyDefault, h->stream));
+  return fw_moe_sync(h, h->stream);
+}
+
+int fw_moe_profile(fw_moe* h, int32_t enable) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  FW_CUDA(cudaSetDevice(h->device));
+  if (enable) {
+    for (auto& ev : h->stage_ev)
+      if (!ev) FW_CUDA(cudaEventCreate(&ev));
+  }
+  h->profile = enable != 0;
+  return FW_OK;
+}
+
+int fw_moe_profile_read(fw_moe* h, float* stage_ms, int32_t n) {
+  if (h == nullptr || stage_ms == nullptr || n < fw::kStages) return fail(FW_EINVAL, "bad argument");
+  if (!h->profile) return fail(FW_EINVAL, "profiling is off");
+  FW_CUDA(cudaSetDevice(h->device));
+  FW_CUDA(cudaEventSynchronize(h->stage_ev[fw::kStages]));
+  for (int i = 0; i < fw::kStages; ++i)
+    FW_CUDA(cudaEventElapsedTime(&stage_ms[i], h->stage_ev[i], h->stage_ev[i + 1]));
+  return FW_OK;
+}
+
+int fw_moe_memory(const fw_moe* h, uint64_t* bytes) {
+  if (h == nullptr || bytes == nullptr) return fail(FW_EINVAL, "null argument");
+  *bytes = h->bytes;
+  return FW_OK;
+}
+
+int fw_linear_bf16(const uint16_t* w, const uint16_t* x, int32_t rows, int32_t cols, int32_t tokens,
+                   uint16_t* y, void* stream) {
+  if (!w || !x || !y) return fail(FW_EINVAL, "null argument");
+  if (rows <= 0 || tokens <= 0 || cols <= 0 || cols % 32 != 0 || 8ull * cols * 4 > 200 * 1024)
+    return fail(FW_EINVAL, "rows/tokens must be positive; cols a multiple of 32, at most 6400");
+  if (!aligned16(w) || !aligned16(x)) return fail(FW_EINVAL, "w / x must be 16-byte aligned");
+  const cudaError_t e = fw::launch_linear(w, x, rows, cols, tokens, y, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FW_ECUDA, std::string("linear: ") + cudaGetErrorString(e));
+  return FW_OK;
+}
+
+int fw_swiglu_bf16(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out, void* stream) {
+  if (!gate || !up || !out || n < 0) return fail(FW_EINVAL, "bad argument");
+  if (n == 0) return FW_OK;
+  int dev = 0;
+  FW_CUDA(cudaGetDevice(&dev));
+  DeviceCommon* c = nullptr;
+  FW_TRY(device_common(dev, &c));
+  const cudaError_t e = fw::launch_swiglu(gate, up, n, c->silu, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FW_ECUDA, std::string("swiglu: ") + cudaGetErrorString(e));
+  return FW_OK;
+}
+
+int fw_route_bf16(const uint16_t* logits, int32_t tokens, int32_t experts, int32_t top_k,
+                  int32_t* indices, uint16_t* scores, void* stream) {
+  if (!logits || !indices || !scores) return fail(FW_EINVAL, "null argument");
+  if (tokens < 0 || experts <= 0 || experts % 32 != 0 || experts > 1024 || top_k < 1 ||
+      top_k > 32 || top_k > experts)
+    return fail(FW_EINVAL, "bad route shape");
+  if (tokens == 0) return FW_OK;
+  int dev = 0;
+  FW_CUDA(cudaGetDevice(&dev));
+  DeviceCommon* c = nullptr;
+  FW_TRY(device_common(dev, &c));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = fw::launch_route(logits, tokens, experts, top_k, indices, scores, c->err, st);
+  if (e != cudaSuccess) return fail(FW_ECUDA, std::string("route: ") + cudaGetErrorString(e));
+  FW_CUDA(cudaStreamSynchronize(st));
+  int code = 0;
+  FW_CUDA(cudaMemcpy(&code, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    FW_CUDA(cudaMemset(c->err, 0, sizeof(int)));
+    return map_device_error(code);
+  }
+  return FW_OK;
+}
+
+bool firewing_cuda_topk_bf16(const uint16_t* values, size_t count, size_t k, size_t* indices) {
+  if (values == nullptr || indices == nullptr || k == 0 || k > count || count % 32 != 0 ||
+      count > 1024 || k > 32)
+    return false;
+  uint16_t* dv = nullptr;
+  int32_t* di = nullptr;
+  uint16_t* ds = nullptr;
+  bool ok = cudaMalloc(&dv, count * 2) == cudaSuccess && cudaMalloc(&di, k * 4) == cudaSuccess &&
+            cudaMalloc(&ds, k * 2) == cudaSuccess &&
+            cudaMemcpy(dv, values, count * 2, cudaMemcpyHostToDevice) == cudaSuccess;
+  std::vector<int32_t> idx(k);
+  if (ok) {
+    ok = fw_route_bf16(dv, 1, static_cast<int32_t>(count), static_cast<int32_t>(k), di, ds, nullptr) ==
+             FW_OK &&
+         cudaMemcpy(idx.data(), di, k * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+  }
+  cudaFree(dv);
+  cudaFree(di);
+  cudaFree(ds);
+  if (!ok) return false;
+  for (size_t i = 0; i < k; ++i) indices[i] = static_cast<size_t>(idx[i]);
+  return true;
+}
+
+}  // extern "C"

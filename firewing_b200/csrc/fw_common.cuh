@@ -1,0 +1,82 @@
+// fw_common.cuh -- device helpers shared by the sparse-MoE kernels (sm_100a).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "fw_kernels.h"
+
+namespace fw {
+
+__device__ __forceinline__ void set_error(int* err, int code) {
+  if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+// bf16 <-> f32 with the reference's arithmetic (src/expert.rs:315-322):
+// round-to-nearest-even by an integer add, no NaN/Inf guard.
+__device__ __forceinline__ float bf16_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+__device__ __forceinline__ uint16_t f32_to_bf16(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+}
+// Two packed bf16 values (little-endian: element 0 in the low half).
+__device__ __forceinline__ float lo_bf16(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// f32 total order (Rust f32::total_cmp) on bf16 bits: larger key = larger
+// value, -0 < +0.  Used with ascending-index tie-break (src/router.rs:241-247).
+__device__ __forceinline__ uint32_t total_key(uint32_t bits16) {
+  return (bits16 & 0x8000u) ? (~bits16 & 0xffffu) : (bits16 | 0x8000u);
+}
+
+// Streaming 16-byte weight load: read-only path, no L1 allocation.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Programmatic dependent launch (PDL): wait for the preceding grid's
+// results / let the next grid start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// One 32-column block of the reference dot schedule for a lane that owns
+// partials 8q..8q+7 (q = lane & 3): acc[i] += w[i] * x[i] for the 8
+// consecutive columns it loaded.  A bf16 x bf16 product is exact in f32
+// (16 significant bits), so fmaf(w, x, acc) rounds exactly like the
+// reference's rounded multiply followed by a rounded add, for every product
+// that neither underflows below 2^-126 nor overflows.
+__device__ __forceinline__ void fma8(const uint4 w, const float4 xa, const float4 xb, float* acc) {
+  acc[0] = fmaf(lo_bf16(w.x), xa.x, acc[0]);
+  acc[1] = fmaf(hi_bf16(w.x), xa.y, acc[1]);
+  acc[2] = fmaf(lo_bf16(w.y), xa.z, acc[2]);
+  acc[3] = fmaf(hi_bf16(w.y), xa.w, acc[3]);
+  acc[4] = fmaf(lo_bf16(w.z), xb.x, acc[4]);
+  acc[5] = fmaf(hi_bf16(w.z), xb.y, acc[5]);
+  acc[6] = fmaf(lo_bf16(w.w), xb.z, acc[6]);
+  acc[7] = fmaf(hi_bf16(w.w), xb.w, acc[7]);
+}
+
+// Finish the reference reduction tree (src/expert.rs:530-540) for a
+// 4-lane group holding the 32 partials as 8 per lane: partial j = 8q + i.
+//   +16: j += j+16  -> lanes q<2 take lanes q+2
+//   +8 : j += j+8   -> lane q=0 takes lane q=1
+//   +4 : j += j+4   -> within lane 0: i += i+4
+//   (0+1)+(2+3)
+// Every lane of the group must call it; the result is valid in lane q = 0.
+__device__ __forceinline__ float reduce_partials(float* p) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] += __shfl_down_sync(0xffffffffu, p[i], 2, 4);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] += __shfl_down_sync(0xffffffffu, p[i], 1, 4);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] += p[i + 4];
+  return (p[0] + p[1]) + (p[2] + p[3]);
+}
+
+}  // namespace fw

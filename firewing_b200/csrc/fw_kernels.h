@@ -1,0 +1,101 @@
+// fw_kernels.h -- host-side launch interface of the sparse-MoE kernels.
+// Internal to libfwmoe; the public C ABI is include/fwmoe.h.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fw {
+
+// Device-side status codes written to the per-handle error word (first
+// writer wins).  The host maps them to FW_E* return codes.
+enum DeviceError : int {
+  kErrNone = 0,
+  kErrNanLogits = 1,   // a router logit was NaN (src/decoder_layer.rs:279)
+  kErrTimeout = 2,     // a bounded wait on an mbarrier / flag gave up
+  kErrBadIndex = 3,    // an expert id outside [0, E) reached a kernel
+  kErrCapacity = 4,    // more (token, expert) pairs than the scratch holds
+};
+
+
+// Block shape.  All counts in elements.
+struct Shape {
+  int H;   // hidden
+  int I;   // routed expert intermediate
+  int Is;  // shared expert intermediate
+  int E;   // routed experts
+  int K;   // top-k
+};
+
+// One layer's device weights, reference layout (src/expert.rs:362-512):
+//   router [E][H], gate_up [E][2I][H] (gate rows then up rows),
+//   down [E][H][I], shared gate/up [Is][H], shared down [H][Is],
+//   shared gate vector [H], optional f32 logit bias [E].
+struct LayerWeights {
+  const uint16_t* router = nullptr;
+  const uint16_t* gate_up = nullptr;
+  const uint16_t* down = nullptr;
+  const uint16_t* sh_gate = nullptr;
+  const uint16_t* sh_up = nullptr;
+  const uint16_t* sh_down = nullptr;
+  const uint16_t* sh_gate_w = nullptr;
+  const float* bias = nullptr;
+  int expert_base = 0;   // first expert id held (expert parallelism)
+  int expert_count = 0;  // experts held
+};
+
+// Scratch for one forward of up to max_T tokens (device memory).
+struct Scratch {
+  uint16_t* logits = nullptr;    // [T][E]
+  uint16_t* sh_logit = nullptr;  // [T]
+  uint16_t* sh_sig = nullptr;    // [T]
+  int32_t* sorted_slot = nullptr;  // [T][K] slots in ascending expert order
+  int32_t* sched = nullptr;      // schedule words, see sched_* helpers
+  uint16_t* act = nullptr;       // [T*K][I]
+  uint16_t* act_sh = nullptr;    // [T][Is]
+  uint16_t* weighted = nullptr;  // [T*K][H]
+  uint16_t* gated_sh = nullptr;  // [T][H]
+  int* err = nullptr;            // device status word
+  int max_T = 0;
+};
+
+// Schedule layout inside Scratch::sched (int32 words):
+//   [0]                  n_active
+//   [1 .. 1+E)           active expert ids, ascending
+//   [1+E .. 2+2E)        pair offsets per active slot (n_active+1 used)
+//   [2+2E .. 2+2E+T*K)   pair ids grouped by expert, tokens ascending
+inline size_t sched_words(int E, int max_T, int K) {
+  return 2 + 2 * static_cast<size_t>(E) + static_cast<size_t>(max_T) * K;
+}
+
+// Lookup tables built on the host (bf16(silu(g)) and bf16(sigmoid(g)) for
+// every bf16 bit pattern, src/metal_moe.rs:385-392).
+struct Luts {
+  const uint16_t* silu = nullptr;
+  const uint16_t* sigmoid = nullptr;
+};
+
+// Pipeline stages of one block forward (for per-stage timing).
+enum Stage : int { kStageRouter = 0, kStageRoute, kStageUp, kStageDown, kStageCombine, kStages };
+
+// Whole decode-path block for T tokens, stream-ordered.  When stage_events is
+// non-null, kStages + 1 events are recorded around the stages.
+cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts,
+                         const Scratch& sc, const uint16_t* x, int T, uint16_t* y,
+                         int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
+                         cudaEvent_t* stage_events = nullptr);
+
+// Primitives (the reference crate's functions over device buffers).
+cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int cols, int T,
+                          uint16_t* y, cudaStream_t st);
+cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
+                         uint16_t* score, int* err, cudaStream_t st);
+cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, long long n,
+                          const uint16_t* silu_lut, uint16_t* out, cudaStream_t st);
+
+// Seeded synthetic bf16 tensor (identical bits to the CPU generator);
+// key = SplitMix64 stream key of (seed, tensor id).
+cudaError_t launch_synth(uint64_t key, uint32_t tensor, uint64_t start, uint64_t count,
+                         float scale, uint16_t* out, cudaStream_t st);
+
+}  // namespace fw

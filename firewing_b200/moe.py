@@ -1,0 +1,240 @@
+"""ctypes binding of libfwmoe (include/fwmoe.h).
+
+Mirrors the reference crate's API for the sparse-MoE block:
+
+* ``MoeBlock`` -- the resident runner (``ExactResidentTop10Runner``,
+  src/metal_moe.rs:399-447): install weights once, then run the whole block
+  (router -> top-k -> routed SwiGLU experts -> ascending-id bf16 combine ->
+  sigmoid-gated shared expert) per call;
+* ``linear_bf16`` / ``swiglu_bf16`` / ``route_bf16`` / ``topk_bf16`` -- the
+  crate's primitives (src/expert.rs:554-571, src/decoder_layer.rs:278-307,
+  native/topk_shim.cpp:18-44) over device buffers.
+
+Errors follow the reference's fail-closed ``Result<_, String>``: every
+non-zero status raises ``FwError`` carrying the library's message.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+FW_OK = 0
+FW_EINVAL = -1
+FW_ECUDA = -2
+FW_ENCCL = -3
+FW_ETIMEOUT = -4
+FW_ENOMEM = -5
+FW_ENAN = -6
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def library_path() -> str:
+    return os.path.join(_HERE, "libfwmoe.so")
+
+
+class FwError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"fwmoe error {code}: {message}")
+        self.code = code
+        self.message = message
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int32),
+        ("intermediate", ctypes.c_int32),
+        ("shared_intermediate", ctypes.c_int32),
+        ("experts", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("max_tokens", ctypes.c_int32),
+        ("layers", ctypes.c_int32),
+    ]
+
+
+_lib = None
+vp = ctypes.c_void_p
+
+
+def library() -> ctypes.CDLL:
+    """Load libfwmoe.so (built in-tree by firewing_b200/build.py)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"{path} is missing: build it with `python firewing_b200/build.py` "
+            "(there is no CPU fallback)")
+    L = ctypes.CDLL(path)
+    L.fw_last_error.restype = ctypes.c_char_p
+    L.fw_last_error.argtypes = []
+    L.fw_moe_create.argtypes = [ctypes.POINTER(_Config), ctypes.c_int, ctypes.POINTER(vp)]
+    L.fw_moe_destroy.argtypes = [vp]
+    L.fw_moe_load_layer.argtypes = [vp, ctypes.c_int32] + [vp] * 7 + [vp]
+    L.fw_moe_synth_layer.argtypes = [vp, ctypes.c_int32, ctypes.c_uint64, ctypes.c_float,
+                                     ctypes.c_int32]
+    L.fw_moe_forward.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp]
+    L.fw_moe_forward_async.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp, vp]
+    L.fw_moe_sync.argtypes = [vp, vp]
+    L.fw_moe_memory.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
+    L.fw_moe_profile.argtypes = [vp, ctypes.c_int32]
+    L.fw_moe_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
+    L.fw_linear_bf16.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp]
+    L.fw_swiglu_bf16.argtypes = [vp, vp, ctypes.c_int64, vp, vp]
+    L.fw_route_bf16.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp, vp]
+    L.firewing_cuda_topk_bf16.restype = ctypes.c_bool
+    L.firewing_cuda_topk_bf16.argtypes = [vp, ctypes.c_size_t, ctypes.c_size_t,
+                                          ctypes.POINTER(ctypes.c_size_t)]
+    for name in ("fw_moe_create", "fw_moe_destroy", "fw_moe_load_layer", "fw_moe_synth_layer",
+                 "fw_moe_forward", "fw_moe_forward_async", "fw_moe_sync", "fw_moe_memory",
+                 "fw_moe_profile", "fw_moe_profile_read",
+                 "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16"):
+        getattr(L, name).restype = ctypes.c_int
+    _lib = L
+    return L
+
+
+def _check(rc: int) -> None:
+    if rc != FW_OK:
+        raise FwError(rc, library().fw_last_error().decode("utf-8", "replace"))
+
+
+def _ptr(a) -> Optional[int]:
+    """Address of a numpy array (host) or a torch tensor (host or device)."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        assert a.flags.c_contiguous, "arrays must be C-contiguous"
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        assert a.is_contiguous(), "tensors must be contiguous"
+        return a.data_ptr()
+    raise TypeError(f"unsupported buffer type {type(a)}")
+
+
+def _stream(s) -> Optional[int]:
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return getattr(s, "cuda_stream", None) or None
+
+
+@dataclass
+class MoeConfig:
+    hidden: int = 2048
+    intermediate: int = 512
+    shared_intermediate: int = 512
+    experts: int = 512
+    top_k: int = 10
+    max_tokens: int = 64
+    layers: int = 1
+
+    def c(self) -> _Config:
+        return _Config(self.hidden, self.intermediate, self.shared_intermediate, self.experts,
+                       self.top_k, self.max_tokens, self.layers)
+
+
+class MoeBlock:
+    """Resident sparse-MoE block runner on one device."""
+
+    def __init__(self, config: MoeConfig, device: int = 0):
+        self.config = config
+        self.device = device
+        h = vp()
+        _check(library().fw_moe_create(ctypes.byref(config.c()), device, ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            library().fw_moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def handle(self) -> int:
+        return self._h.value
+
+    def load_layer(self, layer: int, router, gate_up, down, shared_gate, shared_up, shared_down,
+                   shared_gate_w, logit_bias=None) -> None:
+        _check(library().fw_moe_load_layer(
+            self._h, layer, _ptr(router), _ptr(gate_up), _ptr(down), _ptr(shared_gate),
+            _ptr(shared_up), _ptr(shared_down), _ptr(shared_gate_w), _ptr(logit_bias)))
+
+    def synth_layer(self, layer: int, seed: int, std: float = 0.02, zipf: bool = False) -> None:
+        _check(library().fw_moe_synth_layer(self._h, layer, seed, std, 1 if zipf else 0))
+
+    def forward(self, layer: int, x: np.ndarray):
+        """Host buffers in and out (synchronous): returns (y, topk_idx, scores)."""
+        cfg = self.config
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        T = x.shape[0]
+        y = np.empty((T, cfg.hidden), dtype=np.uint16)
+        idx = np.empty((T, cfg.top_k), dtype=np.int32)
+        sc = np.empty((T, cfg.top_k), dtype=np.uint16)
+        _check(library().fw_moe_forward(self._h, layer, _ptr(x), T, _ptr(y), _ptr(idx), _ptr(sc)))
+        return y, idx, sc
+
+    def forward_async(self, layer: int, x, tokens: int, y, topk_idx=None, topk_scores=None,
+                      stream=None) -> None:
+        """Device buffers (torch tensors or raw addresses), stream-ordered."""
+        _check(library().fw_moe_forward_async(self._h, layer, _ptr(x), tokens, _ptr(y),
+                                              _ptr(topk_idx), _ptr(topk_scores), _stream(stream)))
+
+    def sync(self, stream=None) -> None:
+        _check(library().fw_moe_sync(self._h, _stream(stream)))
+
+    STAGES = ("router", "route", "expert_up", "expert_down", "combine")
+
+    def profile(self, enable: bool) -> None:
+        _check(library().fw_moe_profile(self._h, 1 if enable else 0))
+
+    def profile_read(self) -> dict:
+        """Stage durations (ms) of the last forward while profiling is on."""
+        buf = (ctypes.c_float * 5)()
+        _check(library().fw_moe_profile_read(self._h, buf, 5))
+        return dict(zip(self.STAGES, [float(v) for v in buf]))
+
+    def memory_bytes(self) -> int:
+        v = ctypes.c_uint64()
+        _check(library().fw_moe_memory(self._h, ctypes.byref(v)))
+        return int(v.value)
+
+
+def linear_bf16(w, x, rows: int, cols: int, tokens: int, y, stream=None) -> None:
+    _check(library().fw_linear_bf16(_ptr(w), _ptr(x), rows, cols, tokens, _ptr(y), _stream(stream)))
+
+
+def swiglu_bf16(gate, up, n: int, out, stream=None) -> None:
+    _check(library().fw_swiglu_bf16(_ptr(gate), _ptr(up), n, _ptr(out), _stream(stream)))
+
+
+def route_bf16(logits, tokens: int, experts: int, top_k: int, indices, scores, stream=None) -> None:
+    _check(library().fw_route_bf16(_ptr(logits), tokens, experts, top_k, _ptr(indices),
+                                   _ptr(scores), _stream(stream)))
+
+
+def topk_bf16(values: np.ndarray, k: int):
+    """Drop-in of firewing_torch_topk_bf16 (host buffers); None on failure."""
+    values = np.ascontiguousarray(values, dtype=np.uint16)
+    out = (ctypes.c_size_t * k)()
+    ok = library().firewing_cuda_topk_bf16(_ptr(values), values.size, k, out)
+    return list(out) if ok else None

@@ -1,0 +1,160 @@
+/*
+ * fwmoe.h -- C ABI of the B200 (sm_100a) sparse-MoE block library.
+ *
+ * Drop-in GPU backend for the sparse-MoE block of x3haloed/firewing (Rust
+ * crate).  Plain C types only: pointers, sizes, status codes.  Every entry
+ * point cites the reference interface it replaces (paths relative to the
+ * firewing source tree).
+ *
+ * Conventions (mirroring the reference's fail-closed `Result<_, String>`):
+ *   - every function returns an int status: FW_OK (0) or a negative FW_E*;
+ *     fw_last_error() returns a thread-local message for the last failure;
+ *   - tensors are bf16 bit patterns (uint16_t), row-major, little-endian, in
+ *     the reference's layout (src/expert.rs:362-512);
+ *   - a handle is not thread-safe and owns one device; calls made with it
+ *     switch the calling thread's current CUDA device to that device;
+ *   - `stream` arguments are cudaStream_t values passed as void*
+ *     (NULL = the legacy default stream).
+ *
+ * Numerics: every GEMV keeps the reference's f32 reduction order
+ * (src/expert.rs:514-552) and every bf16 rounding point, so outputs are
+ * bit-identical to the reference CPU path except for the router softmax,
+ * whose exp is correctly rounded where the host libm's expf may be one ulp
+ * off; a renormalised score can then differ by one bf16 ulp.  Products must
+ * stay inside the normal f32 range (|w*x| >= 2^-126 or zero) for the
+ * bit-exact claim; outside it results stay within one f32 rounding.
+ */
+#ifndef FWMOE_H
+#define FWMOE_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FW_OK 0
+#define FW_EINVAL (-1)   /* bad argument, shape or state */
+#define FW_ECUDA (-2)    /* a CUDA call failed */
+#define FW_ENCCL (-3)    /* a collective failed (expert parallelism) */
+#define FW_ETIMEOUT (-4) /* a bounded device wait gave up */
+#define FW_ENOMEM (-5)   /* device allocation failed */
+#define FW_ENAN (-6)     /* router logits contained NaN (src/decoder_layer.rs:279) */
+
+typedef struct fw_moe fw_moe;
+
+/* Block configuration.  The reference hard-codes these
+ * (src/decoder_layer.rs:14-17, 40-42; src/metal_moe.rs:15-21).
+ * Constraints: hidden % 64 == 0 and <= 8192; intermediate and
+ * shared_intermediate % 64 == 0; experts % 32 == 0 and <= 1024;
+ * 1 <= top_k <= min(32, experts); 1 <= max_tokens <= 256. */
+typedef struct fw_moe_config {
+    int32_t hidden;              /* H */
+    int32_t intermediate;        /* I of a routed expert */
+    int32_t shared_intermediate; /* Is of the shared expert */
+    int32_t experts;             /* E routed experts */
+    int32_t top_k;               /* K */
+    int32_t max_tokens;          /* largest T passed to a forward */
+    int32_t layers;              /* resident layers (each loaded separately) */
+} fw_moe_config;
+
+/* Thread-local description of the last failure ("" if none). */
+const char* fw_last_error(void);
+
+/* Create a block runner on `device`: allocates scratch and builds the bf16
+ * SiLU / sigmoid tables on the host, as ExactResidentTop10Runner::install
+ * does (src/metal_moe.rs:95-223, 385-392, 399-421). */
+int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out);
+int fw_moe_destroy(fw_moe* handle);
+
+/* Copy one layer's weights (host or device pointers) into memory the handle
+ * owns.  Layouts: router [E][H] (model.layers.N.mlp.gate.weight);
+ * gate_up [E][2I][H] (experts.gate_up_proj, gate rows first); down [E][H][I]
+ * (experts.down_proj); shared_gate, shared_up [Is][H]; shared_down [H][Is];
+ * shared_gate_w [1][H] (shared_expert_gate.weight); logit_bias [E] f32 or
+ * NULL.  Replaces the reference's per-call weight reads
+ * (src/expert.rs:362-512) and buffer install (src/metal_moe.rs:162-207). */
+int fw_moe_load_layer(fw_moe* handle, int32_t layer, const uint16_t* router,
+                      const uint16_t* gate_up, const uint16_t* down,
+                      const uint16_t* shared_gate, const uint16_t* shared_up,
+                      const uint16_t* shared_down, const uint16_t* shared_gate_w,
+                      const float* logit_bias);
+
+/* Fill one layer with seeded synthetic weights generated on the device
+ * (no reference counterpart: the benchmark configurations use synthetic
+ * weights).  Element i of tensor id (router 0, gate_up 1, down 2,
+ * shared_gate 3, shared_up 4, shared_down 5, shared_gate_w 6) is output i of
+ * a SplitMix64 stream keyed by (seed, id), as an Irwin-Hall(4) sum of 16-bit
+ * uniforms scaled to standard deviation `std`, rounded to bf16.  zipf_bias
+ * != 0 installs logit_bias[e] = 0.5*ln((e+1)^-1.1). */
+int fw_moe_synth_layer(fw_moe* handle, int32_t layer, uint64_t seed, float std,
+                       int32_t zipf_bias);
+
+/* Whole sparse-MoE block for `tokens` tokens, synchronous, HOST buffers:
+ * x [T][H] -> y [T][H] = routed top-k mixture + sigmoid-gated shared expert;
+ * topk_idx [T][K] / topk_scores [T][K] (may be NULL) receive the selection in
+ * top-k order and the renormalised bf16 scores.  Replaces the in-layer block
+ * body (src/decoder_layer.rs:460-586) and ExactResidentTop10Runner::
+ * execute_exact (src/metal_moe.rs:423-441).  Returns FW_ENAN when a token's
+ * router logits contain NaN, like route() (src/decoder_layer.rs:278-281). */
+int fw_moe_forward(fw_moe* handle, int32_t layer, const uint16_t* x, int32_t tokens,
+                   uint16_t* y, int32_t* topk_idx, uint16_t* topk_scores);
+
+/* Same, DEVICE buffers, stream-ordered and asynchronous.  topk_idx /
+ * topk_scores may be NULL.  Device-side failures (NaN logits) are reported by
+ * the next fw_moe_sync on the handle. */
+int fw_moe_forward_async(fw_moe* handle, int32_t layer, const uint16_t* x, int32_t tokens,
+                         uint16_t* y, int32_t* topk_idx, uint16_t* topk_scores,
+                         void* stream);
+
+/* Wait for `stream`, then report and clear device-side status. */
+int fw_moe_sync(fw_moe* handle, void* stream);
+
+/* Per-stage timing, for roofline measurement (the reference times its phases
+ * with host intervals, src/metal_moe.rs:473-477, 590-606).  While enabled,
+ * every forward records CUDA events around its five kernels (router logits,
+ * route + permute, expert gate_up + SwiGLU, expert down + scale, combine),
+ * which serialises them; fw_moe_profile_read waits for the last forward and
+ * returns the five durations in milliseconds (n >= 5). */
+int fw_moe_profile(fw_moe* handle, int32_t enable);
+int fw_moe_profile_read(fw_moe* handle, float* stage_ms, int32_t n);
+
+/* Device bytes the handle holds (weights + scratch). */
+int fw_moe_memory(const fw_moe* handle, uint64_t* bytes);
+
+/* ---- primitives over DEVICE buffers (the reference crate's functions) ---- */
+
+/* y[t][r] = bf16(dot(w[r], x[t])) with the reference reduction order:
+ * linear_bf16 (src/expert.rs:554-560) for `tokens` input vectors.
+ * cols % 32 == 0. */
+int fw_linear_bf16(const uint16_t* w, const uint16_t* x, int32_t rows, int32_t cols,
+                   int32_t tokens, uint16_t* y, void* stream);
+
+/* out[i] = bf16(bf16(silu(gate[i])) * up[i]): swiglu_bf16
+ * (src/expert.rs:562-571) via the host-built table of
+ * src/metal_moe.rs:385-392. */
+int fw_swiglu_bf16(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out,
+                   void* stream);
+
+/* In-layer route for `tokens` logit rows [T][experts]: top-k (logit
+ * descending, ties by ascending index, src/router.rs:241-247), f32 softmax,
+ * renormalised bf16 scores: route (src/decoder_layer.rs:278-307).
+ * experts % 32 == 0, <= 1024.  Synchronous; FW_ENAN on NaN logits. */
+int fw_route_bf16(const uint16_t* logits, int32_t tokens, int32_t experts, int32_t top_k,
+                  int32_t* indices, uint16_t* scores, void* stream);
+
+/* Drop-in for the reference's only C ABI on the path,
+ * `bool firewing_torch_topk_bf16(const uint16_t*, size_t, size_t, size_t*)`
+ * (native/topk_shim.cpp:18-44, bound at src/decoder_layer.rs:19-39): HOST
+ * buffers, runs on the current device.  false on null pointers, k == 0,
+ * k > count, count % 32 != 0 or count > 1024.  Ties are ordered by
+ * ascending index (the shim's order among equal values depends on the C++
+ * library). */
+bool firewing_cuda_topk_bf16(const uint16_t* values, size_t count, size_t k, size_t* indices);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FWMOE_H */
