@@ -273,6 +273,12 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     sampler = ClockSampler(local_rank)
     el = timed(T, bufs, args.steps, args.warmup, sampler)
     clocks = sampler.summary()
+    if args.minimal:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": world * T * L * args.steps / el,
+                              "unit": UNIT, "minimal": True, "layers": L, "tokens": T}))
+        blk.close()
+        return
     value = world * T * L * args.steps / el
     # routing statistics of the run itself (distinct experts per layer)
     idx_host = bufs[2].cpu().numpy()
@@ -421,6 +427,9 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--minimal", action="store_true",
+                    help="timed steps only (no T=4 pass, e2e, stage profile or CPU leg); "
+                         "for ncu captures")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)

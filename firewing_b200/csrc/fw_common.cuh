@@ -13,10 +13,16 @@ __device__ __forceinline__ void set_error(int* err, int code) {
 }
 
 // bf16 <-> f32 with the reference's arithmetic (src/expert.rs:315-322):
-// round-to-nearest-even by an integer add, no NaN/Inf guard.
+// round-to-nearest-even by an integer add.  One deviation, for NaN only: GPU
+// arithmetic returns the canonical NaN 0x7fffffff, which that integer add
+// would carry into -0.0, whereas the reference's CPU propagates the input
+// NaN's payload (0x7fc00000) and the add keeps it a NaN.  A NaN therefore
+// rounds to the quiet NaN 0x7fc0, so NaN inputs still reach route()'s NaN
+// rejection (src/decoder_layer.rs:279-281).
 __device__ __forceinline__ float bf16_to_f32(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 __device__ __forceinline__ uint16_t f32_to_bf16(float v) {
   const uint32_t b = __float_as_uint(v);
+  if ((b & 0x7fffffffu) > 0x7f800000u) return 0x7fc0u;
   return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
 }
 // Two packed bf16 values (little-endian: element 0 in the low half).
