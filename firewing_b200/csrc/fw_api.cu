@@ -17,19 +17,26 @@
 
 namespace {
 
-thread_local std::string g_last_error;
+// The last failure's message, per thread, in a fixed buffer (recording an
+// error never allocates).
+thread_local char g_last_error[512] = "";
 
-int fail(int code, const std::string& msg) {
-  g_last_error = msg;
+int fail(int code, const char* msg) {
+  std::snprintf(g_last_error, sizeof g_last_error, "%s", msg);
   return code;
 }
+int fail(int code, const char* what, const char* detail) {
+  std::snprintf(g_last_error, sizeof g_last_error, "%s: %s", what, detail);
+  return code;
+}
+int fail(int code, const std::string& msg) { return fail(code, msg.c_str()); }
 
 #define FW_CUDA(call)                                                                    \
   do {                                                                                   \
     const cudaError_t e_ = (call);                                                       \
     if (e_ != cudaSuccess)                                                               \
-      return fail(e_ == cudaErrorMemoryAllocation ? FW_ENOMEM : FW_ECUDA,                \
-                  std::string(#call) + ": " + cudaGetErrorString(e_));                   \
+      return fail(e_ == cudaErrorMemoryAllocation ? FW_ENOMEM : FW_ECUDA, #call,         \
+                  cudaGetErrorString(e_));                                               \
   } while (0)
 
 // bf16 helpers with the reference arithmetic (src/expert.rs:315-322).
@@ -200,7 +207,7 @@ int free_layer(OwnedLayer& L) {
 
 extern "C" {
 
-const char* fw_last_error(void) { return g_last_error.c_str(); }
+const char* fw_last_error(void) { return g_last_error; }
 
 int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
   if (out == nullptr) return fail(FW_EINVAL, "out is null");
