@@ -13,6 +13,7 @@ from .moe import (  # noqa: F401
     FwError,
     MoeBlock,
     MoeConfig,
+    forward_noalloc,
     library,
     library_path,
     linear_bf16,

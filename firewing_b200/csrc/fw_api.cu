@@ -128,6 +128,10 @@ struct OwnedLayer {
 
 }  // namespace
 
+namespace fw {
+int record_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace fw
+
 struct fw_moe {
   fw_moe_config cfg{};
   int device = 0;

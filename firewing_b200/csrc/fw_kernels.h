@@ -93,6 +93,10 @@ cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* i
 cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, long long n,
                           const uint16_t* silu_lut, uint16_t* out, cudaStream_t st);
 
+// Store a failure message for fw_last_error() (fixed buffer, no allocation);
+// returns `code`.
+int record_error(int code, const char* msg);
+
 // Seeded synthetic bf16 tensor (identical bits to the CPU generator);
 // key = SplitMix64 stream key of (seed, tensor id).
 cudaError_t launch_synth(uint64_t key, uint32_t tensor, uint64_t start, uint64_t count,

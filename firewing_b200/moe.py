@@ -56,6 +56,12 @@ class _Config(ctypes.Structure):
     ]
 
 
+class _Weights(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in (
+        "router", "gate_up", "down", "shared_gate", "shared_up", "shared_down", "shared_gate_w",
+        "logit_bias")]
+
+
 _lib = None
 vp = ctypes.c_void_p
 
@@ -87,13 +93,15 @@ def library() -> ctypes.CDLL:
     L.fw_linear_bf16.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp]
     L.fw_swiglu_bf16.argtypes = [vp, vp, ctypes.c_int64, vp, vp]
     L.fw_route_bf16.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp, vp]
+    L.fw_moe_forward_noalloc.argtypes = [ctypes.POINTER(_Config), ctypes.POINTER(_Weights), vp,
+                                         ctypes.c_int32, vp, vp, vp, vp]
     L.firewing_cuda_topk_bf16.restype = ctypes.c_bool
     L.firewing_cuda_topk_bf16.argtypes = [vp, ctypes.c_size_t, ctypes.c_size_t,
                                           ctypes.POINTER(ctypes.c_size_t)]
     for name in ("fw_moe_create", "fw_moe_destroy", "fw_moe_load_layer", "fw_moe_synth_layer",
                  "fw_moe_forward", "fw_moe_forward_async", "fw_moe_sync", "fw_moe_memory",
                  "fw_moe_profile", "fw_moe_profile_read",
-                 "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16"):
+                 "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
@@ -217,6 +225,18 @@ class MoeBlock:
         v = ctypes.c_uint64()
         _check(library().fw_moe_memory(self._h, ctypes.byref(v)))
         return int(v.value)
+
+
+def forward_noalloc(config: MoeConfig, weights: dict, x, tokens: int, y, topk_idx=None,
+                    topk_scores=None, stream=None) -> None:
+    """The block over caller-owned DEVICE buffers with no device allocation
+    (fw_moe_forward_noalloc): for callers that cannot cudaMalloc.  `weights`
+    maps router, gate_up, down, shared_gate, shared_up, shared_down,
+    shared_gate_w and optionally logit_bias to device buffers.  Synchronous."""
+    w = _Weights(*[_ptr(weights.get(name)) for name, _ in _Weights._fields_])
+    _check(library().fw_moe_forward_noalloc(ctypes.byref(config.c()), ctypes.byref(w), _ptr(x),
+                                            tokens, _ptr(y), _ptr(topk_idx), _ptr(topk_scores),
+                                            _stream(stream)))
 
 
 def linear_bf16(w, x, rows: int, cols: int, tokens: int, y, stream=None) -> None:

@@ -124,6 +124,38 @@ int fw_moe_profile_read(fw_moe* handle, float* stage_ms, int32_t n);
 /* Device bytes the handle holds (weights + scratch). */
 int fw_moe_memory(const fw_moe* handle, uint64_t* bytes);
 
+/* Device pointers to one layer's weights, in the layouts of
+ * fw_moe_load_layer (logit_bias may be NULL). */
+typedef struct fw_moe_weights {
+    const uint16_t* router;
+    const uint16_t* gate_up;
+    const uint16_t* down;
+    const uint16_t* shared_gate;
+    const uint16_t* shared_up;
+    const uint16_t* shared_down;
+    const uint16_t* shared_gate_w;
+    const float* logit_bias;
+} fw_moe_weights;
+
+/* The whole block, like fw_moe_forward_async, for callers that cannot
+ * allocate device memory (no counterpart in the reference): a framework whose
+ * caching allocator already holds the GPU's memory, or a latency-critical
+ * loop that must not call cudaMalloc/cudaFree, which synchronise the device.
+ * It allocates nothing: weights, x [T][H], y [T][H], topk_idx [T][K] and
+ * topk_scores [T][K] are the caller's DEVICE buffers on the current device
+ * (topk buffers may be NULL), and the scratch lives in an 8 MiB array
+ * compiled into the library, which every GPU that loads the library holds
+ * until exit.  Only the shape fields of `config` are read.  Shapes whose
+ * scratch exceeds 8 MiB are rejected with FW_EINVAL (config 0, H=2048 with
+ * K=10, fits up to T=128).  The first call on a device sets up that device
+ * (looks up the array's device address, uploads the SiLU/sigmoid tables):
+ * make it before any stream capture.  Calls share the scratch array, so
+ * calls that overlap on the GPU race; each call is synchronous on `stream`.
+ * Returns FW_ENAN on NaN router logits, like fw_moe_forward. */
+int fw_moe_forward_noalloc(const fw_moe_config* config, const fw_moe_weights* weights,
+                           const uint16_t* x, int32_t tokens, uint16_t* y, int32_t* topk_idx,
+                           uint16_t* topk_scores, void* stream);
+
 /* ---- primitives over DEVICE buffers (the reference crate's functions) ---- */
 
 /* y[t][r] = bf16(dot(w[r], x[t])) with the reference reduction order:
