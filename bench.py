@@ -59,12 +59,14 @@ def algorithmic_bytes(w: dict, T: int, unique: int) -> int:
     return unique * 3 * H * I * 2 + E * H * 2 + 3 * H * Is * 2 + H * 2 + T * H * 2 * 2
 
 
-def up_kernel_bytes(w: dict, T: int, unique: int, pairs: int) -> int:
-    """Algorithmic bytes of the expert gate_up + SwiGLU kernel: distinct
-    experts' gate_up slices, shared gate/up, activations in, SwiGLU out."""
+def experts_kernel_bytes(w: dict, T: int, unique: int, pairs: int) -> int:
+    """Algorithmic bytes of the expert kernel: the distinct experts' gate_up
+    and down slices, the shared expert, activations in, SwiGLU rows out and
+    back in, weighted rows out."""
     H, I, Is = w["hidden"], w["intermediate"], w["shared_intermediate"]
-    return (unique * 2 * I * H * 2 + 2 * Is * H * 2 + (pairs + T) * H * 2 + pairs * I * 2
-            + T * Is * 2)
+    weights = unique * 3 * I * H * 2 + 3 * Is * H * 2
+    acts = (pairs + T) * H * 2 + 2 * (pairs * I + T * Is) * 2 + (pairs + T) * H * 2
+    return weights + acts
 
 
 # ---------------------------------------------------------------------------
@@ -304,12 +306,12 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
                 st = blk.profile_read()
                 for k_, v_ in st.items():
                     stage_tot[k_] += v_
-                up_bytes += up_kernel_bytes(w, T, unique[l], T * K)
+                up_bytes += experts_kernel_bytes(w, T, unique[l], T * K)
     blk.profile(False)
-    up_s = stage_tot["expert_up"] / 1e3
+    up_s = stage_tot["experts"] / 1e3
     up_gbs = up_bytes / up_s / 1e9
     traffic = None
-    prof_path = os.path.join(ROOT, "profiles", "expert_up_cfg1_traffic.json")
+    prof_path = os.path.join(ROOT, "profiles", "experts_cfg1_traffic.json")
     if os.path.exists(prof_path):
         try:
             p = json.load(open(prof_path))
@@ -318,7 +320,7 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             traffic = None
     roofline = {"bound": "hbm", "achieved": up_gbs, "peak": hbm_peak, "unit": "GB/s",
                 "frac": up_gbs / hbm_peak, "traffic": traffic,
-                "kernel": "k_expert_up (expert gate_up GEMV + SwiGLU)",
+                "kernel": "k_experts (gate_up + SwiGLU and down + scale, persistent)",
                 "peak_source": f"{peak_src} hbm_gbs",
                 "stage_ms_per_layer": {k_: v_ / (prof_steps * L) for k_, v_ in stage_tot.items()}}
 

@@ -175,11 +175,11 @@ bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0
 
 int check_config(const fw_moe_config* c) {
   if (c == nullptr) return fail(FW_EINVAL, "config is null");
-  if (c->hidden <= 0 || c->hidden % 64 != 0 || c->hidden > 8192)
-    return fail(FW_EINVAL, "hidden must be a positive multiple of 64, at most 8192");
+  if (c->hidden <= 0 || c->hidden % 64 != 0 || c->hidden > 4096)
+    return fail(FW_EINVAL, "hidden must be a positive multiple of 64, at most 4096");
   if (c->intermediate <= 0 || c->intermediate % 64 != 0 || c->shared_intermediate <= 0 ||
-      c->shared_intermediate % 64 != 0)
-    return fail(FW_EINVAL, "intermediate sizes must be positive multiples of 64");
+      c->shared_intermediate % 64 != 0 || c->intermediate > 4096 || c->shared_intermediate > 4096)
+    return fail(FW_EINVAL, "intermediate sizes must be positive multiples of 64, at most 4096");
   if (c->experts <= 0 || c->experts % 32 != 0 || c->experts > 1024)
     return fail(FW_EINVAL, "experts must be a multiple of 32, at most 1024");
   if (c->top_k < 1 || c->top_k > 32 || c->top_k > c->experts)
@@ -253,6 +253,7 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &s.act_sh, static_cast<size_t>(M) * Is, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.weighted, static_cast<size_t>(M) * K * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.gated_sh, static_cast<size_t>(M) * H, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.up_done, static_cast<size_t>(E) + 1, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.err, 1, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->x_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->y_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
@@ -473,6 +474,7 @@ int fw_moe_profile_read(fw_moe* h, float* stage_ms, int32_t n) {
   FW_CUDA(cudaEventSynchronize(h->stage_ev[fw::kStages]));
   for (int i = 0; i < fw::kStages; ++i)
     FW_CUDA(cudaEventElapsedTime(&stage_ms[i], h->stage_ev[i], h->stage_ev[i + 1]));
+  for (int i = fw::kStages; i < n; ++i) stage_ms[i] = 0.0f;
   return FW_OK;
 }
 

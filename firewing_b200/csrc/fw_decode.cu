@@ -5,8 +5,8 @@
 //   k_rows_dot       router logits [T][E] (+ shared-gate logit) -- exact GEMV
 //   k_route_permute  f32 softmax, top-k, renormalised scores, sigmoid gate,
 //                    per-expert pair lists (one CTA)
-//   k_expert_up      gate_up GEMV + SwiGLU for every (active expert, token)
-//   k_expert_down    down GEMV + route-weight scale (shared: sigmoid scale)
+//   k_experts        (fw_experts.cu) gate_up + SwiGLU and down + route-weight
+//                    scale for every active expert and the shared expert
 //   k_combine        ascending-expert bf16 accumulation + gated shared add
 //
 // Every GEMV reproduces the reference's f32 reduction order exactly
@@ -168,6 +168,7 @@ struct RouteArgs {
   uint16_t* sh_sig;          // [T]
   int32_t* sorted_slot;      // [T][K]
   int32_t* sched;            // schedule words (see fw_kernels.h)
+  int* up_done;              // [E+1] expert-kernel slot counters to zero
 };
 
 constexpr int kRouteWarps = 32;
@@ -335,6 +336,8 @@ __global__ void __launch_bounds__(1024) k_route_permute(RouteArgs a) {
   int32_t* active = a.sched + 1;
   int32_t* offsets = a.sched + 1 + E;
   int32_t* pairs = a.sched + 2 + 2 * E;
+  if (a.up_done != nullptr)
+    for (int i = threadIdx.x; i <= E; i += blockDim.x) a.up_done[i] = 0;
   if (e < E) {
     const int slot = wsum[warp] + iflag - f;
     const int off = wsum[32 + warp] + ic - c;
@@ -359,140 +362,6 @@ __global__ void __launch_bounds__(1024) k_route_permute(RouteArgs a) {
     for (int wd = 0; wd < (t >> 6); ++wd) rank += __popcll(m[wd]);
     rank += __popcll(m[t >> 6] & ((1ull << (t & 63)) - 1ull));
     pairs[poff[ex_id] + rank] = p;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Expert kernels.  grid.y = schedule slot (active experts ascending, then the
-// shared expert at slot n_active); grid.x = row tile.
-struct ExpertArgs {
-  int H, I, Is, E, K, T;
-  const uint16_t* x;        // [T][H]
-  const uint16_t* gate_up;  // [E_local][2I][H]
-  const uint16_t* down;     // [E_local][H][I]
-  const uint16_t* sh_gate;  // [Is][H]
-  const uint16_t* sh_up;    // [Is][H]
-  const uint16_t* sh_down;  // [H][Is]
-  int expert_base;
-  const uint16_t* silu_lut;
-  const int32_t* sched;
-  const uint16_t* pair_score;  // [T*K]
-  const uint16_t* sh_sig;      // [T]
-  uint16_t* act;               // [T*K][I]
-  uint16_t* act_sh;            // [T][Is]
-  uint16_t* weighted;          // [T*K][H]
-  uint16_t* gated_sh;          // [T][H]
-  int* err;
-};
-
-constexpr int kUpRowsPerCta = 32;    // 8 warps x 4 gate rows (+4 up rows)
-constexpr int kDownRowsPerCta = 64;  // 8 warps x 8 rows
-
-__global__ void __launch_bounds__(256) k_expert_up(ExpertArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const int n_active = a.sched[0];
-  const int s = blockIdx.y;
-  if (s > n_active) return;
-  const bool shared = (s == n_active);
-  const int half = shared ? a.Is : a.I;
-  const int r0 = blockIdx.x * kUpRowsPerCta;
-  if (r0 >= half) return;
-  const int H = a.H, K = a.K;
-  int p0 = 0, n_tok = a.T;
-  const uint16_t *gate_base, *up_base;
-  if (shared) {
-    gate_base = a.sh_gate;
-    up_base = a.sh_up;
-  } else {
-    const int e = a.sched[1 + s] - a.expert_base;
-    p0 = a.sched[1 + a.E + s];
-    n_tok = a.sched[1 + a.E + s + 1] - p0;
-    gate_base = a.gate_up + static_cast<size_t>(e) * 2 * a.I * H;
-    up_base = gate_base + static_cast<size_t>(a.I) * H;
-  }
-  const int32_t* pairs = a.sched + 2 + 2 * a.E + p0;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, q = lane & 3;
-  const int row = r0 + warp * 4 + (g & 3);
-  const uint16_t* row_ptr = (g < 4 ? gate_base : up_base) + static_cast<size_t>(row) * H;
-  extern __shared__ float xs[];
-  for (int t0 = 0; t0 < n_tok; t0 += kTG) {
-    const int nt = min(kTG, n_tok - t0);
-    __syncthreads();
-    stage_rows_f32(xs, H, nt, [&](int r) {
-      const int tok = shared ? (t0 + r) : (pairs[t0 + r] / K);
-      return a.x + static_cast<size_t>(tok) * H;
-    });
-    __syncthreads();
-    float val[kTG];
-    dispatch_row_dot(nt, row_ptr, xs, H, H, q, val);
-    for (int t = 0; t < nt; ++t) {
-      const uint32_t vb = f32_to_bf16(val[t]);
-      const uint32_t ub = __shfl_down_sync(0xffffffffu, vb, 16);
-      if (q == 0 && g < 4) {
-        // swiglu_bf16 (src/expert.rs:562-571): bf16(silu(g)) from the LUT.
-        const float silu = bf16_to_f32(a.silu_lut[vb]);
-        const uint16_t out = f32_to_bf16(silu * bf16_to_f32(ub));
-        uint16_t* dst = shared ? a.act_sh + static_cast<size_t>(t0 + t) * a.Is
-                               : a.act + static_cast<size_t>(pairs[t0 + t]) * a.I;
-        dst[row] = out;
-      }
-    }
-  }
-}
-
-__global__ void __launch_bounds__(256) k_expert_down(ExpertArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const int n_active = a.sched[0];
-  const int s = blockIdx.y;
-  if (s > n_active) return;
-  const bool shared = (s == n_active);
-  const int kd = shared ? a.Is : a.I;
-  const int H = a.H;
-  const int h0 = blockIdx.x * kDownRowsPerCta;
-  int p0 = 0, n_tok = a.T;
-  const uint16_t* w_base;
-  if (shared) {
-    w_base = a.sh_down;
-  } else {
-    const int e = a.sched[1 + s] - a.expert_base;
-    p0 = a.sched[1 + a.E + s];
-    n_tok = a.sched[1 + a.E + s + 1] - p0;
-    w_base = a.down + static_cast<size_t>(e) * H * a.I;
-  }
-  const int32_t* pairs = a.sched + 2 + 2 * a.E + p0;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, q = lane & 3;
-  const int row = h0 + warp * 8 + g;
-  const uint16_t* row_ptr = w_base + static_cast<size_t>(row) * kd;
-  extern __shared__ float xs[];
-  for (int t0 = 0; t0 < n_tok; t0 += kTG) {
-    const int nt = min(kTG, n_tok - t0);
-    __syncthreads();
-    stage_rows_f32(xs, kd, nt, [&](int r) {
-      return shared ? a.act_sh + static_cast<size_t>(t0 + r) * a.Is
-                    : a.act + static_cast<size_t>(pairs[t0 + r]) * a.I;
-    });
-    __syncthreads();
-    float val[kTG];
-    dispatch_row_dot(nt, row_ptr, xs, kd, kd, q, val);
-    if (q == 0) {
-      for (int t = 0; t < nt; ++t) {
-        const float d = bf16_to_f32(f32_to_bf16(val[t]));
-        if (shared) {
-          // gated = bf16(sigmoid * down) (src/expert.rs:1144-1147)
-          const float sig = bf16_to_f32(a.sh_sig[t0 + t]);
-          a.gated_sh[static_cast<size_t>(t0 + t) * H + row] = f32_to_bf16(d * sig);
-        } else {
-          // weighted = bf16(down * route weight) (src/expert.rs:748-751)
-          const int p = pairs[t0 + t];
-          const float w = bf16_to_f32(a.pair_score[p]);
-          a.weighted[static_cast<size_t>(p) * H + row] = f32_to_bf16(d * w);
-        }
-      }
-    }
   }
 }
 
@@ -643,7 +512,7 @@ cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int co
 
 cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
                          uint16_t* score, int* err, cudaStream_t st) {
-  RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr};
+  RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   return launch_route_kernel(a, route_smem(E, T, K, false), st);
 }
 
@@ -679,33 +548,18 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
   // 2. route + permute
   {
     RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
-                sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, sc.sched};
+                sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, sc.sched, sc.up_done};
     e = launch_route_kernel(a, route_smem(s.E, T, s.K, true), st);
     if (e != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
   }
-  ExpertArgs ea{s.H, s.I, s.Is, s.E, s.K, T, x, w.gate_up, w.down, w.sh_gate, w.sh_up, w.sh_down,
-                w.expert_base, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act, sc.act_sh,
-                sc.weighted, sc.gated_sh, sc.err};
-  const int slots = (T * s.K < s.E ? T * s.K : s.E) + 1;
-  // 3. gate_up + SwiGLU
-  {
-    const int half = s.I > s.Is ? s.I : s.Is;
-    const dim3 grid(half / kUpRowsPerCta, slots);
-    e = launch_pdl(k_expert_up, grid, dim3(256), sizeof(float) * kTG * s.H, st, ea);
-    if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
-  }
-  // 4. down + route scale
-  {
-    const int kd = s.I > s.Is ? s.I : s.Is;
-    const dim3 grid(s.H / kDownRowsPerCta, slots);
-    e = launch_pdl(k_expert_down, grid, dim3(256), sizeof(float) * kTG * kd, st, ea);
-    if (e != cudaSuccess || (e = mark(4)) != cudaSuccess) return e;
-  }
-  // 5. combine
+  // 3. experts: gate_up + SwiGLU, then down + scale (one persistent kernel)
+  e = launch_experts(s, w, luts, sc, x, T, topk_score, st);
+  if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
+  // 4. combine
   {
     CombineArgs a{s.H, s.K, T, sc.sorted_slot, sc.weighted, sc.gated_sh, y};
     e = launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
-    if (e == cudaSuccess) e = mark(5);
+    if (e == cudaSuccess) e = mark(4);
   }
   return e;
 }

@@ -55,6 +55,7 @@ struct Scratch {
   uint16_t* act_sh = nullptr;    // [T][Is]
   uint16_t* weighted = nullptr;  // [T*K][H]
   uint16_t* gated_sh = nullptr;  // [T][H]
+  int* up_done = nullptr;        // [E+1] per-slot SwiGLU completion counters
   int* err = nullptr;            // device status word
   int max_T = 0;
 };
@@ -76,7 +77,7 @@ struct Luts {
 };
 
 // Pipeline stages of one block forward (for per-stage timing).
-enum Stage : int { kStageRouter = 0, kStageRoute, kStageUp, kStageDown, kStageCombine, kStages };
+enum Stage : int { kStageRouter = 0, kStageRoute, kStageExperts, kStageCombine, kStages };
 
 // Whole decode-path block for T tokens, stream-ordered.  When stage_events is
 // non-null, kStages + 1 events are recorded around the stages.
@@ -84,6 +85,12 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
                          const Scratch& sc, const uint16_t* x, int T, uint16_t* y,
                          int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
                          cudaEvent_t* stage_events = nullptr);
+
+// The persistent expert kernel (gate_up + SwiGLU and down + scale for every
+// active expert and the shared expert); dynamic shared memory it needs.
+size_t experts_smem_bytes(const Shape& s);
+cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
+                           const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st);
 
 // Primitives (the reference crate's functions over device buffers).
 cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int cols, int T,

@@ -128,6 +128,7 @@ size_t carve(const fw::Shape& s, int T, bool need_idx, bool need_score, unsigned
   sc->act_sh = reinterpret_cast<uint16_t*>(take(M * Is * 2));
   sc->weighted = reinterpret_cast<uint16_t*>(take(M * K * H * 2));
   sc->gated_sh = reinterpret_cast<uint16_t*>(take(M * H * 2));
+  sc->up_done = reinterpret_cast<int*>(take((E + 1) * 4));
   sc->err = reinterpret_cast<int*>(take(sizeof(int)));
   *idx = need_idx ? reinterpret_cast<int32_t*>(take(M * K * 4)) : nullptr;
   *score = need_score ? reinterpret_cast<uint16_t*>(take(M * K * 2)) : nullptr;
@@ -144,8 +145,9 @@ extern "C" int fw_moe_forward_noalloc(const fw_moe_config* config, const fw_moe_
   if (config == nullptr || weights == nullptr)
     return fw::record_error(FW_EINVAL, "fw_moe_forward_noalloc: config / weights is null");
   const fw_moe_config& c = *config;
-  if (c.hidden <= 0 || c.hidden % 64 != 0 || c.hidden > 6400 || c.intermediate <= 0 ||
+  if (c.hidden <= 0 || c.hidden % 64 != 0 || c.hidden > 4096 || c.intermediate <= 0 ||
       c.intermediate % 64 != 0 || c.shared_intermediate <= 0 || c.shared_intermediate % 64 != 0 ||
+      c.intermediate > 4096 || c.shared_intermediate > 4096 ||
       c.experts <= 0 || c.experts % 32 != 0 || c.experts > 1024 || c.top_k < 1 || c.top_k > 32 ||
       c.top_k > c.experts)
     return fw::record_error(FW_EINVAL, "fw_moe_forward_noalloc: unsupported block shape");

@@ -210,15 +210,15 @@ class MoeBlock:
     def sync(self, stream=None) -> None:
         _check(library().fw_moe_sync(self._h, _stream(stream)))
 
-    STAGES = ("router", "route", "expert_up", "expert_down", "combine")
+    STAGES = ("router", "route", "experts", "combine")
 
     def profile(self, enable: bool) -> None:
         _check(library().fw_moe_profile(self._h, 1 if enable else 0))
 
     def profile_read(self) -> dict:
         """Stage durations (ms) of the last forward while profiling is on."""
-        buf = (ctypes.c_float * 5)()
-        _check(library().fw_moe_profile_read(self._h, buf, 5))
+        buf = (ctypes.c_float * len(self.STAGES))()
+        _check(library().fw_moe_profile_read(self._h, buf, len(self.STAGES)))
         return dict(zip(self.STAGES, [float(v) for v in buf]))
 
     def memory_bytes(self) -> int:

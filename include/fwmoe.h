@@ -47,8 +47,8 @@ typedef struct fw_moe fw_moe;
 
 /* Block configuration.  The reference hard-codes these
  * (src/decoder_layer.rs:14-17, 40-42; src/metal_moe.rs:15-21).
- * Constraints: hidden % 64 == 0 and <= 8192; intermediate and
- * shared_intermediate % 64 == 0; experts % 32 == 0 and <= 1024;
+ * Constraints: hidden, intermediate and shared_intermediate multiples of
+ * 64, at most 4096; experts % 32 == 0 and <= 1024;
  * 1 <= top_k <= min(32, experts); 1 <= max_tokens <= 256. */
 typedef struct fw_moe_config {
     int32_t hidden;              /* H */
@@ -114,10 +114,10 @@ int fw_moe_sync(fw_moe* handle, void* stream);
 
 /* Per-stage timing, for roofline measurement (the reference times its phases
  * with host intervals, src/metal_moe.rs:473-477, 590-606).  While enabled,
- * every forward records CUDA events around its five kernels (router logits,
- * route + permute, expert gate_up + SwiGLU, expert down + scale, combine),
+ * every forward records CUDA events around its four kernels (router logits,
+ * route + permute, experts: gate_up + SwiGLU and down + scale, combine),
  * which serialises them; fw_moe_profile_read waits for the last forward and
- * returns the five durations in milliseconds (n >= 5). */
+ * returns the four durations in milliseconds (n >= 4). */
 int fw_moe_profile(fw_moe* handle, int32_t enable);
 int fw_moe_profile_read(fw_moe* handle, float* stage_ms, int32_t n);
 
