@@ -169,6 +169,7 @@ struct RouteArgs {
   int32_t* sorted_slot;      // [T][K]
   int32_t* sched;            // schedule words (see fw_kernels.h)
   int* up_done;              // [E+1] expert-kernel slot counters to zero
+  int tgp, qpr, qps, ops;    // expert-kernel pass size, quads/octets per slot
 };
 
 constexpr int kRouteWarps = 32;
@@ -280,7 +281,7 @@ __global__ void __launch_bounds__(1024) k_route_permute(RouteArgs a) {
   if (a.sched == nullptr) return;
   __syncthreads();
 
-  // ---- permute: expert schedule for the up/down kernels ----
+  // ---- permute: expert schedule for the expert kernel ----
   const int P = T * K;
   const int W = (T + 63) >> 6;  // 64-bit token masks per expert
   unsigned long long* mask = reinterpret_cast<unsigned long long*>(pidx + ((P + 3) & ~3));
@@ -338,20 +339,79 @@ __global__ void __launch_bounds__(1024) k_route_permute(RouteArgs a) {
   int32_t* pairs = a.sched + 2 + 2 * E;
   if (a.up_done != nullptr)
     for (int i = threadIdx.x; i <= E; i += blockDim.x) a.up_done[i] = 0;
+  const int my_slot = wsum[warp] + iflag - f;  // this expert's slot (if active)
   if (e < E) {
-    const int slot = wsum[warp] + iflag - f;
     const int off = wsum[32 + warp] + ic - c;
     poff[e] = off;
     if (f) {
-      active[slot] = e;
-      offsets[slot] = off;
+      active[my_slot] = e;
+      offsets[my_slot] = off;
     }
     if (e == E - 1) {
-      a.sched[0] = slot + f;
-      offsets[slot + f] = off + c;
+      a.sched[0] = my_slot + f;
+      offsets[my_slot + f] = off + c;
     }
   }
   __syncthreads();
+  // Cost prefixes for the expert kernel.  A slot of n tokens has
+  // ceil(n / tgp) token passes of qpr quads (up) and ops octets (down); a
+  // unit of a pass with nt tokens costs 4 + pad(nt) (pad = 1, 2, 4, 8: the
+  // tokens the kernel computes), weighing bytes and FMAs.
+  {
+    const int nfull = f ? c / a.tgp : 0, rem = f ? c % a.tgp : 0;
+    const int pad = rem <= 1 ? rem : rem <= 2 ? 2 : rem <= 4 ? 4 : 8;
+    const int pc = nfull * (4 + a.tgp) + (rem ? 4 + pad : 0);  // per-unit-row cost of the slot
+    const int vu = pc * a.qpr, vd = pc * a.ops;
+    int iu = vu, id = vd;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int yu = __shfl_up_sync(0xffffffffu, iu, o);
+      const int yd = __shfl_up_sync(0xffffffffu, id, o);
+      if (lane >= o) {
+        iu += yu;
+        id += yd;
+      }
+    }
+    __syncthreads();  // wsum reuse
+    if (lane == 31) {
+      wsum[warp] = iu;
+      wsum[32 + warp] = id;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int su0 = wsum[lane], sd0 = wsum[32 + lane];
+      int su = su0, sd = sd0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int yu = __shfl_up_sync(0xffffffffu, su, o);
+        const int yd = __shfl_up_sync(0xffffffffu, sd, o);
+        if (lane >= o) {
+          su += yu;
+          sd += yd;
+        }
+      }
+      wsum[lane] = su - su0;
+      wsum[32 + lane] = sd - sd0;
+    }
+    __syncthreads();
+    int32_t* up_pref = pairs + P;
+    int32_t* dn_pref = up_pref + E + 2;
+    if (e < E && f) {
+      up_pref[my_slot] = wsum[warp] + iu - vu;
+      dn_pref[my_slot] = wsum[32 + warp] + id - vd;
+    }
+    if (e == E - 1) {
+      const int n_act = my_slot + f;
+      const int sfull = T / a.tgp, srem = T % a.tgp;
+      const int spad = srem <= 1 ? srem : srem <= 2 ? 2 : srem <= 4 ? 4 : 8;
+      const int spc = sfull * (4 + a.tgp) + (srem ? 4 + spad : 0);
+      const int tu = wsum[warp] + iu, td = wsum[32 + warp] + id;
+      up_pref[n_act] = tu;
+      up_pref[n_act + 1] = tu + spc * a.qps;
+      dn_pref[n_act] = td;
+      dn_pref[n_act + 1] = td + spc * a.ops;
+    }
+  }
   // Stable fill: a pair's rank in its expert's list is the number of earlier
   // tokens that selected the same expert (an expert appears once per token).
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
@@ -512,7 +572,8 @@ cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int co
 
 cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
                          uint16_t* score, int* err, cudaStream_t st) {
-  RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+              0, 0, 0, 0};
   return launch_route_kernel(a, route_smem(E, T, K, false), st);
 }
 
@@ -548,7 +609,8 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
   // 2. route + permute
   {
     RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
-                sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, sc.sched, sc.up_done};
+                sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, sc.sched, sc.up_done,
+                experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8};
     e = launch_route_kernel(a, route_smem(s.E, T, s.K, true), st);
     if (e != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
   }

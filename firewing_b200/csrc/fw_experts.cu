@@ -1,33 +1,34 @@
 // fw_experts.cu -- persistent expert kernel for the decode path (sm_100a).
 //
-// One CTA per SM.  The work of a layer is two row spaces:
-//   up   : for every schedule slot (active routed experts in ascending id,
-//          then the shared expert) its gate/up row pairs, in "quads" of 4
-//          gate rows + the 4 matching up rows;
-//   down : for every slot its H down rows, in "octets" of 8 rows.
-// Each CTA takes one contiguous, equal-sized range of each space, so the
-// bytes streamed per SM are balanced whatever the routing.  Inside a CTA,
-// 8 warps take the quads (octets) of the range round-robin.
+// One CTA per SM (cooperative launch, so all CTAs are co-resident).  A
+// layer's expert work is two unit spaces, each ordered slot-major (slots =
+// active routed experts in ascending id, then the shared expert at slot
+// n_active):
+//   up   : unit = (slot, token pass, quad); a quad is 4 gate rows + the 4
+//          matching up rows of the slot's gate_up weights;
+//   down : unit = (slot, token pass, octet); an octet is 8 down rows.
+// A token pass covers up to `tgp` of the slot's tokens (their activations
+// sit in shared memory as f32).  Units all stream the same bytes, so each
+// CTA takes one contiguous, equal-sized unit range: a slot with many tokens
+// (the shared expert, a hot expert) spreads its passes over several SMs.
 //
-// Every warp owns a 4-stage shared-memory ring.  Lane 0 runs ahead of the
-// warp's own consumption and issues one bulk async copy per weight row
-// (cp.async.bulk, completion counted on the stage's mbarrier; never
-// multicast), so up to 3 stages x 4 KB per warp are in flight regardless of
-// occupancy.  A stage is 8 rows x up to 256 columns.  Rows are padded by
-// 16 bytes in shared memory so the 8 lanes of a quarter-warp, which read the
-// same columns of 8 different rows, hit 8 distinct bank groups.
+// Inside a CTA the units of a pass go round-robin to 8 warps.  Every warp
+// owns a 2-stage shared-memory ring.  A stage is 8 rows x up to 512 columns
+// (1 KB per row).  After consuming a stage the warp refills it: lane 0 posts
+// the expected bytes on the stage's mbarrier and lanes 0..7 each issue one
+// row's bulk async copy (cp.async.bulk, never multicast).  Rows are padded
+// by 16 bytes so the 8 lanes of a quarter-warp, which read the same columns
+// of 8 different rows, hit 8 distinct bank groups.
 //
-// Lane mapping (exact reference reduction, src/expert.rs:514-552): lane l
-// owns row r = l & 7 and partials 8q..8q+7, q = l >> 3; it walks the
-// 32-column blocks of its row in order, one 16-byte shared load per block,
-// and fw::reduce_partials_strided applies the reference tree.
+// Exact reduction (src/expert.rs:514-552): lane l owns row r = l & 7 and
+// partials 8q..8q+7, q = l >> 3; it walks the 32-column blocks of its row
+// in order with one 16-byte shared load per block, and
+// fw::reduce_partials_strided applies the reference tree.
 //
-// The down rows of a slot need all of that slot's SwiGLU rows: the CTA that
-// finishes its share of a slot's quads adds them to up_done[slot]
-// (release); a CTA about to stage a slot's activations for its down rows
-// waits (acquire, bounded) until the count is complete.  Up work never
-// waits, and all CTAs are co-resident (cooperative launch), so the waits
-// always end.
+// The down rows of a slot need all of that slot's SwiGLU rows: a CTA adds
+// the up units it finished for a slot to up_done[slot] (release); a CTA
+// waits (acquire, bounded) for the slot's full unit count before staging
+// its activations.  Up work never waits, so the waits always end.
 #include <cstdint>
 
 #include "fw_common.cuh"
@@ -38,15 +39,15 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kRing = 4;                                 // stages per warp ring
-constexpr int kMaxChunk = 256;                        // columns per stage
-constexpr int kStageBytes = 8 * (kMaxChunk * 2 + 16);  // 4224
-constexpr int kTGP = 4;                                // tokens per pass
-constexpr uint64_t kWaitNs = 2000000000ull;            // bounded waits: 2 s
-constexpr uint64_t kDrainNs = 200000000ull;            // drain after abort: 0.2 s
+constexpr int kRing = 2;                          // stages per warp ring
+constexpr int kMaxChunk = 512;                    // columns per stage
+constexpr int kStageBytes = 8 * (kMaxChunk * 2 + 16);  // 8320
+constexpr int kMaxTGP = 8;                        // tokens per pass (upper bound)
+constexpr uint64_t kWaitNs = 2000000000ull;       // bounded waits: 2 s
+constexpr uint64_t kDrainNs = 200000000ull;       // drain after abort: 0.2 s
 
 struct ExpertsArgs {
-  int H, I, Is, E, K, T;
+  int H, I, Is, E, K, T, tgp;
   const uint16_t* x;        // [T][H]
   const uint16_t* gate_up;  // [E_local][2I][H]
   const uint16_t* down;     // [E_local][H][I]
@@ -72,160 +73,192 @@ __device__ __forceinline__ int chunk_cols(int k) {
   return 32;
 }
 
-// Geometry of one launch, identical in every thread.
-struct Geo {
-  int n_active;    // routed slots; the shared expert is slot n_active
-  int qpr, qps;    // quads per routed / shared slot
-  int ops;         // octets per slot (H / 8)
-  int up_lo, up_hi;  // this CTA's quad range
-  int dn_lo, dn_hi;  // this CTA's octet range
-  int cu;          // up chunk columns
-  int cdr, cds;    // down chunk columns (routed / shared)
+// Per-launch constants, identical in every thread of a CTA.
+struct Ctx {
+  const ExpertsArgs* a;
+  int n_active;
+  const int32_t* up_pref;  // [n_active + 2] unit prefix per slot
+  const int32_t* dn_pref;
+  int lo[2], hi[2];        // this CTA's unit range per phase
+  int qpr, qps, ops;       // quads per routed / shared slot, octets per slot
+  int cu, cdr, cds;        // chunk columns: up, down routed, down shared
 };
 
-__device__ __forceinline__ int slot_qbase(const Geo& g, int s) { return s * g.qpr; }
-__device__ __forceinline__ int slot_nq(const Geo& g, int s) { return s < g.n_active ? g.qpr : g.qps; }
-__device__ __forceinline__ int slot_tokens(const ExpertsArgs& a, const Geo& g, int s) {
-  return s < g.n_active ? a.sched[1 + a.E + s + 1] - a.sched[1 + a.E + s] : a.T;
+__device__ __forceinline__ const int32_t* pref(const Ctx& c, int phase) { return phase ? c.dn_pref : c.up_pref; }
+__device__ __forceinline__ int units_per_pass(const Ctx& c, int phase, int s) {
+  return phase ? c.ops : (s < c.n_active ? c.qpr : c.qps);
 }
-// first slot of a phase's range, and one past the last
-__device__ __forceinline__ void phase_slots(const Geo& g, int phase, int& s0, int& s1) {
-  if (phase == 0) {
-    if (g.up_lo >= g.up_hi) {
-      s0 = s1 = 0;
-      return;
-    }
-    const int routed_q = g.n_active * g.qpr;
-    s0 = g.up_lo < routed_q ? g.up_lo / g.qpr : g.n_active;
-    s1 = (g.up_hi - 1) < routed_q ? (g.up_hi - 1) / g.qpr + 1 : g.n_active + 1;
-  } else {
-    if (g.dn_lo >= g.dn_hi) {
-      s0 = s1 = 0;
-      return;
-    }
-    s0 = g.dn_lo / g.ops;
-    s1 = (g.dn_hi - 1) / g.ops + 1;
-  }
+__device__ __forceinline__ int n_chunks(const Ctx& c, int phase, int s) {
+  if (phase == 0) return c.a->H / c.cu;
+  return s < c.n_active ? c.a->I / c.cdr : c.a->Is / c.cds;
 }
-__device__ __forceinline__ void slot_items(const Geo& g, int phase, int s, int& lo, int& hi) {
-  if (phase == 0) {
-    const int b = slot_qbase(g, s);
-    lo = max(g.up_lo, b);
-    hi = min(g.up_hi, b + slot_nq(g, s));
-  } else {
-    const int b = s * g.ops;
-    lo = max(g.dn_lo, b);
-    hi = min(g.dn_hi, b + g.ops);
-  }
-}
-__device__ __forceinline__ int slot_chunks(const ExpertsArgs& a, const Geo& g, int phase, int s) {
-  if (phase == 0) return a.H / g.cu;
-  return s < g.n_active ? a.I / g.cdr : a.Is / g.cds;
+__device__ __forceinline__ int chunk_width(const Ctx& c, int phase, int s) {
+  return phase == 0 ? c.cu : (s < c.n_active ? c.cdr : c.cds);
 }
 
-// Issue-side cursor over this warp's stage sequence:
-// phase -> slot -> token pass -> item (warp-strided) -> chunk.
+// A pass = (phase, slot, token pass) restricted to this CTA: items qa..qb-1
+// (local quad / octet indices of the slot).  CTAs split each phase's COST
+// space, where a unit of a pass with nt tokens costs 4 + pad(nt) (the route
+// kernel's prefix); a unit belongs to the CTA whose range holds its start.
+struct Pass {
+  int phase, s, tg, qa, qb;
+};
+
+__device__ __forceinline__ int pad_tokens(int nt) { return nt <= 1 ? nt : nt <= 2 ? 2 : nt <= 4 ? 4 : 8; }
+
+__device__ __forceinline__ int slot_tokens(const Ctx& c, int s) {
+  const ExpertsArgs& a = *c.a;
+  return s < c.n_active ? a.sched[1 + a.E + s + 1] - a.sched[1 + a.E + s] : a.T;
+}
+
+// Slot whose cost range contains u (binary search over the prefix).
+__device__ int slot_of(const int32_t* p, int n_slots, int u) {
+  int lo = 0, hi = n_slots - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p[mid] <= u) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ int ceil_div_pos(int a, int b) { return a <= 0 ? 0 : (a + b - 1) / b; }
+
+// From pass (s, tg) onwards, find the first pass with units in this CTA's
+// range; false when the range is exhausted.
+__device__ bool settle_pass(const Ctx& c, int phase, int s, int tg, Pass& p) {
+  const int32_t* pr = pref(c, phase);
+  const int lo = c.lo[phase], hi = c.hi[phase];
+  const int tgp = c.a->tgp;
+  while (s <= c.n_active) {
+    const int ntok = slot_tokens(c, s);
+    const int ntg = (ntok + tgp - 1) / tgp;
+    const int n = units_per_pass(c, phase, s);
+    for (; tg < ntg; ++tg) {
+      const int base = pr[s] + tg * n * (4 + tgp);
+      if (base >= hi) return false;
+      const int nt = min(tgp, ntok - tg * tgp);
+      const int u = 4 + pad_tokens(nt);
+      const int i0 = ceil_div_pos(lo - base, u);
+      const int i1 = min(n, ceil_div_pos(hi - base, u));
+      if (i0 < i1) {
+        p = Pass{phase, s, tg, i0, i1};
+        return true;
+      }
+    }
+    ++s;
+    tg = 0;
+  }
+  return false;
+}
+
+__device__ bool first_pass(const Ctx& c, int phase, Pass& p) {
+  const int lo = c.lo[phase], hi = c.hi[phase];
+  if (lo >= hi) return false;
+  const int32_t* pr = pref(c, phase);
+  const int s = slot_of(pr, c.n_active + 1, lo);
+  const int n = units_per_pass(c, phase, s);
+  const int tg = (lo - pr[s]) / (n * (4 + c.a->tgp));
+  return settle_pass(c, phase, s, tg, p);
+}
+
+__device__ bool next_pass(const Ctx& c, Pass& p) {
+  Pass q;
+  if (!settle_pass(c, p.phase, p.s, p.tg + 1, q)) return false;
+  p = q;
+  return true;
+}
+
+// Issue-side cursor over this warp's stages (uniform across the warp).
 struct Cursor {
-  int phase, slot, s_end, tg, ntg, item, lo, hi, chunk, nchunks;
+  Pass p;
+  bool live;
+  int item, chunk, nchunks, cols;
+  const uint16_t* row0;  // up: gate base; down: down base
+  const uint16_t* row1;  // up: up base
 };
 
-__device__ void cursor_enter_slot(Cursor& c, const ExpertsArgs& a, const Geo& g, int warp) {
-  slot_items(g, c.phase, c.slot, c.lo, c.hi);
-  c.tg = 0;
-  c.ntg = (slot_tokens(a, g, c.slot) + kTGP - 1) / kTGP;
-  c.item = c.lo + warp;
-  c.chunk = 0;
-  c.nchunks = slot_chunks(a, g, c.phase, c.slot);
-}
-
-// Move forward until the cursor names a stage, or phase == 2 (done).
-__device__ void cursor_normalize(Cursor& c, const ExpertsArgs& a, const Geo& g, int warp) {
-  while (c.phase < 2) {
-    if (c.slot < c.s_end && c.item < c.hi) return;
-    if (c.slot < c.s_end) {
-      if (++c.tg < c.ntg) {
-        c.item = c.lo + warp;
-        c.chunk = 0;
-        continue;
-      }
-      ++c.slot;
-      if (c.slot < c.s_end) {
-        cursor_enter_slot(c, a, g, warp);
-        continue;
-      }
-    }
-    // next phase
-    ++c.phase;
-    if (c.phase < 2) {
-      phase_slots(g, c.phase, c.slot, c.s_end);
-      if (c.slot < c.s_end) cursor_enter_slot(c, a, g, warp);
-    }
-  }
-}
-
-__device__ void cursor_begin(Cursor& c, const ExpertsArgs& a, const Geo& g, int warp) {
-  c.phase = 0;
-  phase_slots(g, 0, c.slot, c.s_end);
-  if (c.slot < c.s_end) cursor_enter_slot(c, a, g, warp);
-  cursor_normalize(c, a, g, warp);
-}
-
-__device__ void cursor_next(Cursor& c, const ExpertsArgs& a, const Geo& g, int warp) {
-  if (++c.chunk == c.nchunks) {
-    c.chunk = 0;
-    c.item += kWarps;
-  }
-  cursor_normalize(c, a, g, warp);
-}
-
-// Lane 0: issue the 8 row copies of the stage the cursor names into `buf`.
-__device__ void issue_stage(const Cursor& c, const ExpertsArgs& a, const Geo& g, unsigned char* buf,
-                            uint64_t* bar, uint64_t policy) {
-  if (c.phase == 0) {
-    const int lq = c.item - slot_qbase(g, c.slot);
-    const uint16_t *gate_base, *up_base;
-    if (c.slot < g.n_active) {
-      const int e = a.sched[1 + c.slot] - a.expert_base;
-      gate_base = a.gate_up + static_cast<size_t>(e) * 2 * a.I * a.H;
-      up_base = gate_base + static_cast<size_t>(a.I) * a.H;
+__device__ void cursor_slot(Cursor& k, const Ctx& c) {
+  const ExpertsArgs& a = *c.a;
+  const int s = k.p.s;
+  k.nchunks = n_chunks(c, k.p.phase, s);
+  k.cols = chunk_width(c, k.p.phase, s);
+  if (k.p.phase == 0) {
+    if (s < c.n_active) {
+      k.row0 = a.gate_up + static_cast<size_t>(a.sched[1 + s] - a.expert_base) * 2 * a.I * a.H;
+      k.row1 = k.row0 + static_cast<size_t>(a.I) * a.H;
     } else {
-      gate_base = a.sh_gate;
-      up_base = a.sh_up;
-    }
-    const int cols = g.cu, pitch = cols * 2 + 16;
-    const uint32_t bytes = cols * 2;
-    mbar_arrive_expect_tx(bar, 8 * bytes);
-    const size_t col0 = static_cast<size_t>(c.chunk) * cols;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const uint16_t* base = r < 4 ? gate_base : up_base;
-      const size_t row = static_cast<size_t>(4 * lq + (r & 3));
-      bulk_g2s(buf + r * pitch, base + row * a.H + col0, bytes, bar, policy);
+      k.row0 = a.sh_gate;
+      k.row1 = a.sh_up;
     }
   } else {
-    const int lo8 = c.item - c.slot * g.ops;
-    const bool routed = c.slot < g.n_active;
-    const int kd = routed ? a.I : a.Is;
-    const int cols = routed ? g.cdr : g.cds, pitch = cols * 2 + 16;
-    const uint16_t* base = routed ? a.down + static_cast<size_t>(a.sched[1 + c.slot] - a.expert_base) *
-                                                 a.H * a.I
-                                  : a.sh_down;
-    const uint32_t bytes = cols * 2;
-    mbar_arrive_expect_tx(bar, 8 * bytes);
-    const size_t col0 = static_cast<size_t>(c.chunk) * cols;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const size_t row = static_cast<size_t>(8 * lo8 + r);
-      bulk_g2s(buf + r * pitch, base + row * kd + col0, bytes, bar, policy);
-    }
+    k.row0 = s < c.n_active ? a.down + static_cast<size_t>(a.sched[1 + s] - a.expert_base) * a.H * a.I
+                            : a.sh_down;
+    k.row1 = nullptr;
   }
 }
 
-// Accumulate one stage: 8 rows x `cols` columns starting at column col0,
-// NT tokens of f32 activations (row stride xstride) in shared memory.
+// Advance to the first pass with an item for this warp (or end).
+__device__ void cursor_settle(Cursor& k, const Ctx& c, int warp) {
+  while (k.live && k.item >= k.p.qb) {
+    const int s_prev = k.p.s, ph_prev = k.p.phase;
+    if (!next_pass(c, k.p)) {
+      if (k.p.phase == 0 && first_pass(c, 1, k.p)) {
+        // continue in the down phase
+      } else {
+        k.live = false;
+        return;
+      }
+    }
+    k.item = k.p.qa + warp;
+    k.chunk = 0;
+    if (k.p.s != s_prev || k.p.phase != ph_prev) cursor_slot(k, c);
+  }
+}
+
+__device__ void cursor_begin(Cursor& k, const Ctx& c, int warp) {
+  k.live = first_pass(c, 0, k.p) || first_pass(c, 1, k.p);
+  if (!k.live) return;
+  k.item = k.p.qa + warp;
+  k.chunk = 0;
+  cursor_slot(k, c);
+  cursor_settle(k, c, warp);
+}
+
+__device__ __forceinline__ void cursor_next(Cursor& k, const Ctx& c, int warp) {
+  if (++k.chunk == k.nchunks) {
+    k.chunk = 0;
+    k.item += kWarps;
+    cursor_settle(k, c, warp);
+  }
+}
+
+// Whole warp: refill `buf` with the stage the cursor names.
+__device__ __forceinline__ void issue_stage(const Cursor& k, const Ctx& c, unsigned char* buf, uint64_t* bar,
+                                            uint64_t policy, int lane) {
+  const ExpertsArgs& a = *c.a;
+  const int pitch = k.cols * 2 + 16;
+  const uint32_t bytes = k.cols * 2;
+  fence_proxy_async_smem();
+  if (lane == 0) mbar_arrive_expect_tx(bar, 8 * bytes);
+  __syncwarp();
+  if (lane < 8) {
+    const uint16_t* src;
+    if (k.p.phase == 0) {
+      const size_t row = static_cast<size_t>(4 * k.item + (lane & 3));
+      src = (lane < 4 ? k.row0 : k.row1) + row * a.H;
+    } else {
+      const int kd = k.p.s < c.n_active ? a.I : a.Is;
+      src = k.row0 + static_cast<size_t>(8 * k.item + lane) * kd;
+    }
+    bulk_g2s(buf + lane * pitch, src + static_cast<size_t>(k.chunk) * k.cols, bytes, bar, policy);
+  }
+}
+
+// Accumulate one stage: 8 rows x `cols` columns from column col0, NT tokens
+// of f32 activations (row stride xstride) in shared memory.
 template <int NT>
-__device__ __forceinline__ void stage_fma(const unsigned char* buf, int pitch, int cols, const float* xs,
-                                          int xstride, int col0, int r, int q, float (&acc)[kTGP][8]) {
+__device__ __forceinline__ void stage_fma(const unsigned char* buf, int pitch, int cols, const float* xs, int xstride,
+                                          int col0, int r, int q, float (&acc)[kMaxTGP][8]) {
   const uint16_t* wrow = reinterpret_cast<const uint16_t*>(buf + r * pitch) + q * 8;
   const float* xq = xs + col0 + q * 8;
   const int nb = cols >> 5;
@@ -240,101 +273,162 @@ __device__ __forceinline__ void stage_fma(const unsigned char* buf, int pitch, i
   }
 }
 
-__device__ __forceinline__ void stage_fma_nt(int nt, const unsigned char* buf, int pitch, int cols,
-                                             const float* xs, int xstride, int col0, int r, int q,
-                                             float (&acc)[kTGP][8]) {
-  if (nt == 1)
-    stage_fma<1>(buf, pitch, cols, xs, xstride, col0, r, q, acc);
-  else if (nt == 2)
-    stage_fma<2>(buf, pitch, cols, xs, xstride, col0, r, q, acc);
-  else if (nt == 3)
-    stage_fma<3>(buf, pitch, cols, xs, xstride, col0, r, q, acc);
-  else
-    stage_fma<4>(buf, pitch, cols, xs, xstride, col0, r, q, acc);
+// Per-pass token table in shared memory: tok_row[t] is the pair id (routed)
+// or token id (shared) of the pass's token t; tok_scale[t] its route weight
+// (routed) or sigmoid gate (shared) as f32.
+template <int NT>
+__device__ __forceinline__ void epilogue(const Ctx& c, const Pass& p, int item, int nt, float (&acc)[kMaxTGP][8],
+                                         int lane, const int* tok_row, const float* tok_scale) {
+  const ExpertsArgs& a = *c.a;
+  const bool routed = p.s < c.n_active;
+  float val[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) val[t] = reduce_partials_strided(acc[t]);
+  if (p.phase == 0) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint32_t vb = f32_to_bf16(val[t]);
+      const uint32_t ub = __shfl_down_sync(0xffffffffu, vb, 4);
+      if (lane < 4 && t < nt) {
+        // swiglu_bf16 (src/expert.rs:562-571): bf16(silu) from the table
+        const uint16_t out = f32_to_bf16(bf16_to_f32(a.silu_lut[vb]) * bf16_to_f32(ub));
+        const int row = 4 * item + lane;
+        if (routed)
+          a.act[static_cast<size_t>(tok_row[t]) * a.I + row] = out;
+        else
+          a.act_sh[static_cast<size_t>(tok_row[t]) * a.Is + row] = out;
+      }
+    }
+  } else if (lane < 8) {
+    const int h = 8 * item + lane;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      if (t < nt) {
+        const float d = bf16_to_f32(f32_to_bf16(val[t]));
+        // routed: bf16(down * route weight) (src/expert.rs:748-751);
+        // shared: bf16(sigmoid * down) (src/expert.rs:1144-1147)
+        uint16_t* dst = routed ? a.weighted : a.gated_sh;
+        dst[static_cast<size_t>(tok_row[t]) * a.H + h] = f32_to_bf16(d * tok_scale[t]);
+      }
+    }
+  }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) k_experts(ExpertsArgs a) {
+template <int NT>
+__device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, const float* xs, int xstride,
+                                          unsigned char* my_ring, uint64_t* my_bars, Cursor& k, int& consumed,
+                                          uint64_t policy, int warp, int lane, int* s_abort, const int* tok_row,
+                                          const float* tok_scale) {
+  const int r = lane & 7, q = lane >> 3;
+  const int nch = n_chunks(c, p.phase, p.s);
+  const int cols = chunk_width(c, p.phase, p.s);
+  const int pitch = cols * 2 + 16;
+  for (int item = p.qa + warp; item < p.qb; item += kWarps) {
+    float acc[kMaxTGP][8];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[t][i] = 0.0f;
+    for (int ch = 0; ch < nch; ++ch) {
+      const int j = consumed % kRing;
+      if (!mbar_wait_bounded(&my_bars[j], (consumed / kRing) & 1, kWaitNs)) {
+        if (lane == 0) set_error(c.a->err, kErrTimeout);
+        *reinterpret_cast<volatile int*>(s_abort) = 1;
+        return false;
+      }
+      stage_fma<NT>(my_ring + j * kStageBytes, pitch, cols, xs, xstride, ch * cols, r, q, acc);
+      ++consumed;
+      __syncwarp();
+      if (k.live) {
+        issue_stage(k, c, my_ring + j * kStageBytes, &my_bars[j], policy, lane);
+        cursor_next(k, c, warp);
+      }
+    }
+    epilogue<NT>(c, p, item, nt, acc, lane, tok_row, tok_scale);
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__ ExpertsArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* ring = smem;                                                    // [warps][stages][4224]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kRing * kStageBytes);  // [warps][stages]
+  unsigned char* ring = smem;                                                       // [warps][kRing][8320]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kRing * kStageBytes);  // [warps][kRing]
   int* s_abort = reinterpret_cast<int*>(bars + kWarps * kRing);
-  float* xs = reinterpret_cast<float*>(smem + kWarps * kRing * kStageBytes + 512);  // [kTGP][xstride]
+  int* tok_row = s_abort + 4;                                   // [kMaxTGP]
+  float* tok_scale = reinterpret_cast<float*>(tok_row + kMaxTGP);  // [kMaxTGP]
+  float* xs = reinterpret_cast<float*>(smem + kWarps * kRing * kStageBytes + 256);    // [tgp][kd]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = lane & 7, q = lane >> 3;
   unsigned char* my_ring = ring + warp * kRing * kStageBytes;
   uint64_t* my_bars = bars + warp * kRing;
 
   if (threadIdx.x == 0) *s_abort = 0;
-  if (lane == 0) {
+  if (lane == 0)
     for (int i = 0; i < kRing; ++i) mbar_init(&my_bars[i], 1);
-  }
   fence_mbar_init();
 
   pdl_wait();  // the schedule comes from the route kernel
   pdl_launch_dependents();
 
-  Geo g;
-  g.n_active = a.sched[0];
-  g.qpr = a.I / 4;
-  g.qps = a.Is / 4;
-  g.ops = a.H / 8;
-  g.cu = chunk_cols(a.H);
-  g.cdr = chunk_cols(a.I);
-  g.cds = chunk_cols(a.Is);
+  Ctx c;
+  c.a = &a;
+  c.n_active = a.sched[0];
+  c.up_pref = a.sched + 2 + 2 * a.E + a.T * a.K;
+  c.dn_pref = c.up_pref + (a.E + 2);
+  c.qpr = a.I / 4;
+  c.qps = a.Is / 4;
+  c.ops = a.H / 8;
+  c.cu = chunk_cols(a.H);
+  c.cdr = chunk_cols(a.I);
+  c.cds = chunk_cols(a.Is);
   {
-    const long long Q = static_cast<long long>(g.n_active) * g.qpr + g.qps;
-    const long long O = static_cast<long long>(g.n_active + 1) * g.ops;
-    const long long G = gridDim.x, c = blockIdx.x;
-    g.up_lo = static_cast<int>(Q * c / G);
-    g.up_hi = static_cast<int>(Q * (c + 1) / G);
-    g.dn_lo = static_cast<int>(O * c / G);
-    g.dn_hi = static_cast<int>(O * (c + 1) / G);
+    const long long G = gridDim.x, b = blockIdx.x;
+    const long long U = c.up_pref[c.n_active + 1], D = c.dn_pref[c.n_active + 1];
+    c.lo[0] = static_cast<int>(U * b / G);
+    c.hi[0] = static_cast<int>(U * (b + 1) / G);
+    c.lo[1] = static_cast<int>(D * b / G);
+    c.hi[1] = static_cast<int>(D * (b + 1) / G);
   }
   __syncthreads();  // barrier init visible to all warps
 
   const uint64_t policy = l2_evict_first_policy();
-  Cursor ic;  // issue cursor (meaningful in lane 0)
-  int issued = 0;
-  if (lane == 0) {
-    cursor_begin(ic, a, g, warp);
-    for (int i = 0; i < kRing && ic.phase < 2; ++i) {
-      issue_stage(ic, a, g, my_ring + i * kStageBytes, &my_bars[i], policy);
-      ++issued;
-      cursor_next(ic, a, g, warp);
-    }
+  Cursor k;
+  cursor_begin(k, c, warp);
+  for (int i = 0; i < kRing && k.live; ++i) {
+    issue_stage(k, c, my_ring + i * kStageBytes, &my_bars[i], policy, lane);
+    cursor_next(k, c, warp);
   }
   int consumed = 0;
-  const int xstride_up = a.H;
   bool aborted = false;
 
   for (int phase = 0; phase < 2 && !aborted; ++phase) {
-    int s0, s1;
-    phase_slots(g, phase, s0, s1);
-    for (int s = s0; s < s1 && !aborted; ++s) {
-      const bool routed = s < g.n_active;
-      const int ntok = slot_tokens(a, g, s);
-      const int p0 = routed ? a.sched[1 + a.E + s] : 0;
-      const int32_t* pairs = a.sched + 2 + 2 * a.E + p0;
-      int lo, hi;
-      slot_items(g, phase, s, lo, hi);
-      const int nchunks = slot_chunks(a, g, phase, s);
-      const int cols = phase == 0 ? g.cu : (routed ? g.cdr : g.cds);
-      const int pitch = cols * 2 + 16;
-      const int kd = phase == 0 ? a.H : (routed ? a.I : a.Is);
-      if (phase == 1) {
-        // All SwiGLU rows of this slot must be complete (bounded wait).
+    Pass p;
+    bool ok = first_pass(c, phase, p);
+    int cur_s = -1, cur_units = 0;
+    while (ok && !aborted) {
+      const bool routed = p.s < c.n_active;
+      if (phase == 0 && p.s != cur_s && cur_s >= 0) {
+        // every SwiGLU row of the previous slot's units is stored
+        __syncthreads();
         if (threadIdx.x == 0) {
-          const int target = slot_nq(g, s);
-          if (ld_acquire_gpu(&a.up_done[s]) < target) {
+          __threadfence();
+          atomicAdd(&a.up_done[cur_s], cur_units);
+        }
+        cur_units = 0;
+      }
+      if (phase == 1 && p.s != cur_s) {
+        // all of this slot's SwiGLU units must be complete (bounded wait)
+        if (threadIdx.x == 0) {
+          const int target = ((slot_tokens(c, p.s) + a.tgp - 1) / a.tgp) * units_per_pass(c, 0, p.s);
+          if (ld_acquire_gpu(&a.up_done[p.s]) < target) {
             const uint64_t t0 = global_ns();
-            while (ld_acquire_gpu(&a.up_done[s]) < target) {
+            while (ld_acquire_gpu(&a.up_done[p.s]) < target) {
               if (global_ns() - t0 > kWaitNs) {
                 set_error(a.err, kErrTimeout);
                 *s_abort = 1;
                 break;
               }
-              __nanosleep(256);
+              __nanosleep(128);
             }
           }
         }
@@ -344,109 +438,86 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(ExpertsArgs a) {
           break;
         }
       }
-      for (int tg = 0; tg * kTGP < ntok && !aborted; ++tg) {
-        const int nt = min(kTGP, ntok - tg * kTGP);
-        __syncthreads();  // previous pass finished reading xs
-        // Stage the pass's activations as f32 (rows nt..kTGP-1 zero).
-        {
-          const int per_row = kd >> 3;
-          for (int i = threadIdx.x; i < kTGP * per_row; i += kThreads) {
-            const int t = i / per_row, c8 = (i - t * per_row) * 8;
-            float4 lo4 = make_float4(0.f, 0.f, 0.f, 0.f), hi4 = lo4;
-            if (t < nt) {
-              uint4 v;
-              if (phase == 0) {
-                const int tok = routed ? pairs[tg * kTGP + t] / a.K : tg * kTGP + t;
-                v = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(tok) * a.H + c8);
-              } else if (routed) {
-                v = ld_cg_u4(a.act + static_cast<size_t>(pairs[tg * kTGP + t]) * a.I + c8);
-              } else {
-                v = ld_cg_u4(a.act_sh + static_cast<size_t>(tg * kTGP + t) * a.Is + c8);
-              }
-              lo4 = make_float4(lo_bf16(v.x), hi_bf16(v.x), lo_bf16(v.y), hi_bf16(v.y));
-              hi4 = make_float4(lo_bf16(v.z), hi_bf16(v.z), lo_bf16(v.w), hi_bf16(v.w));
-            }
-            *reinterpret_cast<float4*>(xs + t * kd + c8) = lo4;
-            *reinterpret_cast<float4*>(xs + t * kd + c8 + 4) = hi4;
-          }
-        }
-        __syncthreads();
-        for (int item = lo + warp; item < hi; item += kWarps) {
-          float acc[kTGP][8];
-#pragma unroll
-          for (int t = 0; t < kTGP; ++t)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[t][i] = 0.0f;
-          for (int ch = 0; ch < nchunks; ++ch) {
-            const int slot_i = consumed % kRing;
-            if (!mbar_wait_bounded(&my_bars[slot_i], (consumed / kRing) & 1, kWaitNs)) {
-              if (lane == 0) set_error(a.err, kErrTimeout);
-              *reinterpret_cast<volatile int*>(s_abort) = 1;
-              aborted = true;
-              break;
-            }
-            stage_fma_nt(nt, my_ring + slot_i * kStageBytes, pitch, cols, xs, kd, ch * cols, r, q, acc);
-            ++consumed;
-            __syncwarp();
-            if (lane == 0 && ic.phase < 2) {
-              fence_proxy_async_smem();
-              const int j = issued % kRing;
-              issue_stage(ic, a, g, my_ring + j * kStageBytes, &my_bars[j], policy);
-              ++issued;
-              cursor_next(ic, a, g, warp);
-            }
-          }
-          if (aborted) break;
-          // Epilogue: reference reduction tree, then the bf16 boundaries.
-          float val[kTGP];
-#pragma unroll
-          for (int t = 0; t < kTGP; ++t) val[t] = reduce_partials_strided(acc[t]);
-          if (phase == 0) {
-            const int lq = item - slot_qbase(g, s);
-#pragma unroll
-            for (int t = 0; t < kTGP; ++t) {
-              const uint32_t vb = f32_to_bf16(val[t]);
-              const uint32_t ub = __shfl_down_sync(0xffffffffu, vb, 4);
-              if (lane < 4 && t < nt) {
-                // swiglu_bf16 (src/expert.rs:562-571): bf16(silu) from the table
-                const uint16_t out = f32_to_bf16(bf16_to_f32(a.silu_lut[vb]) * bf16_to_f32(ub));
-                const int row = 4 * lq + lane;
-                if (routed)
-                  a.act[static_cast<size_t>(pairs[tg * kTGP + t]) * a.I + row] = out;
-                else
-                  a.act_sh[static_cast<size_t>(tg * kTGP + t) * a.Is + row] = out;
-              }
-            }
-          } else if (lane < 8) {
-            const int h = 8 * (item - s * g.ops) + lane;
-            for (int t = 0; t < nt; ++t) {
-              const float d = bf16_to_f32(f32_to_bf16(val[t]));
-              if (routed) {
-                // bf16(down * route weight) (src/expert.rs:748-751)
-                const int p = pairs[tg * kTGP + t];
-                a.weighted[static_cast<size_t>(p) * a.H + h] = f32_to_bf16(d * bf16_to_f32(a.pair_score[p]));
-              } else {
-                // bf16(sigmoid * down) (src/expert.rs:1144-1147)
-                const int tok = tg * kTGP + t;
-                a.gated_sh[static_cast<size_t>(tok) * a.H + h] = f32_to_bf16(d * bf16_to_f32(a.sh_sig[tok]));
-              }
-            }
-          }
+      cur_s = p.s;
+      cur_units += p.qb - p.qa;
+      const int ntok = slot_tokens(c, p.s);
+      const int t0 = p.tg * a.tgp;
+      const int nt = min(a.tgp, ntok - t0);
+      const int kd = phase == 0 ? a.H : (routed ? a.I : a.Is);
+      const int32_t* pairs = a.sched + 2 + 2 * a.E + (routed ? a.sched[1 + a.E + p.s] : 0);
+      const int nt_pad = nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 : 8;
+      __syncthreads();  // the previous pass finished reading xs and the token table
+      if (threadIdx.x < nt) {
+        const int t = threadIdx.x;
+        if (routed) {
+          const int pr = pairs[t0 + t];
+          tok_row[t] = pr;
+          tok_scale[t] = bf16_to_f32(a.pair_score[pr]);
+        } else {
+          tok_row[t] = t0 + t;
+          tok_scale[t] = bf16_to_f32(a.sh_sig[t0 + t]);
         }
       }
-      if (phase == 0 && !aborted) {
-        __syncthreads();  // every warp's SwiGLU rows of this slot are stored
-        if (threadIdx.x == 0 && hi > lo) {
-          __threadfence();
-          atomicAdd(&a.up_done[s], hi - lo);
+      {
+        const int per_row = kd >> 3;
+        for (int i = threadIdx.x; i < nt_pad * per_row; i += kThreads) {
+          const int t = i / per_row, c8 = (i - t * per_row) * 8;
+          float4 lo4 = make_float4(0.f, 0.f, 0.f, 0.f), hi4 = lo4;
+          if (t < nt) {
+            uint4 v;
+            if (phase == 0) {
+              const int tok = routed ? pairs[t0 + t] / a.K : t0 + t;
+              v = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(tok) * a.H + c8);
+            } else if (routed) {
+              v = ld_cg_u4(a.act + static_cast<size_t>(pairs[t0 + t]) * a.I + c8);
+            } else {
+              v = ld_cg_u4(a.act_sh + static_cast<size_t>(t0 + t) * a.Is + c8);
+            }
+            lo4 = make_float4(lo_bf16(v.x), hi_bf16(v.x), lo_bf16(v.y), hi_bf16(v.y));
+            hi4 = make_float4(lo_bf16(v.z), hi_bf16(v.z), lo_bf16(v.w), hi_bf16(v.w));
+          }
+          *reinterpret_cast<float4*>(xs + t * kd + c8) = lo4;
+          *reinterpret_cast<float4*>(xs + t * kd + c8 + 4) = hi4;
         }
+      }
+      __syncthreads();
+      bool good;
+      if (nt_pad == 1)
+        good = run_items<1>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
+                               tok_scale);
+      else if (nt_pad == 2)
+        good = run_items<2>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
+                               tok_scale);
+      else if (nt_pad == 4)
+        good = run_items<4>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
+                               tok_scale);
+      else
+        good = run_items<8>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
+                               tok_scale);
+      if (!good) {
+        aborted = true;
+        break;
+      }
+      ok = next_pass(c, p);
+    }
+    if (phase == 0 && !aborted && cur_s >= 0) {
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(&a.up_done[cur_s], cur_units);
       }
     }
   }
   if (aborted && lane == 0) {
-    // Let this warp's copies in flight land before the CTA's shared memory
-    // is released (bounded).
-    for (int k = consumed; k < issued; ++k) mbar_wait_bounded(&my_bars[k % kRing], (k / kRing) & 1, kDrainNs);
+    // Stages this warp issued but did not consume: let them land before the
+    // CTA's shared memory is released (bounded).
+    int issued_end = consumed;
+    for (int i = 0; i < kRing; ++i) {
+      const int kk = consumed + i;
+      if (!mbar_wait_bounded(&my_bars[kk % kRing], (kk / kRing) & 1, kDrainNs)) break;
+      issued_end = kk + 1;
+    }
+    (void)issued_end;
   }
 }
 
@@ -454,9 +525,16 @@ int g_num_sms = 0;
 
 }  // namespace
 
+int experts_tokens_per_pass(const Shape& s) {
+  const int kmax = max(s.H, max(s.I, s.Is));
+  const size_t ring = static_cast<size_t>(kWarps) * kRing * kStageBytes + 256;
+  return ring + static_cast<size_t>(8) * kmax * 4 <= 220 * 1024 ? 8 : 4;
+}
+
 size_t experts_smem_bytes(const Shape& s) {
   const int kmax = max(s.H, max(s.I, s.Is));
-  return static_cast<size_t>(kWarps) * kRing * kStageBytes + 512 + static_cast<size_t>(kTGP) * kmax * 4;
+  return static_cast<size_t>(kWarps) * kRing * kStageBytes + 256 +
+         static_cast<size_t>(experts_tokens_per_pass(s)) * kmax * 4;
 }
 
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
@@ -472,9 +550,9 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
   cudaError_t e = cudaFuncSetAttribute(k_experts, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, x, w.gate_up, w.down, w.sh_gate, w.sh_up, w.sh_down,
-                w.expert_base, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act, sc.act_sh,
-                sc.weighted, sc.gated_sh, sc.up_done, sc.err};
+  ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, experts_tokens_per_pass(s), x, w.gate_up, w.down, w.sh_gate,
+                w.sh_up, w.sh_down, w.expert_base, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
+                sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g_num_sms);
   cfg.blockDim = dim3(kThreads);

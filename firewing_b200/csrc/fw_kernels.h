@@ -60,13 +60,17 @@ struct Scratch {
   int max_T = 0;
 };
 
-// Schedule layout inside Scratch::sched (int32 words):
-//   [0]                  n_active
-//   [1 .. 1+E)           active expert ids, ascending
-//   [1+E .. 2+2E)        pair offsets per active slot (n_active+1 used)
-//   [2+2E .. 2+2E+T*K)   pair ids grouped by expert, tokens ascending
+// Schedule layout inside Scratch::sched (int32 words), written by the route
+// kernel for a forward of T tokens:
+//   [0]                         n_active
+//   [1 .. 1+E)                  active expert ids, ascending (slot order)
+//   [1+E .. 2+2E)               pair offsets per slot (n_active+1 used)
+//   [2+2E .. 2+2E+T*K)          pair ids grouped by slot, tokens ascending
+//   [2+2E+T*K .. +E+2)          expert-kernel up-cost prefix per slot
+//   [.. +E+2)                   expert-kernel down-cost prefix per slot
+// (slot n_active is the shared expert; prefixes have n_active+2 entries)
 inline size_t sched_words(int E, int max_T, int K) {
-  return 2 + 2 * static_cast<size_t>(E) + static_cast<size_t>(max_T) * K;
+  return 2 + 2 * static_cast<size_t>(E) + static_cast<size_t>(max_T) * K + 2 * (static_cast<size_t>(E) + 2);
 }
 
 // Lookup tables built on the host (bf16(silu(g)) and bf16(sigmoid(g)) for
@@ -89,6 +93,8 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
 // The persistent expert kernel (gate_up + SwiGLU and down + scale for every
 // active expert and the shared expert); dynamic shared memory it needs.
 size_t experts_smem_bytes(const Shape& s);
+// Tokens the expert kernel stages per pass (8, or 4 for wide hidden sizes).
+int experts_tokens_per_pass(const Shape& s);
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
                            const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st);
 
