@@ -254,12 +254,13 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &s.weighted, static_cast<size_t>(M) * K * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.gated_sh, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.up_done, static_cast<size_t>(E) + 1, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.ticket, 1, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.err, 1, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->x_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->y_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->idx_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->score_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
-    if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess) {
+    if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess || cudaMemset(s.ticket, 0, sizeof(int)) != cudaSuccess) {
       rc = fail(FW_ECUDA, "status reset failed");
       break;
     }

@@ -154,8 +154,111 @@ __global__ void __launch_bounds__(64) k_rows_dot(RowsDotArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Route (src/decoder_layer.rs:278-307) + permute.  One CTA of 32 warps; warp w
-// routes tokens w, w+32, ...  Then the CTA builds the expert schedule.
+// Router logits for the block: rows = the E router rows plus the shared-expert
+// gate vector as row E; grid = (row groups of kRouterRows, token groups of
+// 8).  A CTA bulk-copies its rows into shared memory -- issued before the
+// grid-dependency wait, since weights do not depend on the previous kernel --
+// and its tokens' contiguous [8][H] activation tile after it.  Warp w owns
+// row w; lane j owns partial j (columns j, j+32, ... in order,
+// src/expert.rs:514-552) for the 8 tokens, reading both operands as bf16
+// from shared memory (conflict-free: a warp reads 64 contiguous bytes).
+constexpr int kRouterRows = 8;    // rows (= warps) per CTA
+constexpr int kRouterTokens = 8;  // tokens per CTA
+
+struct RouterArgs {
+  const uint16_t* w;          // [E][H]
+  const uint16_t* extra_row;  // [H] shared-expert gate vector
+  const float* bias;          // [E] or null
+  const uint16_t* x;          // [T][H]
+  uint16_t* logits;           // [T][E]
+  uint16_t* extra_out;        // [T]
+  int E, H, T;
+  int* err;
+};
+
+// Reference tree over the 32 lanes' partials; result valid in lane 0.
+__device__ __forceinline__ float warp_reduce_ref(float p) {
+  p += __shfl_down_sync(0xffffffffu, p, 16);
+  p += __shfl_down_sync(0xffffffffu, p, 8);
+  p += __shfl_down_sync(0xffffffffu, p, 4);
+  const float q = p + __shfl_down_sync(0xffffffffu, p, 1);  // lanes 0, 2: (0+1), (2+3)
+  return q + __shfl_down_sync(0xffffffffu, q, 2);
+}
+
+__global__ void __launch_bounds__(kRouterRows * 32) k_router(RouterArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* rows = reinterpret_cast<uint16_t*>(smem);                                   // [kRouterRows][H]
+  uint16_t* xt = rows + kRouterRows * a.H;                                              // [kRouterTokens][H]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xt + kRouterTokens * a.H);              // [2]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kRouterRows;
+  const int nrows = min(kRouterRows, a.E + 1 - row0);
+  const int t0 = blockIdx.y * kRouterTokens;
+  const int nt = min(kRouterTokens, a.T - t0);
+  const uint32_t row_bytes = static_cast<uint32_t>(a.H) * 2;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bars[0], row_bytes * nrows);
+    const uint64_t policy = l2_evict_first_policy();
+    for (int r = 0; r < nrows; ++r) {
+      const int row = row0 + r;
+      const uint16_t* src = row < a.E ? a.w + static_cast<size_t>(row) * a.H : a.extra_row;
+      bulk_g2s(rows + r * a.H, src, row_bytes, &bars[0], policy);
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bars[1], row_bytes * nt);
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(xt)),
+        "l"(a.x + static_cast<size_t>(t0) * a.H), "r"(row_bytes * nt), "r"(smem_u32(&bars[1]))
+        : "memory");
+  }
+  __syncthreads();  // barrier initialisation visible to all threads
+  const bool ok = mbar_wait_bounded(&bars[0], 0, 2000000000ull) && mbar_wait_bounded(&bars[1], 0, 2000000000ull);
+  if (!ok) {
+    if (lane == 0) set_error(a.err, kErrTimeout);
+    return;
+  }
+  if (warp >= nrows) return;
+  const uint16_t* wr = rows + warp * a.H + lane;
+  const uint16_t* xr = xt + lane;
+  float acc[kRouterTokens];
+#pragma unroll
+  for (int t = 0; t < kRouterTokens; ++t) acc[t] = 0.0f;
+  const int nb = a.H >> 5;
+#pragma unroll 4
+  for (int b = 0; b < nb; ++b) {
+    const float wv = bf16_to_f32(wr[b * 32]);
+#pragma unroll
+    for (int t = 0; t < kRouterTokens; ++t)
+      if (t < nt) acc[t] = fmaf(wv, bf16_to_f32(xr[t * a.H + b * 32]), acc[t]);
+  }
+  const int row = row0 + warp;
+#pragma unroll
+  for (int t = 0; t < kRouterTokens; ++t) {
+    const float dot = warp_reduce_ref(acc[t]);
+    if (lane == 0 && t < nt) {
+      uint16_t v = f32_to_bf16(dot);
+      if (row < a.E) {
+        // build-defined extension: f32 logit bias, re-rounded to bf16
+        if (a.bias != nullptr) v = f32_to_bf16(bf16_to_f32(v) + a.bias[row]);
+        a.logits[static_cast<size_t>(t0 + t) * a.E + row] = v;
+      } else {
+        a.extra_out[t0 + t] = v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Route (src/decoder_layer.rs:278-307) + permute.  One CTA per token, one
+// thread per expert.  The CTA that finishes last (atomic ticket) builds the
+// expert schedule for the expert kernel.
 struct RouteArgs {
   const uint16_t* logits;  // [T][E]
   int T, E, K;
@@ -170,126 +273,77 @@ struct RouteArgs {
   int32_t* sched;            // schedule words (see fw_kernels.h)
   int* up_done;              // [E+1] expert-kernel slot counters to zero
   int tgp, qpr, qps, ops;    // expert-kernel pass size, quads/octets per slot
+  int* ticket;               // CTA completion counter (zero between calls)
 };
 
-constexpr int kRouteWarps = 32;
-
-// Lane `lane` holds experts lane + 32*i, i < NPER, as total-order keys with
-// the index folded in (higher key = higher logit, then lower index).  The
-// bf16 value is recoverable from the key, so no second array is needed.
+// f32 total-order key with the index folded in (higher logit, then lower
+// index, wins), as src/router.rs:241-247 orders the selection.
 __device__ __forceinline__ float key_value(uint32_t key) {
   const uint32_t k16 = key >> 16;
   const uint32_t bits = (k16 & 0x8000u) ? (k16 & 0x7fffu) : (~k16 & 0xffffu);
   return bf16_to_f32(bits);
 }
 
-template <int NPER>
-__device__ void route_token(const RouteArgs& a, int t, float* ex, int32_t* pidx) {
-  const int lane = threadIdx.x & 31;
-  const int E = a.E, K = a.K;
-  const int nper = E >> 5;
-  const uint16_t* lg = a.logits + static_cast<size_t>(t) * E;
-  uint32_t key[NPER];
-  bool nan = false;
+// Block-wide exclusive scan of two values per thread (blockDim.x <= 1024);
+// wsum holds 64 ints.  Returns exclusive prefixes, totals via *tot_a/b.
+__device__ __forceinline__ void block_scan2(int va, int vb, int& ea, int& eb, int* wsum, int& tot_a, int& tot_b) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int ia = va, ib = vb;
 #pragma unroll
-  for (int i = 0; i < NPER; ++i) {
-    key[i] = 0;
-    if (i < nper) {
-      const int e = lane + 32 * i;
-      const uint32_t b = lg[e];
-      nan |= ((b & 0x7f80u) == 0x7f80u) && ((b & 0x007fu) != 0u);
-      key[i] = (total_key(b) << 16) | static_cast<uint32_t>(0xffff - e);
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ya = __shfl_up_sync(0xffffffffu, ia, o);
+    const int yb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ia += ya;
+      ib += yb;
     }
   }
-  if (__any_sync(0xffffffffu, nan)) {
-    // src/decoder_layer.rs:279-281 rejects NaN logits; flag and emit a
-    // placeholder selection so the rest of the pipeline stays in bounds.
-    if (lane == 0) set_error(a.err, kErrNanLogits);
-    for (int k = lane; k < K; k += 32) {
-      a.idx[static_cast<size_t>(t) * K + k] = k;
-      a.score[static_cast<size_t>(t) * K + k] = 0;
-      if (pidx) pidx[t * K + k] = k;
-      if (a.sorted_slot) a.sorted_slot[static_cast<size_t>(t) * K + k] = k;
-    }
-    if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = 0;
-    return;
+  __syncthreads();
+  if (lane == 31) {
+    wsum[warp] = ia;
+    wsum[32 + warp] = ib;
   }
-  // Top-K: K rounds of a warp-wide max over (total-order key, -index)
-  // (selection order of src/router.rs:241-247).
-  uint32_t taken = 0;
-  int sel_mine = -1;  // lane k keeps the k-th selection
-  for (int k = 0; k < K; ++k) {
-    uint32_t best = 0;
+  __syncthreads();
+  if (warp == 0) {
+    const int sa0 = lane < nw ? wsum[lane] : 0, sb0 = lane < nw ? wsum[32 + lane] : 0;
+    int sa = sa0, sb = sb0;
 #pragma unroll
-    for (int i = 0; i < NPER; ++i)
-      if (i < nper && !((taken >> i) & 1u)) best = max(best, key[i]);
-    const uint32_t wbest = __reduce_max_sync(0xffffffffu, best);
-    const int e = 0xffff - static_cast<int>(wbest & 0xffffu);
-    if ((e & 31) == lane) taken |= 1u << (e >> 5);
-    if (lane == k) sel_mine = e;
-  }
-  // Softmax over all experts with the maximum subtracted
-  // (src/decoder_layer.rs:289-297); exp is correctly rounded (f64 then f32).
-  const int top1 = __shfl_sync(0xffffffffu, sel_mine, 0);
-  const float maximum = bf16_to_f32(lg[top1]);
-#pragma unroll
-  for (int i = 0; i < NPER; ++i)
-    if (i < nper)
-      ex[lane + 32 * i] =
-          static_cast<float>(exp(static_cast<double>(__fsub_rn(key_value(key[i]), maximum))));
-  __syncwarp();
-  if (lane == 0) {
-    float den = -0.0f;  // Rust's f32 Sum: start at -0.0, add in index order
-    for (int e = 0; e < E; ++e) den = __fadd_rn(den, ex[e]);
-    ex[E] = den;
-  }
-  __syncwarp();
-  const float den = ex[E];
-  // p_k = e_k / den; selected_sum in top-k order; score = bf16(p_k / sum).
-  float p_mine = 0.0f;
-  if (lane < K) p_mine = __fdiv_rn(ex[sel_mine], den);
-  float ssum = -0.0f;
-  for (int k = 0; k < K; ++k) ssum = __fadd_rn(ssum, __shfl_sync(0xffffffffu, p_mine, k));
-  if (lane < K) {
-    a.idx[static_cast<size_t>(t) * K + lane] = sel_mine;
-    a.score[static_cast<size_t>(t) * K + lane] = f32_to_bf16(__fdiv_rn(p_mine, ssum));
-    if (pidx) pidx[t * K + lane] = sel_mine;
-  }
-  if (a.sorted_slot != nullptr) {
-    // Slot order by ascending expert id (src/decoder_layer.rs:428-429).
-    int rank = 0;
-    for (int k = 0; k < K; ++k) {
-      const int other = __shfl_sync(0xffffffffu, sel_mine, k);
-      rank += (other < sel_mine) ? 1 : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ya = __shfl_up_sync(0xffffffffu, sa, o);
+      const int yb = __shfl_up_sync(0xffffffffu, sb, o);
+      if (lane >= o) {
+        sa += ya;
+        sb += yb;
+      }
     }
-    if (lane < K) a.sorted_slot[static_cast<size_t>(t) * K + rank] = lane;
+    wsum[lane] = sa - sa0;
+    wsum[32 + lane] = sb - sb0;
+    if (lane == 31) {
+      wsum[64] = sa;
+      wsum[65] = sb;
+    }
   }
-  if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = a.sig_lut[a.sh_logit[t]];
-  __syncwarp();
+  __syncthreads();
+  ea = wsum[warp] + ia - va;
+  eb = wsum[32 + warp] + ib - vb;
+  tot_a = wsum[64];
+  tot_b = wsum[65];
+  __syncthreads();
 }
 
-template <int NPER>
-__global__ void __launch_bounds__(1024) k_route_permute(RouteArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int E = a.E, K = a.K, T = a.T;
-  const int warp = threadIdx.x >> 5;
-  float* ex = reinterpret_cast<float*>(smem_raw) + warp * (E + 4);
-  int32_t* pidx = reinterpret_cast<int32_t*>(smem_raw + sizeof(float) * kRouteWarps * (E + 4));
-  for (int t = warp; t < T; t += kRouteWarps) route_token<NPER>(a, t, ex, a.sched ? pidx : nullptr);
-  if (a.sched == nullptr) return;
-  __syncthreads();
-
-  // ---- permute: expert schedule for the expert kernel ----
-  const int P = T * K;
+// The expert schedule (see fw_kernels.h) from all T*K selections.
+__device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
+  const int E = a.E, K = a.K, T = a.T, P = T * K;
   const int W = (T + 63) >> 6;  // 64-bit token masks per expert
-  unsigned long long* mask = reinterpret_cast<unsigned long long*>(pidx + ((P + 3) & ~3));
+  int32_t* pidx = reinterpret_cast<int32_t*>(smem);
+  unsigned long long* mask = reinterpret_cast<unsigned long long*>(pidx + ((P + 1) & ~1));
   int* cnt = reinterpret_cast<int*>(mask + static_cast<size_t>(E) * W);
   int* poff = cnt + E;
-  int* wsum = poff + E;  // [32] warp totals of flags, [32] of counts
+  int* wsum = poff + E;  // 66 ints
+  for (int p = threadIdx.x; p < P; p += blockDim.x) pidx[p] = __ldcg(a.idx + p);
   for (int i = threadIdx.x; i < E * W; i += blockDim.x) mask[i] = 0ull;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) a.up_done[i] = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     const int e = pidx[p];
@@ -298,120 +352,51 @@ __global__ void __launch_bounds__(1024) k_route_permute(RouteArgs a) {
     atomicOr(&mask[e * W + (t >> 6)], 1ull << (t & 63));
   }
   __syncthreads();
-  // Block-wide exclusive scans over experts (E <= 1024 = blockDim).
-  const int e = threadIdx.x;
-  const int lane = threadIdx.x & 31;
-  const int c = (e < E) ? cnt[e] : 0;
-  const int f = c > 0 ? 1 : 0;
-  int ic = c, iflag = f;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int yc = __shfl_up_sync(0xffffffffu, ic, o);
-    const int yf = __shfl_up_sync(0xffffffffu, iflag, o);
-    if (lane >= o) {
-      ic += yc;
-      iflag += yf;
-    }
-  }
-  if (lane == 31) {
-    wsum[warp] = iflag;
-    wsum[32 + warp] = ic;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int vf = wsum[lane], vc = wsum[32 + lane];
-    int sf = vf, sc = vc;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int yf = __shfl_up_sync(0xffffffffu, sf, o);
-      const int yc = __shfl_up_sync(0xffffffffu, sc, o);
-      if (lane >= o) {
-        sf += yf;
-        sc += yc;
-      }
-    }
-    wsum[lane] = sf - vf;  // exclusive warp prefix
-    wsum[32 + lane] = sc - vc;
-  }
-  __syncthreads();
   int32_t* active = a.sched + 1;
   int32_t* offsets = a.sched + 1 + E;
   int32_t* pairs = a.sched + 2 + 2 * E;
-  if (a.up_done != nullptr)
-    for (int i = threadIdx.x; i <= E; i += blockDim.x) a.up_done[i] = 0;
-  const int my_slot = wsum[warp] + iflag - f;  // this expert's slot (if active)
+  int32_t* up_pref = pairs + P;
+  int32_t* dn_pref = up_pref + E + 2;
+  // thread e owns expert e (blockDim.x >= E)
+  const int e = threadIdx.x;
+  const int c = e < E ? cnt[e] : 0;
+  const int f = c > 0 ? 1 : 0;
+  int slot, off, n_act, n_pairs;
+  block_scan2(f, c, slot, off, wsum, n_act, n_pairs);
   if (e < E) {
-    const int off = wsum[32 + warp] + ic - c;
     poff[e] = off;
     if (f) {
-      active[my_slot] = e;
-      offsets[my_slot] = off;
-    }
-    if (e == E - 1) {
-      a.sched[0] = my_slot + f;
-      offsets[my_slot + f] = off + c;
+      active[slot] = e;
+      offsets[slot] = off;
     }
   }
-  __syncthreads();
+  if (threadIdx.x == 0) {
+    a.sched[0] = n_act;
+    offsets[n_act] = n_pairs;
+  }
   // Cost prefixes for the expert kernel.  A slot of n tokens has
   // ceil(n / tgp) token passes of qpr quads (up) and ops octets (down); a
   // unit of a pass with nt tokens costs 4 + pad(nt) (pad = 1, 2, 4, 8: the
   // tokens the kernel computes), weighing bytes and FMAs.
-  {
-    const int nfull = f ? c / a.tgp : 0, rem = f ? c % a.tgp : 0;
-    const int pad = rem <= 1 ? rem : rem <= 2 ? 2 : rem <= 4 ? 4 : 8;
-    const int pc = nfull * (4 + a.tgp) + (rem ? 4 + pad : 0);  // per-unit-row cost of the slot
-    const int vu = pc * a.qpr, vd = pc * a.ops;
-    int iu = vu, id = vd;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int yu = __shfl_up_sync(0xffffffffu, iu, o);
-      const int yd = __shfl_up_sync(0xffffffffu, id, o);
-      if (lane >= o) {
-        iu += yu;
-        id += yd;
-      }
-    }
-    __syncthreads();  // wsum reuse
-    if (lane == 31) {
-      wsum[warp] = iu;
-      wsum[32 + warp] = id;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      const int su0 = wsum[lane], sd0 = wsum[32 + lane];
-      int su = su0, sd = sd0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int yu = __shfl_up_sync(0xffffffffu, su, o);
-        const int yd = __shfl_up_sync(0xffffffffu, sd, o);
-        if (lane >= o) {
-          su += yu;
-          sd += yd;
-        }
-      }
-      wsum[lane] = su - su0;
-      wsum[32 + lane] = sd - sd0;
-    }
-    __syncthreads();
-    int32_t* up_pref = pairs + P;
-    int32_t* dn_pref = up_pref + E + 2;
-    if (e < E && f) {
-      up_pref[my_slot] = wsum[warp] + iu - vu;
-      dn_pref[my_slot] = wsum[32 + warp] + id - vd;
-    }
-    if (e == E - 1) {
-      const int n_act = my_slot + f;
-      const int sfull = T / a.tgp, srem = T % a.tgp;
-      const int spad = srem <= 1 ? srem : srem <= 2 ? 2 : srem <= 4 ? 4 : 8;
-      const int spc = sfull * (4 + a.tgp) + (srem ? 4 + spad : 0);
-      const int tu = wsum[warp] + iu, td = wsum[32 + warp] + id;
-      up_pref[n_act] = tu;
-      up_pref[n_act + 1] = tu + spc * a.qps;
-      dn_pref[n_act] = td;
-      dn_pref[n_act + 1] = td + spc * a.ops;
-    }
+  const int nfull = f ? c / a.tgp : 0, rem = f ? c % a.tgp : 0;
+  const int pad = rem <= 1 ? rem : rem <= 2 ? 2 : rem <= 4 ? 4 : 8;
+  const int pc = nfull * (4 + a.tgp) + (rem ? 4 + pad : 0);
+  int pu, pd, tu, td;
+  block_scan2(pc * a.qpr, pc * a.ops, pu, pd, wsum, tu, td);
+  if (e < E && f) {
+    up_pref[slot] = pu;
+    dn_pref[slot] = pd;
   }
+  if (threadIdx.x == 0) {
+    const int sfull = T / a.tgp, srem = T % a.tgp;
+    const int spad = srem <= 1 ? srem : srem <= 2 ? 2 : srem <= 4 ? 4 : 8;
+    const int spc = sfull * (4 + a.tgp) + (srem ? 4 + spad : 0);
+    up_pref[n_act] = tu;
+    up_pref[n_act + 1] = tu + spc * a.qps;
+    dn_pref[n_act] = td;
+    dn_pref[n_act + 1] = td + spc * a.ops;
+  }
+  __syncthreads();
   // Stable fill: a pair's rank in its expert's list is the number of earlier
   // tokens that selected the same expert (an expert appears once per token).
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
@@ -423,6 +408,112 @@ __global__ void __launch_bounds__(1024) k_route_permute(RouteArgs a) {
     rank += __popcll(m[t >> 6] & ((1ull << (t & 63)) - 1ull));
     pairs[poff[ex_id] + rank] = p;
   }
+}
+
+__global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int E = a.E, K = a.K;
+  const int t = blockIdx.x;
+  const int e = threadIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  float* ex = reinterpret_cast<float*>(smem);                          // [E + 4]
+  uint32_t* cand = reinterpret_cast<uint32_t*>(ex + E + 4);            // [nw * K]
+  int* sel = reinterpret_cast<int*>(cand + nw * K);                    // [K]
+  int* flag = sel + 32;                                                // [4]
+  pdl_wait();
+  pdl_launch_dependents();
+  uint32_t key = 0;
+  bool nan = false;
+  if (e < E) {
+    const uint32_t b = a.logits[static_cast<size_t>(t) * E + e];
+    nan = ((b & 0x7f80u) == 0x7f80u) && ((b & 0x007fu) != 0u);
+    key = (total_key(b) << 16) | static_cast<uint32_t>(0xffff - e);
+  }
+  if (__syncthreads_or(nan)) {
+    // src/decoder_layer.rs:279-281 rejects NaN logits: flag it and emit a
+    // placeholder selection so the rest of the pipeline stays in bounds.
+    if (threadIdx.x == 0) set_error(a.err, kErrNanLogits);
+    if (threadIdx.x < K) {
+      a.idx[static_cast<size_t>(t) * K + threadIdx.x] = threadIdx.x;
+      a.score[static_cast<size_t>(t) * K + threadIdx.x] = 0;
+      if (a.sorted_slot) a.sorted_slot[static_cast<size_t>(t) * K + threadIdx.x] = threadIdx.x;
+    }
+    if (a.sh_sig != nullptr && threadIdx.x == 0) a.sh_sig[t] = 0;
+  } else {
+    // The shared-expert gate lookup has no dependency on the selection.
+    if (a.sh_sig != nullptr && threadIdx.x == 32) a.sh_sig[t] = a.sig_lut[a.sh_logit[t]];
+    // Top-K per warp (K rounds of a warp max), then warp 0 merges.
+    bool taken = false;
+    for (int k = 0; k < K; ++k) {
+      const uint32_t m = __reduce_max_sync(0xffffffffu, taken ? 0u : key);
+      if (!taken && key == m && m != 0u) taken = true;
+      if (lane == 0) cand[warp * K + k] = m;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int C = nw * K;
+      for (int k = 0; k < K; ++k) {
+        uint32_t best = 0;
+        for (int i = lane; i < C; i += 32) best = max(best, cand[i]);
+        const uint32_t m = __reduce_max_sync(0xffffffffu, best);
+        for (int i = lane; i < C; i += 32)
+          if (cand[i] == m) cand[i] = 0;
+        __syncwarp();
+        if (lane == 0) {
+          sel[k] = 0xffff - static_cast<int>(m & 0xffffu);
+          if (k == 0) ex[E + 1] = key_value(m);  // the largest logit
+        }
+      }
+    }
+    __syncthreads();
+    // Softmax with the maximum subtracted (src/decoder_layer.rs:289-297);
+    // exp is correctly rounded (f64, then f32).
+    const float maximum = ex[E + 1];
+    if (e < E) ex[e] = static_cast<float>(exp(static_cast<double>(__fsub_rn(key_value(key), maximum))));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // Rust's f32 Sum: start at -0.0, add in index order.
+      float den = -0.0f;
+      const float4* ex4 = reinterpret_cast<const float4*>(ex);
+      for (int i = 0; i < (E >> 2); ++i) {
+        const float4 v = ex4[i];
+        den = __fadd_rn(den, v.x);
+        den = __fadd_rn(den, v.y);
+        den = __fadd_rn(den, v.z);
+        den = __fadd_rn(den, v.w);
+      }
+      ex[E] = den;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const float den = ex[E];
+      const int my = lane < K ? sel[lane] : 0;
+      const float pk = lane < K ? __fdiv_rn(ex[my], den) : 0.0f;
+      float ssum = -0.0f;  // selected_sum in top-k order
+      for (int k = 0; k < K; ++k) ssum = __fadd_rn(ssum, __shfl_sync(0xffffffffu, pk, k));
+      int rank = 0;  // slot order by ascending expert id (src/decoder_layer.rs:428-429)
+      for (int k = 0; k < K; ++k) rank += (__shfl_sync(0xffffffffu, my, k) < my) ? 1 : 0;
+      if (lane < K) {
+        a.idx[static_cast<size_t>(t) * K + lane] = my;
+        a.score[static_cast<size_t>(t) * K + lane] = f32_to_bf16(__fdiv_rn(pk, ssum));
+        if (a.sorted_slot != nullptr) a.sorted_slot[static_cast<size_t>(t) * K + rank] = lane;
+      }
+    }
+  }
+  if (a.sched == nullptr) return;
+  // The last CTA to finish builds the schedule from every token's selection.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    flag[0] = (atomicAdd(a.ticket, 1) == a.T - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  const bool last = flag[0] != 0;
+  __syncthreads();  // every thread has read the flag before the schedule reuses smem
+  if (!last) return;
+  __threadfence();
+  build_schedule(a, smem);
+  if (threadIdx.x == 0) *a.ticket = 0;  // ready for the next forward
 }
 
 // ---------------------------------------------------------------------------
@@ -446,15 +537,28 @@ __global__ void k_combine(CombineArgs a) {
   uint32_t acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0;  // bf16(0.0)
-  for (int n = 0; n < a.K; ++n) {
-    const int slot = a.sorted_slot[static_cast<size_t>(t) * a.K + n];
-    const size_t p = static_cast<size_t>(t) * a.K + slot;
-    const uint4 v = *reinterpret_cast<const uint4*>(a.weighted + p * a.H + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const int32_t* ss = a.sorted_slot + static_cast<size_t>(t) * a.K;
+  // Issue the slot loads, then all row loads of a group, before any add, so
+  // the dependent loads cost two memory latencies per 8 experts.
+  for (int n0 = 0; n0 < a.K; n0 += 8) {
+    int sl[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      acc[2 * i] = f32_to_bf16(bf16_to_f32(acc[2 * i]) + lo_bf16(w[i]));
-      acc[2 * i + 1] = f32_to_bf16(bf16_to_f32(acc[2 * i + 1]) + hi_bf16(w[i]));
+    for (int i = 0; i < 8; ++i) sl[i] = n0 + i < a.K ? ss[n0 + i] : 0;
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (n0 + i < a.K)
+        v[i] = *reinterpret_cast<const uint4*>(a.weighted + (static_cast<size_t>(t) * a.K + sl[i]) * a.H + c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (n0 + i < a.K) {
+        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] = f32_to_bf16(bf16_to_f32(acc[2 * j]) + lo_bf16(w[j]));
+          acc[2 * j + 1] = f32_to_bf16(bf16_to_f32(acc[2 * j + 1]) + hi_bf16(w[j]));
+        }
+      }
     }
   }
   const uint4 sv = *reinterpret_cast<const uint4*>(a.gated_sh + static_cast<size_t>(t) * a.H + c);
@@ -542,23 +646,22 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
   return cudaLaunchKernelEx(&cfg, kern, arg);
 }
 
-cudaError_t launch_route_kernel(const RouteArgs& a, size_t smem, cudaStream_t st) {
-  const int nper = a.E / 32;
-  if (nper <= 4) return launch_pdl(k_route_permute<4>, dim3(1), dim3(1024), smem, st, a);
-  if (nper <= 8) return launch_pdl(k_route_permute<8>, dim3(1), dim3(1024), smem, st, a);
-  if (nper <= 16) return launch_pdl(k_route_permute<16>, dim3(1), dim3(1024), smem, st, a);
-  return launch_pdl(k_route_permute<32>, dim3(1), dim3(1024), smem, st, a);
-}
-
-size_t route_smem(int E, int T, int K, bool permute) {
-  size_t b = sizeof(float) * kRouteWarps * (E + 4);
-  if (permute) {
+size_t route_smem(int E, int T, int K, bool schedule) {
+  const int nw = (E + 31) / 32;
+  size_t b = sizeof(float) * (E + 4) + sizeof(uint32_t) * nw * K + sizeof(int) * 36;
+  if (schedule) {
     const int P = T * K;
     const int W = (T + 63) / 64;
-    b += sizeof(int32_t) * ((P + 3) & ~3) + sizeof(unsigned long long) * static_cast<size_t>(E) * W +
-         sizeof(int) * (2 * E + 64);
+    const size_t s = sizeof(int32_t) * ((P + 1) & ~1) + sizeof(unsigned long long) * static_cast<size_t>(E) * W +
+                     sizeof(int) * (2 * E + 66);
+    b = b > s ? b : s;
   }
-  return b;
+  return (b + 15) & ~size_t(15);
+}
+
+cudaError_t launch_route_kernel(const RouteArgs& a, cudaStream_t st) {
+  const int threads = (a.E + 31) / 32 * 32;
+  return launch_pdl(k_route, dim3(a.T), dim3(threads), route_smem(a.E, a.T, a.K, a.sched != nullptr), st, a);
 }
 
 }  // namespace
@@ -573,8 +676,8 @@ cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int co
 cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
                          uint16_t* score, int* err, cudaStream_t st) {
   RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-              0, 0, 0, 0};
-  return launch_route_kernel(a, route_smem(E, T, K, false), st);
+              0, 0, 0, 0, nullptr};
+  return launch_route_kernel(a, st);
 }
 
 cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, long long n,
@@ -601,17 +704,18 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
   if ((e = mark(0)) != cudaSuccess) return e;
   // 1. router logits + shared-gate logit
   {
-    RowsDotArgs a{w.router, s.E, s.H, T, x, sc.logits, w.bias, w.sh_gate_w, sc.sh_logit};
-    const dim3 grid((s.E + 1 + kRowsPerDotCta - 1) / kRowsPerDotCta, (T + kTG - 1) / kTG);
-    e = launch_pdl(k_rows_dot, grid, dim3(64), sizeof(float) * kTG * s.H, st, a);
+    RouterArgs a{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T, sc.err};
+    const size_t smem = static_cast<size_t>(kRouterRows + kRouterTokens) * s.H * 2 + 16;
+    const dim3 grid((s.E + 1 + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
+    e = launch_pdl(k_router, grid, dim3(kRouterRows * 32), smem, st, a);
     if (e != cudaSuccess || (e = mark(1)) != cudaSuccess) return e;
   }
   // 2. route + permute
   {
     RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
                 sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, sc.sched, sc.up_done,
-                experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8};
-    e = launch_route_kernel(a, route_smem(s.E, T, s.K, true), st);
+                experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket};
+    e = launch_route_kernel(a, st);
     if (e != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
   }
   // 3. experts: gate_up + SwiGLU, then down + scale (one persistent kernel)

@@ -56,6 +56,7 @@ struct Scratch {
   uint16_t* weighted = nullptr;  // [T*K][H]
   uint16_t* gated_sh = nullptr;  // [T][H]
   int* up_done = nullptr;        // [E+1] per-slot SwiGLU completion counters
+  int* ticket = nullptr;         // route-kernel completion counter (kept at 0)
   int* err = nullptr;            // device status word
   int max_T = 0;
 };

@@ -129,6 +129,7 @@ size_t carve(const fw::Shape& s, int T, bool need_idx, bool need_score, unsigned
   sc->weighted = reinterpret_cast<uint16_t*>(take(M * K * H * 2));
   sc->gated_sh = reinterpret_cast<uint16_t*>(take(M * H * 2));
   sc->up_done = reinterpret_cast<int*>(take((E + 1) * 4));
+  sc->ticket = reinterpret_cast<int*>(take(sizeof(int)));
   sc->err = reinterpret_cast<int*>(take(sizeof(int)));
   *idx = need_idx ? reinterpret_cast<int32_t*>(take(M * K * 4)) : nullptr;
   *score = need_score ? reinterpret_cast<uint16_t*>(take(M * K * 2)) : nullptr;
@@ -199,9 +200,10 @@ extern "C" int fw_moe_forward_noalloc(const fw_moe_config* config, const fw_moe_
   lw.expert_count = c.experts;
   const fw::Luts luts{st->silu, st->sigmoid};
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  // The status word is the only scratch that must start at zero; every other
-  // scratch byte is written before it is read within the call.
+  // The status word and the route kernel's completion ticket must start at
+  // zero; every other scratch byte is written before it is read in the call.
   if ((e = cudaMemsetAsync(sc.err, 0, sizeof(int), cs)) != cudaSuccess) return cuda_fail("status reset", e);
+  if ((e = cudaMemsetAsync(sc.ticket, 0, sizeof(int), cs)) != cudaSuccess) return cuda_fail("ticket reset", e);
   e = fw::launch_block(s, lw, luts, sc, x, tokens, y, topk_idx ? topk_idx : idx_scratch,
                        topk_scores ? topk_scores : score_scratch, cs);
   if (e != cudaSuccess) return cuda_fail("launch", e);
