@@ -249,8 +249,8 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &s.sh_sig, M, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.sorted_slot, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.sched, fw::sched_words(E, M, K), o)) != FW_OK) break;
-    if ((rc = alloc(h, &s.act, static_cast<size_t>(M) * K * I, o)) != FW_OK) break;
-    if ((rc = alloc(h, &s.act_sh, static_cast<size_t>(M) * Is, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.act, static_cast<size_t>(M) * K * 2 * I, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.act_sh, static_cast<size_t>(M) * 2 * Is, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.weighted, static_cast<size_t>(M) * K * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.gated_sh, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.up_done, static_cast<size_t>(E) + 1, o)) != FW_OK) break;

@@ -190,3 +190,36 @@ __device__ __forceinline__ float reduce_partials_strided(float* p) {
 }
 
 }  // namespace fw
+
+namespace fw {
+
+// acc[i] += w[i] * x[i] for 8 bf16 pairs, with the sm_100 mixed-precision
+// FMA (bf16 operands, f32 accumulator): the bf16 x bf16 product is exact in
+// f32 and the add is rounded once -- the reference's rounded multiply
+// followed by a rounded add, for every product in the normal f32 range.
+__device__ __forceinline__ void fma8_bf16(const uint4 w, const uint4 x, float* acc) {
+  asm("{\n\t"
+      ".reg .b16 w0, w1, w2, w3, w4, w5, w6, w7, x0, x1, x2, x3, x4, x5, x6, x7;\n\t"
+      "mov.b32 {w0, w1}, %8;\n\t"
+      "mov.b32 {w2, w3}, %9;\n\t"
+      "mov.b32 {w4, w5}, %10;\n\t"
+      "mov.b32 {w6, w7}, %11;\n\t"
+      "mov.b32 {x0, x1}, %12;\n\t"
+      "mov.b32 {x2, x3}, %13;\n\t"
+      "mov.b32 {x4, x5}, %14;\n\t"
+      "mov.b32 {x6, x7}, %15;\n\t"
+      "fma.rn.f32.bf16 %0, w0, x0, %0;\n\t"
+      "fma.rn.f32.bf16 %1, w1, x1, %1;\n\t"
+      "fma.rn.f32.bf16 %2, w2, x2, %2;\n\t"
+      "fma.rn.f32.bf16 %3, w3, x3, %3;\n\t"
+      "fma.rn.f32.bf16 %4, w4, x4, %4;\n\t"
+      "fma.rn.f32.bf16 %5, w5, x5, %5;\n\t"
+      "fma.rn.f32.bf16 %6, w6, x6, %6;\n\t"
+      "fma.rn.f32.bf16 %7, w7, x7, %7;\n\t"
+      "}"
+      : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+        "+f"(acc[7])
+      : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
+}
+
+}  // namespace fw

@@ -18,7 +18,9 @@
 // the expected bytes on the stage's mbarrier and lanes 0..7 each issue one
 // row's bulk async copy (cp.async.bulk, never multicast).  Rows are padded
 // by 16 bytes so the 8 lanes of a quarter-warp, which read the same columns
-// of 8 different rows, hit 8 distinct bank groups.
+// of 8 different rows, hit 8 distinct bank groups.  Activations sit in
+// shared memory as bf16 and meet the weights in sm_100 mixed-precision FMAs
+// (bf16 operands, f32 accumulator: fw::fma8_bf16).
 //
 // Exact reduction (src/expert.rs:514-552): lane l owns row r = l & 7 and
 // partials 8q..8q+7, q = l >> 3; it walks the 32-column blocks of its row
@@ -37,12 +39,13 @@
 namespace fw {
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 8;                     // warps per CTA (one ring each)
 constexpr int kThreads = kWarps * 32;
 constexpr int kRing = 2;                          // stages per warp ring
 constexpr int kMaxChunk = 512;                    // columns per stage
 constexpr int kStageBytes = 8 * (kMaxChunk * 2 + 16);  // 8320
 constexpr int kMaxTGP = 8;                        // tokens per pass (upper bound)
+constexpr int kSmemMeta = 512;                    // mbarriers, abort flag, token table
 constexpr uint64_t kWaitNs = 2000000000ull;       // bounded waits: 2 s
 constexpr uint64_t kDrainNs = 200000000ull;       // drain after abort: 0.2 s
 
@@ -59,8 +62,8 @@ struct ExpertsArgs {
   const int32_t* sched;
   const uint16_t* pair_score;  // [T*K]
   const uint16_t* sh_sig;      // [T]
-  uint16_t* act;               // [T*K][I]
-  uint16_t* act_sh;            // [T][Is]
+  uint16_t* act;               // [T*K][2I] gate | up rows (bf16), SwiGLU applied when staged
+  uint16_t* act_sh;            // [T][2Is]
   uint16_t* weighted;          // [T*K][H]
   uint16_t* gated_sh;          // [T][H]
   int* up_done;                // [E+1], zeroed by the route kernel
@@ -232,7 +235,8 @@ __device__ __forceinline__ void cursor_next(Cursor& k, const Ctx& c, int warp) {
   }
 }
 
-// Whole warp: refill `buf` with the stage the cursor names.
+// Whole warp: refill `buf` with the stage the cursor names (lane 0 posts
+// the byte count, lanes 0..7 copy one row each).
 __device__ __forceinline__ void issue_stage(const Cursor& k, const Ctx& c, unsigned char* buf, uint64_t* bar,
                                             uint64_t policy, int lane) {
   const ExpertsArgs& a = *c.a;
@@ -255,21 +259,19 @@ __device__ __forceinline__ void issue_stage(const Cursor& k, const Ctx& c, unsig
 }
 
 // Accumulate one stage: 8 rows x `cols` columns from column col0, NT tokens
-// of f32 activations (row stride xstride) in shared memory.
+// of bf16 activations (row stride xstride elements) in shared memory.
 template <int NT>
-__device__ __forceinline__ void stage_fma(const unsigned char* buf, int pitch, int cols, const float* xs, int xstride,
-                                          int col0, int r, int q, float (&acc)[kMaxTGP][8]) {
+__device__ __forceinline__ void stage_fma(const unsigned char* buf, int pitch, int cols, const uint16_t* xs,
+                                          int xstride, int col0, int r, int q, float (&acc)[kMaxTGP][8]) {
   const uint16_t* wrow = reinterpret_cast<const uint16_t*>(buf + r * pitch) + q * 8;
-  const float* xq = xs + col0 + q * 8;
+  const uint16_t* xq = xs + col0 + q * 8;
   const int nb = cols >> 5;
 #pragma unroll 4
   for (int b = 0; b < nb; ++b) {
     const uint4 w = *reinterpret_cast<const uint4*>(wrow + b * 32);
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const float* xr = xq + t * xstride + b * 32;
-      fma8(w, *reinterpret_cast<const float4*>(xr), *reinterpret_cast<const float4*>(xr + 4), acc[t]);
-    }
+    for (int t = 0; t < NT; ++t)
+      fma8_bf16(w, *reinterpret_cast<const uint4*>(xq + t * xstride + b * 32), acc[t]);
   }
 }
 
@@ -285,19 +287,16 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const Pass& p, int item, 
 #pragma unroll
   for (int t = 0; t < NT; ++t) val[t] = reduce_partials_strided(acc[t]);
   if (p.phase == 0) {
+    // Gate and up rows as bf16 (linear_bf16); SwiGLU is applied when the
+    // down phase stages them.
+    if (lane < 8) {
+      const int row = 4 * item + (lane & 3);
+      const int half = routed ? a.I : a.Is;
+      const int col = lane < 4 ? row : half + row;
+      uint16_t* base = routed ? a.act : a.act_sh;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const uint32_t vb = f32_to_bf16(val[t]);
-      const uint32_t ub = __shfl_down_sync(0xffffffffu, vb, 4);
-      if (lane < 4 && t < nt) {
-        // swiglu_bf16 (src/expert.rs:562-571): bf16(silu) from the table
-        const uint16_t out = f32_to_bf16(bf16_to_f32(a.silu_lut[vb]) * bf16_to_f32(ub));
-        const int row = 4 * item + lane;
-        if (routed)
-          a.act[static_cast<size_t>(tok_row[t]) * a.I + row] = out;
-        else
-          a.act_sh[static_cast<size_t>(tok_row[t]) * a.Is + row] = out;
-      }
+      for (int t = 0; t < NT; ++t)
+        if (t < nt) base[static_cast<size_t>(tok_row[t]) * 2 * half + col] = f32_to_bf16(val[t]);
     }
   } else if (lane < 8) {
     const int h = 8 * item + lane;
@@ -315,7 +314,7 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const Pass& p, int item, 
 }
 
 template <int NT>
-__device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, const float* xs, int xstride,
+__device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, const uint16_t* xs, int xstride,
                                           unsigned char* my_ring, uint64_t* my_bars, Cursor& k, int& consumed,
                                           uint64_t policy, int warp, int lane, int* s_abort, const int* tok_row,
                                           const float* tok_scale) {
@@ -351,17 +350,16 @@ __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, c
 
 __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__ ExpertsArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* ring = smem;                                                       // [warps][kRing][8320]
+  unsigned char* ring = smem;                                                         // [warps][kRing][8320]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kRing * kStageBytes);  // [warps][kRing]
   int* s_abort = reinterpret_cast<int*>(bars + kWarps * kRing);
-  int* tok_row = s_abort + 4;                                   // [kMaxTGP]
+  int* tok_row = s_abort + 4;                                    // [kMaxTGP]
   float* tok_scale = reinterpret_cast<float*>(tok_row + kMaxTGP);  // [kMaxTGP]
-  float* xs = reinterpret_cast<float*>(smem + kWarps * kRing * kStageBytes + 256);    // [tgp][kd]
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem + kWarps * kRing * kStageBytes + kSmemMeta);  // [tgp][kd] bf16
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* my_ring = ring + warp * kRing * kStageBytes;
   uint64_t* my_bars = bars + warp * kRing;
-
   if (threadIdx.x == 0) *s_abort = 0;
   if (lane == 0)
     for (int i = 0; i < kRing; ++i) mbar_init(&my_bars[i], 1);
@@ -408,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
     while (ok && !aborted) {
       const bool routed = p.s < c.n_active;
       if (phase == 0 && p.s != cur_s && cur_s >= 0) {
-        // every SwiGLU row of the previous slot's units is stored
+        // every gate/up row of the previous slot's units is stored
         __syncthreads();
         if (threadIdx.x == 0) {
           __threadfence();
@@ -417,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
         cur_units = 0;
       }
       if (phase == 1 && p.s != cur_s) {
-        // all of this slot's SwiGLU units must be complete (bounded wait)
+        // all of this slot's up units must be complete (bounded wait)
         if (threadIdx.x == 0) {
           const int target = ((slot_tokens(c, p.s) + a.tgp - 1) / a.tgp) * units_per_pass(c, 0, p.s);
           if (ld_acquire_gpu(&a.up_done[p.s]) < target) {
@@ -459,41 +457,56 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
         }
       }
       {
+        // Stage the pass's activations as f32 (rows nt..nt_pad-1 zero).  Up:
+        // the tokens' inputs.  Down: swiglu_bf16 (src/expert.rs:562-571) of
+        // the stored gate/up rows, bf16(bf16(silu(g)) * u), silu from the table.
         const int per_row = kd >> 3;
         for (int i = threadIdx.x; i < nt_pad * per_row; i += kThreads) {
           const int t = i / per_row, c8 = (i - t * per_row) * 8;
-          float4 lo4 = make_float4(0.f, 0.f, 0.f, 0.f), hi4 = lo4;
+          uint4 out = make_uint4(0u, 0u, 0u, 0u);
           if (t < nt) {
-            uint4 v;
             if (phase == 0) {
               const int tok = routed ? pairs[t0 + t] / a.K : t0 + t;
-              v = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(tok) * a.H + c8);
-            } else if (routed) {
-              v = ld_cg_u4(a.act + static_cast<size_t>(pairs[t0 + t]) * a.I + c8);
+              out = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(tok) * a.H + c8);
             } else {
-              v = ld_cg_u4(a.act_sh + static_cast<size_t>(t0 + t) * a.Is + c8);
+              const uint16_t* row = routed ? a.act + static_cast<size_t>(pairs[t0 + t]) * 2 * a.I
+                                           : a.act_sh + static_cast<size_t>(t0 + t) * 2 * a.Is;
+              const uint4 g = ld_cg_u4(row + c8);
+              const uint4 u = ld_cg_u4(row + kd + c8);
+              const uint32_t gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
+              uint16_t sl[8];
+#pragma unroll
+              for (int e2 = 0; e2 < 4; ++e2) {
+                sl[2 * e2] = a.silu_lut[gg[e2] & 0xffffu];
+                sl[2 * e2 + 1] = a.silu_lut[gg[e2] >> 16];
+              }
+              uint32_t o[4];
+#pragma unroll
+              for (int e2 = 0; e2 < 4; ++e2) {
+                const uint32_t lo = f32_to_bf16(bf16_to_f32(sl[2 * e2]) * lo_bf16(uu[e2]));
+                const uint32_t hi = f32_to_bf16(bf16_to_f32(sl[2 * e2 + 1]) * hi_bf16(uu[e2]));
+                o[e2] = lo | (hi << 16);
+              }
+              out = make_uint4(o[0], o[1], o[2], o[3]);
             }
-            lo4 = make_float4(lo_bf16(v.x), hi_bf16(v.x), lo_bf16(v.y), hi_bf16(v.y));
-            hi4 = make_float4(lo_bf16(v.z), hi_bf16(v.z), lo_bf16(v.w), hi_bf16(v.w));
           }
-          *reinterpret_cast<float4*>(xs + t * kd + c8) = lo4;
-          *reinterpret_cast<float4*>(xs + t * kd + c8 + 4) = hi4;
+          *reinterpret_cast<uint4*>(xs + t * kd + c8) = out;
         }
       }
       __syncthreads();
       bool good;
       if (nt_pad == 1)
-        good = run_items<1>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
-                               tok_scale);
+        good = run_items<1>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+                               tok_row, tok_scale);
       else if (nt_pad == 2)
-        good = run_items<2>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
-                               tok_scale);
+        good = run_items<2>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+                               tok_row, tok_scale);
       else if (nt_pad == 4)
-        good = run_items<4>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
-                               tok_scale);
+        good = run_items<4>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+                               tok_row, tok_scale);
       else
-        good = run_items<8>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort, tok_row,
-                               tok_scale);
+        good = run_items<8>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+                               tok_row, tok_scale);
       if (!good) {
         aborted = true;
         break;
@@ -511,13 +524,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
   if (aborted && lane == 0) {
     // Stages this warp issued but did not consume: let them land before the
     // CTA's shared memory is released (bounded).
-    int issued_end = consumed;
     for (int i = 0; i < kRing; ++i) {
       const int kk = consumed + i;
       if (!mbar_wait_bounded(&my_bars[kk % kRing], (kk / kRing) & 1, kDrainNs)) break;
-      issued_end = kk + 1;
     }
-    (void)issued_end;
   }
 }
 
@@ -527,14 +537,14 @@ int g_num_sms = 0;
 
 int experts_tokens_per_pass(const Shape& s) {
   const int kmax = max(s.H, max(s.I, s.Is));
-  const size_t ring = static_cast<size_t>(kWarps) * kRing * kStageBytes + 256;
-  return ring + static_cast<size_t>(8) * kmax * 4 <= 220 * 1024 ? 8 : 4;
+  const size_t ring = static_cast<size_t>(kWarps) * kRing * kStageBytes + kSmemMeta;
+  return ring + static_cast<size_t>(8) * kmax * 2 <= 220 * 1024 ? 8 : 4;
 }
 
 size_t experts_smem_bytes(const Shape& s) {
   const int kmax = max(s.H, max(s.I, s.Is));
-  return static_cast<size_t>(kWarps) * kRing * kStageBytes + 256 +
-         static_cast<size_t>(experts_tokens_per_pass(s)) * kmax * 4;
+  return static_cast<size_t>(kWarps) * kRing * kStageBytes + kSmemMeta +
+         static_cast<size_t>(experts_tokens_per_pass(s)) * kmax * 2;
 }
 
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,

@@ -51,8 +51,8 @@ struct Scratch {
   uint16_t* sh_sig = nullptr;    // [T]
   int32_t* sorted_slot = nullptr;  // [T][K] slots in ascending expert order
   int32_t* sched = nullptr;      // schedule words, see sched_* helpers
-  uint16_t* act = nullptr;       // [T*K][I]
-  uint16_t* act_sh = nullptr;    // [T][Is]
+  uint16_t* act = nullptr;       // [T*K][2I] gate | up rows (SwiGLU applied on staging)
+  uint16_t* act_sh = nullptr;    // [T][2Is]
   uint16_t* weighted = nullptr;  // [T*K][H]
   uint16_t* gated_sh = nullptr;  // [T][H]
   int* up_done = nullptr;        // [E+1] per-slot SwiGLU completion counters

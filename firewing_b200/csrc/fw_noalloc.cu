@@ -124,8 +124,8 @@ size_t carve(const fw::Shape& s, int T, bool need_idx, bool need_score, unsigned
   sc->sh_sig = reinterpret_cast<uint16_t*>(take(M * 2));
   sc->sorted_slot = reinterpret_cast<int32_t*>(take(M * K * 4));
   sc->sched = reinterpret_cast<int32_t*>(take(fw::sched_words(s.E, T, s.K) * 4));
-  sc->act = reinterpret_cast<uint16_t*>(take(M * K * I * 2));
-  sc->act_sh = reinterpret_cast<uint16_t*>(take(M * Is * 2));
+  sc->act = reinterpret_cast<uint16_t*>(take(M * K * 2 * I * 2));
+  sc->act_sh = reinterpret_cast<uint16_t*>(take(M * 2 * Is * 2));
   sc->weighted = reinterpret_cast<uint16_t*>(take(M * K * H * 2));
   sc->gated_sh = reinterpret_cast<uint16_t*>(take(M * H * 2));
   sc->up_done = reinterpret_cast<int*>(take((E + 1) * 4));
