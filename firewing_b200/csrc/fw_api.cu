@@ -2,6 +2,7 @@
 //
 // Host-side runtime around the kernels: handle lifetime, device weight
 // ownership, scratch sizing, the bf16 SiLU/sigmoid tables, status mapping.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -303,14 +304,13 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
   free_layer(L);
   const size_t H = h->cfg.hidden, I = h->cfg.intermediate, Is = h->cfg.shared_intermediate;
   const size_t E = h->cfg.experts;
+  // Router and shared gate vector keep the reference layout.
   struct Item {
     const void* src;
     size_t count;
     const uint16_t** dst;
   } items[] = {
-      {router, E * H, &L.w.router},          {gate_up, E * 2 * I * H, &L.w.gate_up},
-      {down, E * H * I, &L.w.down},          {shared_gate, Is * H, &L.w.sh_gate},
-      {shared_up, Is * H, &L.w.sh_up},       {shared_down, H * Is, &L.w.sh_down},
+      {router, E * H, &L.w.router},
       {shared_gate_w, H, &L.w.sh_gate_w},
   };
   for (auto& it : items) {
@@ -323,10 +323,61 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
     const cudaError_t e = cudaMemcpy(d, it.src, it.count * 2, cudaMemcpyDefault);
     if (e != cudaSuccess) {
       free_layer(L);
-      return fail(FW_ECUDA, std::string("weight copy: ") + cudaGetErrorString(e));
+      return fail(FW_ECUDA, "weight copy", cudaGetErrorString(e));
     }
     *it.dst = d;
   }
+  // Expert banks and the shared expert go to the tiled layout through a
+  // bounded temporary buffer, a few experts at a time.
+  struct Tiled {
+    fw::TiledSpec spec;
+    long long n_mats;
+    const uint16_t* src0;
+    const uint16_t* src1;
+    const uint16_t** dst;
+  } tiled[] = {
+      {{0, static_cast<int>(H), static_cast<int>(I), static_cast<long long>(2 * I * H),
+        static_cast<long long>(2 * I * H)},
+       static_cast<long long>(E), gate_up, nullptr, &L.w.gate_up},
+      {{1, static_cast<int>(I), 0, static_cast<long long>(H * I), static_cast<long long>(H * I)},
+       static_cast<long long>(E), down, nullptr, &L.w.down},
+      {{0, static_cast<int>(H), 0, static_cast<long long>(2 * Is * H), static_cast<long long>(Is * H)}, 1,
+       shared_gate, shared_up, &L.w.sh_gate},
+      {{1, static_cast<int>(Is), 0, static_cast<long long>(H * Is), static_cast<long long>(H * Is)}, 1,
+       shared_down, nullptr, &L.w.sh_down},
+  };
+  for (auto& t : tiled) {
+    uint16_t* d = nullptr;
+    int rc = alloc(h, &d, static_cast<size_t>(t.n_mats * t.spec.mat_elems), L.owned);
+    if (rc != FW_OK) {
+      free_layer(L);
+      return rc;
+    }
+    const size_t src_elems = static_cast<size_t>(t.spec.src_mat_elems);
+    const size_t per_chunk = std::max<size_t>(1, (size_t(256) << 20) / (src_elems * 2 * (t.src1 ? 2 : 1)));
+    const size_t chunk = std::min<size_t>(per_chunk, static_cast<size_t>(t.n_mats));
+    uint16_t* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, chunk * src_elems * 2 * (t.src1 ? 2 : 1));
+    for (size_t m0 = 0; e == cudaSuccess && m0 < static_cast<size_t>(t.n_mats); m0 += chunk) {
+      const size_t n = std::min(chunk, static_cast<size_t>(t.n_mats) - m0);
+      e = cudaMemcpy(tmp, t.src0 + m0 * src_elems, n * src_elems * 2, cudaMemcpyDefault);
+      if (e == cudaSuccess && t.src1)
+        e = cudaMemcpy(tmp + n * src_elems, t.src1 + m0 * src_elems, n * src_elems * 2, cudaMemcpyDefault);
+      if (e == cudaSuccess)
+        e = fw::launch_relayout(t.spec, static_cast<long long>(m0), static_cast<long long>(n), tmp,
+                                t.src1 ? tmp + n * src_elems : nullptr, d, h->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+    }
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+      free_layer(L);
+      return fail(e == cudaErrorMemoryAllocation ? FW_ENOMEM : FW_ECUDA, "expert re-layout",
+                  cudaGetErrorString(e));
+    }
+    *t.dst = d;
+  }
+  L.w.sh_up = L.w.sh_gate;  // tiled: the gate/up tiles hold both
+  L.w.tiled = true;
   if (logit_bias != nullptr) {
     float* d = nullptr;
     const int rc = alloc(h, &d, E, L.owned);
@@ -356,13 +407,13 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
   const size_t H = h->cfg.hidden, I = h->cfg.intermediate, Is = h->cfg.shared_intermediate;
   const size_t E = h->cfg.experts;
   const float scale = synth_scale(std_dev);
+  // Router and shared gate vector: reference layout.
   struct Item {
     uint32_t id;
     size_t count;
     const uint16_t** dst;
   } items[] = {
-      {0, E * H, &L.w.router},  {1, E * 2 * I * H, &L.w.gate_up}, {2, E * H * I, &L.w.down},
-      {3, Is * H, &L.w.sh_gate}, {4, Is * H, &L.w.sh_up},          {5, H * Is, &L.w.sh_down},
+      {0, E * H, &L.w.router},
       {6, H, &L.w.sh_gate_w},
   };
   for (auto& it : items) {
@@ -375,10 +426,45 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
     const cudaError_t e = fw::launch_synth(synth_key(seed, it.id), it.id, 0, it.count, scale, d, h->stream);
     if (e != cudaSuccess) {
       free_layer(L);
-      return fail(FW_ECUDA, std::string("synth launch: ") + cudaGetErrorString(e));
+      return fail(FW_ECUDA, "synth launch", cudaGetErrorString(e));
     }
     *it.dst = d;
   }
+  // Expert banks and the shared expert: generated straight into the tiled
+  // layout (element values are those of their reference indices).
+  struct Tiled {
+    fw::TiledSpec spec;
+    long long n_mats;
+    uint32_t id0, id1;
+    const uint16_t** dst;
+  } tiled[] = {
+      {{0, static_cast<int>(H), static_cast<int>(I), static_cast<long long>(2 * I * H),
+        static_cast<long long>(2 * I * H)},
+       static_cast<long long>(E), 1, 1, &L.w.gate_up},
+      {{1, static_cast<int>(I), 0, static_cast<long long>(H * I), static_cast<long long>(H * I)},
+       static_cast<long long>(E), 2, 2, &L.w.down},
+      {{0, static_cast<int>(H), 0, static_cast<long long>(2 * Is * H), static_cast<long long>(Is * H)}, 1, 3, 4,
+       &L.w.sh_gate},
+      {{1, static_cast<int>(Is), 0, static_cast<long long>(H * Is), static_cast<long long>(H * Is)}, 1, 5, 5,
+       &L.w.sh_down},
+  };
+  for (auto& t : tiled) {
+    uint16_t* d = nullptr;
+    const int rc = alloc(h, &d, static_cast<size_t>(t.n_mats * t.spec.mat_elems), L.owned);
+    if (rc != FW_OK) {
+      free_layer(L);
+      return rc;
+    }
+    const cudaError_t e = fw::launch_synth_tiled(t.spec, t.n_mats, synth_key(seed, t.id0), synth_key(seed, t.id1),
+                                                 scale, d, h->stream);
+    if (e != cudaSuccess) {
+      free_layer(L);
+      return fail(FW_ECUDA, "synth launch", cudaGetErrorString(e));
+    }
+    *t.dst = d;
+  }
+  L.w.sh_up = L.w.sh_gate;
+  L.w.tiled = true;
   if (zipf_bias) {
     std::vector<float> bias(E);
     for (size_t e = 0; e < E; ++e)

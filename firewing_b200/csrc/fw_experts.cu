@@ -70,12 +70,6 @@ struct ExpertsArgs {
   int* err;
 };
 
-__device__ __forceinline__ int chunk_cols(int k) {
-  for (int c = kMaxChunk; c >= 32; c -= 32)
-    if (k % c == 0) return c;
-  return 32;
-}
-
 // Per-launch constants, identical in every thread of a CTA.
 struct Ctx {
   const ExpertsArgs* a;
@@ -190,7 +184,7 @@ __device__ void cursor_slot(Cursor& k, const Ctx& c) {
       k.row0 = a.gate_up + static_cast<size_t>(a.sched[1 + s] - a.expert_base) * 2 * a.I * a.H;
       k.row1 = k.row0 + static_cast<size_t>(a.I) * a.H;
     } else {
-      k.row0 = a.sh_gate;
+      k.row0 = a.sh_gate;  // tiled: the shared gate/up tiles
       k.row1 = a.sh_up;
     }
   } else {
@@ -235,14 +229,25 @@ __device__ __forceinline__ void cursor_next(Cursor& k, const Ctx& c, int warp) {
   }
 }
 
-// Whole warp: refill `buf` with the stage the cursor names (lane 0 posts
-// the byte count, lanes 0..7 copy one row each).
+// Whole warp: refill `buf` with the stage the cursor names.  Reference
+// layout: lane 0 posts the byte count, lanes 0..7 copy one padded row each.
+// Tiled layout: the stage is one contiguous tile, a single copy.
+template <bool kTiled>
 __device__ __forceinline__ void issue_stage(const Cursor& k, const Ctx& c, unsigned char* buf, uint64_t* bar,
                                             uint64_t policy, int lane) {
   const ExpertsArgs& a = *c.a;
+  fence_proxy_async_smem();
+  if (kTiled) {
+    if (lane == 0) {
+      const uint32_t bytes = 8u * k.cols * 2;
+      mbar_arrive_expect_tx(bar, bytes);
+      const size_t tile = static_cast<size_t>(k.item) * k.nchunks + k.chunk;
+      bulk_g2s(buf, k.row0 + tile * 8 * k.cols, bytes, bar, policy);
+    }
+    return;
+  }
   const int pitch = k.cols * 2 + 16;
   const uint32_t bytes = k.cols * 2;
-  fence_proxy_async_smem();
   if (lane == 0) mbar_arrive_expect_tx(bar, 8 * bytes);
   __syncwarp();
   if (lane < 8) {
@@ -260,15 +265,18 @@ __device__ __forceinline__ void issue_stage(const Cursor& k, const Ctx& c, unsig
 
 // Accumulate one stage: 8 rows x `cols` columns from column col0, NT tokens
 // of bf16 activations (row stride xstride elements) in shared memory.
-template <int NT>
-__device__ __forceinline__ void stage_fma(const unsigned char* buf, int pitch, int cols, const uint16_t* xs,
-                                          int xstride, int col0, int r, int q, float (&acc)[kMaxTGP][8]) {
-  const uint16_t* wrow = reinterpret_cast<const uint16_t*>(buf + r * pitch) + q * 8;
+// Reference layout: rows padded to cols*2+16 bytes.  Tiled layout: rows of
+// cols*2 bytes, 16-byte chunk c of row r at chunk c ^ r.
+template <int NT, bool kTiled>
+__device__ __forceinline__ void stage_fma(const unsigned char* buf, int cols, const uint16_t* xs, int xstride,
+                                          int col0, int r, int q, float (&acc)[kMaxTGP][8]) {
+  const unsigned char* wrow = buf + r * (kTiled ? cols * 2 : cols * 2 + 16);
   const uint16_t* xq = xs + col0 + q * 8;
   const int nb = cols >> 5;
 #pragma unroll 4
   for (int b = 0; b < nb; ++b) {
-    const uint4 w = *reinterpret_cast<const uint4*>(wrow + b * 32);
+    const int chunk = kTiled ? ((4 * b + q) ^ r) : (4 * b + q);
+    const uint4 w = *reinterpret_cast<const uint4*>(wrow + chunk * 16);
 #pragma unroll
     for (int t = 0; t < NT; ++t)
       fma8_bf16(w, *reinterpret_cast<const uint4*>(xq + t * xstride + b * 32), acc[t]);
@@ -313,7 +321,7 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const Pass& p, int item, 
   }
 }
 
-template <int NT>
+template <int NT, bool kTiled>
 __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, const uint16_t* xs, int xstride,
                                           unsigned char* my_ring, uint64_t* my_bars, Cursor& k, int& consumed,
                                           uint64_t policy, int warp, int lane, int* s_abort, const int* tok_row,
@@ -321,7 +329,6 @@ __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, c
   const int r = lane & 7, q = lane >> 3;
   const int nch = n_chunks(c, p.phase, p.s);
   const int cols = chunk_width(c, p.phase, p.s);
-  const int pitch = cols * 2 + 16;
   for (int item = p.qa + warp; item < p.qb; item += kWarps) {
     float acc[kMaxTGP][8];
 #pragma unroll
@@ -335,11 +342,11 @@ __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, c
         *reinterpret_cast<volatile int*>(s_abort) = 1;
         return false;
       }
-      stage_fma<NT>(my_ring + j * kStageBytes, pitch, cols, xs, xstride, ch * cols, r, q, acc);
+      stage_fma<NT, kTiled>(my_ring + j * kStageBytes, cols, xs, xstride, ch * cols, r, q, acc);
       ++consumed;
       __syncwarp();
       if (k.live) {
-        issue_stage(k, c, my_ring + j * kStageBytes, &my_bars[j], policy, lane);
+        issue_stage<kTiled>(k, c, my_ring + j * kStageBytes, &my_bars[j], policy, lane);
         cursor_next(k, c, warp);
       }
     }
@@ -348,6 +355,7 @@ __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, c
   return true;
 }
 
+template <bool kTiled>
 __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__ ExpertsArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* ring = smem;                                                         // [warps][kRing][8320]
@@ -393,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
   Cursor k;
   cursor_begin(k, c, warp);
   for (int i = 0; i < kRing && k.live; ++i) {
-    issue_stage(k, c, my_ring + i * kStageBytes, &my_bars[i], policy, lane);
+    issue_stage<kTiled>(k, c, my_ring + i * kStageBytes, &my_bars[i], policy, lane);
     cursor_next(k, c, warp);
   }
   int consumed = 0;
@@ -496,16 +504,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
       __syncthreads();
       bool good;
       if (nt_pad == 1)
-        good = run_items<1>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<1, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       else if (nt_pad == 2)
-        good = run_items<2>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<2, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       else if (nt_pad == 4)
-        good = run_items<4>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<4, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       else
-        good = run_items<8>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<8, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       if (!good) {
         aborted = true;
@@ -557,8 +565,8 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
     if (e != cudaSuccess) return e;
   }
   const size_t smem = experts_smem_bytes(s);
-  cudaError_t e = cudaFuncSetAttribute(k_experts, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  auto kern = w.tiled ? k_experts<true> : k_experts<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, experts_tokens_per_pass(s), x, w.gate_up, w.down, w.sh_gate,
                 w.sh_up, w.sh_down, w.expert_base, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
@@ -575,7 +583,7 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, k_experts, a);
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace fw

@@ -42,6 +42,33 @@ struct LayerWeights {
   const float* bias = nullptr;
   int expert_base = 0;   // first expert id held (expert parallelism)
   int expert_count = 0;  // experts held
+  // Expert banks in the tiled layout (see TiledSpec) instead of the
+  // reference layout; sh_gate then holds the shared gate/up tiles and sh_up
+  // is unused.
+  bool tiled = false;
+};
+
+// Columns per expert-kernel stage for a matrix of k columns: the largest
+// multiple of 32 that divides k, at most 512.
+__host__ __device__ inline int chunk_cols(int k) {
+  for (int c = 512; c >= 32; c -= 32)
+    if (k % c == 0) return c;
+  return 32;
+}
+
+// Tiled expert layout.  A matrix of R x K (reference, row-major) is stored
+// as tiles of 8 rows x cw columns (cw = chunk_cols(K)), tile-contiguous,
+// ordered row-group-major then column chunk.  Inside a tile, row r holds its
+// cw columns with 16-byte chunk c stored at chunk position c ^ r.  Paired
+// tiles (kind 0) hold the 4 gate rows 4g..4g+3 then the 4 matching up rows
+// of a gate_up bank; plain tiles (kind 1) hold rows 8g..8g+7.  One tile is
+// one expert-kernel stage: a single bulk copy, read conflict-free.
+struct TiledSpec {
+  int kind;                // 0: paired gate/up rows, 1: plain rows
+  int K;                   // columns
+  int half;                // kind 0, one source: up rows start at row `half` of it; 0: two sources
+  long long mat_elems;     // elements per matrix (expert) in the tiled buffer
+  long long src_mat_elems; // elements per matrix in the reference source
 };
 
 // Scratch for one forward of up to max_T tokens (device memory).
@@ -110,6 +137,16 @@ cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, long long n,
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.
 int record_error(int code, const char* msg);
+
+// Seeded synthetic weights written straight into the tiled layout: element
+// d takes the generator value of its reference index under stream
+// keys[source] (the same bits fw_moe_synth_layer gives in reference layout).
+cudaError_t launch_synth_tiled(const TiledSpec& spec, long long n_mats, uint64_t key0, uint64_t key1, float scale,
+                               uint16_t* out, cudaStream_t st);
+// Reference-layout matrices [m0, m0 + n) (src0 / src1 hold exactly those
+// matrices) into the tiled buffer out (whole tensor).
+cudaError_t launch_relayout(const TiledSpec& spec, long long m0, long long n, const uint16_t* src0,
+                            const uint16_t* src1, uint16_t* out, cudaStream_t st);
 
 // Seeded synthetic bf16 tensor (identical bits to the CPU generator);
 // key = SplitMix64 stream key of (seed, tensor id).
