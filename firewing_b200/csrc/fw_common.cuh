@@ -155,6 +155,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Bulk prefetch of global memory into L2 (no shared-memory destination).
+// src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Order this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (bulk copy) writes to the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -375,14 +375,17 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
     offsets[n_act] = n_pairs;
   }
   // Cost prefixes for the expert kernel.  A slot of n tokens has
-  // ceil(n / tgp) token passes of qpr quads (up) and ops octets (down); a
-  // unit of a pass with nt tokens costs 4 + pad(nt) (pad = 1, 2, 4, 8: the
-  // tokens the kernel computes), weighing bytes and FMAs.
+  // ceil(n / tgp) token passes of qpr quads (up) and ops octets (down).  A
+  // unit of a pass with nt tokens costs 4 + pad(nt) in the up phase and
+  // 4 + 4 pad(nt) in the down phase (pad = 1, 2, 4, 8: the tokens the
+  // kernel computes): both weigh the unit's bytes against its FMAs and
+  // reductions, which a down unit (one stage) pays per stage.
   const int nfull = f ? c / a.tgp : 0, rem = f ? c % a.tgp : 0;
   const int pad = rem <= 1 ? rem : rem <= 2 ? 2 : rem <= 4 ? 4 : 8;
-  const int pc = nfull * (4 + a.tgp) + (rem ? 4 + pad : 0);
+  const int pcu = nfull * (4 + a.tgp) + (rem ? 4 + pad : 0);
+  const int pcd = nfull * (4 + 4 * a.tgp) + (rem ? 4 + 4 * pad : 0);
   int pu, pd, tu, td;
-  block_scan2(pc * a.qpr, pc * a.ops, pu, pd, wsum, tu, td);
+  block_scan2(pcu * a.qpr, pcd * a.ops, pu, pd, wsum, tu, td);
   if (e < E && f) {
     up_pref[slot] = pu;
     dn_pref[slot] = pd;
@@ -390,11 +393,12 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
   if (threadIdx.x == 0) {
     const int sfull = T / a.tgp, srem = T % a.tgp;
     const int spad = srem <= 1 ? srem : srem <= 2 ? 2 : srem <= 4 ? 4 : 8;
-    const int spc = sfull * (4 + a.tgp) + (srem ? 4 + spad : 0);
+    const int spcu = sfull * (4 + a.tgp) + (srem ? 4 + spad : 0);
+    const int spcd = sfull * (4 + 4 * a.tgp) + (srem ? 4 + 4 * spad : 0);
     up_pref[n_act] = tu;
-    up_pref[n_act + 1] = tu + spc * a.qps;
+    up_pref[n_act + 1] = tu + spcu * a.qps;
     dn_pref[n_act] = td;
-    dn_pref[n_act + 1] = td + spc * a.ops;
+    dn_pref[n_act + 1] = td + spcd * a.ops;
   }
   __syncthreads();
   // Stable fill: a pair's rank in its expert's list is the number of earlier

@@ -41,9 +41,13 @@ namespace {
 
 constexpr int kWarps = 8;                     // warps per CTA (one ring each)
 constexpr int kThreads = kWarps * 32;
-constexpr int kRing = 2;                          // stages per warp ring
+// Ring per warp: 2 stages; tiled stages are exactly 8 KB, padded
+// reference-layout stages 8 rows of 1040 bytes.
+template <bool kTiled> struct RingCfg {
+  static constexpr int kRing = 2;                                     // stages per warp ring
+  static constexpr int kStageBytes = kTiled ? 8192 : 8 * (512 * 2 + 16);  // 8192 / 8320
+};
 constexpr int kMaxChunk = 512;                    // columns per stage
-constexpr int kStageBytes = 8 * (kMaxChunk * 2 + 16);  // 8320
 constexpr int kMaxTGP = 8;                        // tokens per pass (upper bound)
 constexpr int kSmemMeta = 512;                    // mbarriers, abort flag, token table
 constexpr uint64_t kWaitNs = 2000000000ull;       // bounded waits: 2 s
@@ -74,8 +78,10 @@ struct ExpertsArgs {
 struct Ctx {
   const ExpertsArgs* a;
   int n_active;
-  const int32_t* up_pref;  // [n_active + 2] unit prefix per slot
+  const int32_t* up_pref;  // [n_active + 2] cost prefix per slot (shared memory)
   const int32_t* dn_pref;
+  const int32_t* offs;     // [n_active + 1] pair offsets per slot (shared memory)
+  const int32_t* act_ids;  // [n_active] expert id per slot (shared memory)
   int lo[2], hi[2];        // this CTA's unit range per phase
   int qpr, qps, ops;       // quads per routed / shared slot, octets per slot
   int cu, cdr, cds;        // chunk columns: up, down routed, down shared
@@ -95,17 +101,20 @@ __device__ __forceinline__ int chunk_width(const Ctx& c, int phase, int s) {
 
 // A pass = (phase, slot, token pass) restricted to this CTA: items qa..qb-1
 // (local quad / octet indices of the slot).  CTAs split each phase's COST
-// space, where a unit of a pass with nt tokens costs 4 + pad(nt) (the route
-// kernel's prefix); a unit belongs to the CTA whose range holds its start.
+// space, where a unit of a pass with nt tokens costs unit_cost(phase, nt)
+// (the route kernel's prefix); a unit belongs to the CTA whose range holds
+// its start.
 struct Pass {
   int phase, s, tg, qa, qb;
 };
 
 __device__ __forceinline__ int pad_tokens(int nt) { return nt <= 1 ? nt : nt <= 2 ? 2 : nt <= 4 ? 4 : 8; }
+// Cost of one unit of a pass with nt tokens (must match the route kernel).
+__device__ __forceinline__ int unit_cost(int phase, int nt) { return 4 + (phase ? 4 : 1) * pad_tokens(nt); }
 
 __device__ __forceinline__ int slot_tokens(const Ctx& c, int s) {
   const ExpertsArgs& a = *c.a;
-  return s < c.n_active ? a.sched[1 + a.E + s + 1] - a.sched[1 + a.E + s] : a.T;
+  return s < c.n_active ? c.offs[s + 1] - c.offs[s] : a.T;
 }
 
 // Slot whose cost range contains u (binary search over the prefix).
@@ -131,10 +140,10 @@ __device__ bool settle_pass(const Ctx& c, int phase, int s, int tg, Pass& p) {
     const int ntg = (ntok + tgp - 1) / tgp;
     const int n = units_per_pass(c, phase, s);
     for (; tg < ntg; ++tg) {
-      const int base = pr[s] + tg * n * (4 + tgp);
+      const int base = pr[s] + tg * n * unit_cost(phase, tgp);
       if (base >= hi) return false;
       const int nt = min(tgp, ntok - tg * tgp);
-      const int u = 4 + pad_tokens(nt);
+      const int u = unit_cost(phase, nt);
       const int i0 = ceil_div_pos(lo - base, u);
       const int i1 = min(n, ceil_div_pos(hi - base, u));
       if (i0 < i1) {
@@ -154,7 +163,7 @@ __device__ bool first_pass(const Ctx& c, int phase, Pass& p) {
   const int32_t* pr = pref(c, phase);
   const int s = slot_of(pr, c.n_active + 1, lo);
   const int n = units_per_pass(c, phase, s);
-  const int tg = (lo - pr[s]) / (n * (4 + c.a->tgp));
+  const int tg = (lo - pr[s]) / (n * unit_cost(phase, c.a->tgp));
   return settle_pass(c, phase, s, tg, p);
 }
 
@@ -181,14 +190,14 @@ __device__ void cursor_slot(Cursor& k, const Ctx& c) {
   k.cols = chunk_width(c, k.p.phase, s);
   if (k.p.phase == 0) {
     if (s < c.n_active) {
-      k.row0 = a.gate_up + static_cast<size_t>(a.sched[1 + s] - a.expert_base) * 2 * a.I * a.H;
+      k.row0 = a.gate_up + static_cast<size_t>(c.act_ids[s] - a.expert_base) * 2 * a.I * a.H;
       k.row1 = k.row0 + static_cast<size_t>(a.I) * a.H;
     } else {
       k.row0 = a.sh_gate;  // tiled: the shared gate/up tiles
       k.row1 = a.sh_up;
     }
   } else {
-    k.row0 = s < c.n_active ? a.down + static_cast<size_t>(a.sched[1 + s] - a.expert_base) * a.H * a.I
+    k.row0 = s < c.n_active ? a.down + static_cast<size_t>(c.act_ids[s] - a.expert_base) * a.H * a.I
                             : a.sh_down;
     k.row1 = nullptr;
   }
@@ -326,6 +335,7 @@ __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, c
                                           unsigned char* my_ring, uint64_t* my_bars, Cursor& k, int& consumed,
                                           uint64_t policy, int warp, int lane, int* s_abort, const int* tok_row,
                                           const float* tok_scale) {
+  constexpr int kRing = RingCfg<kTiled>::kRing, kStageBytes = RingCfg<kTiled>::kStageBytes;
   const int r = lane & 7, q = lane >> 3;
   const int nch = n_chunks(c, p.phase, p.s);
   const int cols = chunk_width(c, p.phase, p.s);
@@ -357,8 +367,9 @@ __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, c
 
 template <bool kTiled>
 __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__ ExpertsArgs a) {
+  constexpr int kRing = RingCfg<kTiled>::kRing, kStageBytes = RingCfg<kTiled>::kStageBytes;
   extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* ring = smem;                                                         // [warps][kRing][8320]
+  unsigned char* ring = smem;                                                         // [warps][kRing][stage]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kRing * kStageBytes);  // [warps][kRing]
   int* s_abort = reinterpret_cast<int*>(bars + kWarps * kRing);
   int* tok_row = s_abort + 4;                                    // [kMaxTGP]
@@ -379,8 +390,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
   Ctx c;
   c.a = &a;
   c.n_active = a.sched[0];
-  c.up_pref = a.sched + 2 + 2 * a.E + a.T * a.K;
-  c.dn_pref = c.up_pref + (a.E + 2);
+  {
+    // The schedule's slot tables, once, into shared memory: every cursor step
+    // and pass boundary reads them.
+    int32_t* t = reinterpret_cast<int32_t*>(xs + static_cast<size_t>(a.tgp) * max(a.H, max(a.I, a.Is)));
+    const int n = c.n_active;
+    const int32_t* g_act = a.sched + 1;
+    const int32_t* g_off = a.sched + 1 + a.E;
+    const int32_t* g_up = a.sched + 2 + 2 * a.E + a.T * a.K;
+    const int32_t* g_dn = g_up + (a.E + 2);
+    int32_t* s_up = t;
+    int32_t* s_dn = t + (a.E + 2);
+    int32_t* s_off = t + 2 * (a.E + 2);
+    int32_t* s_act = s_off + (a.E + 2);
+    for (int i = threadIdx.x; i < n + 2; i += kThreads) {
+      s_up[i] = g_up[i];
+      s_dn[i] = g_dn[i];
+      if (i <= n) s_off[i] = g_off[i];
+      if (i < n) s_act[i] = g_act[i];
+    }
+    c.up_pref = s_up;
+    c.dn_pref = s_dn;
+    c.offs = s_off;
+    c.act_ids = s_act;
+    __syncthreads();
+  }
   c.qpr = a.I / 4;
   c.qps = a.Is / 4;
   c.ops = a.H / 8;
@@ -450,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
       const int t0 = p.tg * a.tgp;
       const int nt = min(a.tgp, ntok - t0);
       const int kd = phase == 0 ? a.H : (routed ? a.I : a.Is);
-      const int32_t* pairs = a.sched + 2 + 2 * a.E + (routed ? a.sched[1 + a.E + p.s] : 0);
+      const int32_t* pairs = a.sched + 2 + 2 * a.E + (routed ? c.offs[p.s] : 0);
       const int nt_pad = nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 : 8;
       __syncthreads();  // the previous pass finished reading xs and the token table
       if (threadIdx.x < nt) {
@@ -543,16 +577,24 @@ int g_num_sms = 0;
 
 }  // namespace
 
+// Both layouts use the same tokens per pass (the route kernel's cost
+// prefixes depend on it): 8 when the padded 2-stage ring leaves room.
 int experts_tokens_per_pass(const Shape& s) {
   const int kmax = max(s.H, max(s.I, s.Is));
-  const size_t ring = static_cast<size_t>(kWarps) * kRing * kStageBytes + kSmemMeta;
-  return ring + static_cast<size_t>(8) * kmax * 2 <= 220 * 1024 ? 8 : 4;
+  const size_t ring = static_cast<size_t>(kWarps) * 2 * (8 * (512 * 2 + 16)) + kSmemMeta;
+  return ring + static_cast<size_t>(8) * kmax * 2 + static_cast<size_t>(4) * (s.E + 2) * 4 <= 220 * 1024 ? 8 : 4;
 }
 
-size_t experts_smem_bytes(const Shape& s) {
+static size_t ring_bytes(bool tiled) {
+  return tiled ? static_cast<size_t>(kWarps) * RingCfg<true>::kRing * RingCfg<true>::kStageBytes
+               : static_cast<size_t>(kWarps) * RingCfg<false>::kRing * RingCfg<false>::kStageBytes;
+}
+
+size_t experts_smem_bytes(const Shape& s, bool tiled) {
   const int kmax = max(s.H, max(s.I, s.Is));
-  return static_cast<size_t>(kWarps) * kRing * kStageBytes + kSmemMeta +
-         static_cast<size_t>(experts_tokens_per_pass(s)) * kmax * 2;
+  // ring, meta, activations, then the slot tables (4 x (E + 2) ints)
+  return ring_bytes(tiled) + kSmemMeta + static_cast<size_t>(experts_tokens_per_pass(s)) * kmax * 2 +
+         static_cast<size_t>(4) * (s.E + 2) * 4;
 }
 
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
@@ -564,7 +606,7 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
     e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
   }
-  const size_t smem = experts_smem_bytes(s);
+  const size_t smem = experts_smem_bytes(s, w.tiled);
   auto kern = w.tiled ? k_experts<true> : k_experts<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;

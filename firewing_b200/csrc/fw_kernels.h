@@ -120,7 +120,7 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
 
 // The persistent expert kernel (gate_up + SwiGLU and down + scale for every
 // active expert and the shared expert); dynamic shared memory it needs.
-size_t experts_smem_bytes(const Shape& s);
+size_t experts_smem_bytes(const Shape& s, bool tiled);
 // Tokens the expert kernel stages per pass (8, or 4 for wide hidden sizes).
 int experts_tokens_per_pass(const Shape& s);
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
