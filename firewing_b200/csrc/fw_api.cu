@@ -125,6 +125,8 @@ struct OwnedLayer {
   fw::LayerWeights w;
   std::vector<void*> owned;
   bool loaded = false;
+  bool prefill = false;           // tensor maps below are valid
+  fw::PrefillWeightMaps maps{};   // the tiled banks as tensor-core operands
 };
 
 }  // namespace
@@ -132,6 +134,10 @@ struct OwnedLayer {
 namespace fw {
 int record_error(int code, const char* msg) { return fail(code, msg); }
 }  // namespace fw
+
+// Widest forward the decode kernels take; wider ones use the prefill path.
+constexpr int kDecodeMaxTokens = 256;
+constexpr int kMaxTokens = 16384;
 
 struct fw_moe {
   fw_moe_config cfg{};
@@ -151,6 +157,9 @@ struct fw_moe {
   uint64_t bytes = 0;
   bool profile = false;
   cudaEvent_t stage_ev[fw::kStages + 1] = {};
+  bool prefill_ok = false;            // shape supported and scratch maps built
+  fw::PrefillScratchMaps pf_maps{};
+  int prefill_min_tokens = kDecodeMaxTokens + 1;  // forwards this wide or wider take the prefill path
 };
 
 namespace {
@@ -185,8 +194,11 @@ int check_config(const fw_moe_config* c) {
     return fail(FW_EINVAL, "experts must be a multiple of 32, at most 1024");
   if (c->top_k < 1 || c->top_k > 32 || c->top_k > c->experts)
     return fail(FW_EINVAL, "top_k must be in [1, min(32, experts)]");
-  if (c->max_tokens < 1 || c->max_tokens > 256)
-    return fail(FW_EINVAL, "max_tokens must be in [1, 256]");
+  if (c->max_tokens < 1 || c->max_tokens > kMaxTokens)
+    return fail(FW_EINVAL, "max_tokens must be in [1, 16384]");
+  if (c->max_tokens > kDecodeMaxTokens &&
+      !fw::prefill_supported(fw::Shape{c->hidden, c->intermediate, c->shared_intermediate, c->experts, c->top_k}))
+    return fail(FW_EINVAL, "max_tokens above 256 needs hidden and 2*intermediate sizes that are multiples of 128");
   if (c->layers < 1) return fail(FW_EINVAL, "layers must be >= 1");
   // shared memory of the GEMV stages: 8 tokens x cols x f32
   if (8ull * c->hidden * 4 > 200 * 1024) return fail(FW_EINVAL, "hidden too large for staging");
@@ -257,12 +269,24 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &s.up_done, static_cast<size_t>(E) + 1, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.ticket, 1, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.err, 1, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.pair_count, E, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.pair_fill, E, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.pair_offset, static_cast<size_t>(E) + 1, o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.unit_prefix, 2 * (static_cast<size_t>(E) + 2), o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.pair_tk, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->x_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->y_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->idx_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->score_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
-    if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess || cudaMemset(s.ticket, 0, sizeof(int)) != cudaSuccess) {
+    if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess || cudaMemset(s.ticket, 0, sizeof(int)) != cudaSuccess ||
+        cudaMemset(s.pair_count, 0, sizeof(int) * E) != cudaSuccess ||
+        cudaMemset(s.pair_fill, 0, sizeof(int) * E) != cudaSuccess) {
       rc = fail(FW_ECUDA, "status reset failed");
+      break;
+    }
+    h->prefill_ok = fw::prefill_supported(h->shape) && fw::make_prefill_scratch_maps(h->shape, s, &h->pf_maps);
+    if (M > kDecodeMaxTokens && !h->prefill_ok) {
+      rc = fail(FW_ECUDA, "prefill tensor maps could not be encoded");
       break;
     }
     if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -393,6 +417,7 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
   }
   L.w.expert_base = 0;
   L.w.expert_count = static_cast<int>(E);
+  L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
   return FW_OK;
 }
@@ -488,6 +513,7 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
   }
   L.w.expert_base = 0;
   L.w.expert_count = static_cast<int>(E);
+  L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
   return FW_OK;
 }
@@ -502,12 +528,26 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   if (!aligned4(topk_idx) || !aligned4(topk_scores))
     return fail(FW_EINVAL, "topk buffers must be 4-byte aligned");
   FW_CUDA(cudaSetDevice(h->device));
-  const cudaError_t e = fw::launch_block(h->shape, h->layers[layer].w, h->luts, h->sc, x, tokens, y,
-                                         topk_idx ? topk_idx : h->idx_dev,
-                                         topk_scores ? topk_scores : h->score_dev,
-                                         static_cast<cudaStream_t>(stream),
-                                         h->profile ? h->stage_ev : nullptr);
+  const OwnedLayer& L = h->layers[layer];
+  const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
+  if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
+  int32_t* idx = topk_idx ? topk_idx : h->idx_dev;
+  uint16_t* sc = topk_scores ? topk_scores : h->score_dev;
+  const cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
+  const cudaError_t e =
+      prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev)
+              : fw::launch_block(h->shape, L.w, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev);
   if (e != cudaSuccess) return fail(FW_ECUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return FW_OK;
+}
+
+int fw_moe_set_prefill_min_tokens(fw_moe* h, int32_t min_tokens) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  if (min_tokens < 1) return fail(FW_EINVAL, "min_tokens must be >= 1");
+  if (min_tokens <= kDecodeMaxTokens && !h->prefill_ok)
+    return fail(FW_EINVAL, "this block shape has no prefill path");
+  h->prefill_min_tokens = min_tokens;
   return FW_OK;
 }
 

@@ -274,6 +274,7 @@ struct RouteArgs {
   int* up_done;              // [E+1] expert-kernel slot counters to zero
   int tgp, qpr, qps, ops;    // expert-kernel pass size, quads/octets per slot
   int* ticket;               // CTA completion counter (zero between calls)
+  int* pair_count;           // [E] prefill path: per-expert pair counts to add into (or null)
 };
 
 // f32 total-order key with the index folded in (higher logit, then lower
@@ -441,6 +442,7 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
       a.idx[static_cast<size_t>(t) * K + threadIdx.x] = threadIdx.x;
       a.score[static_cast<size_t>(t) * K + threadIdx.x] = 0;
       if (a.sorted_slot) a.sorted_slot[static_cast<size_t>(t) * K + threadIdx.x] = threadIdx.x;
+      if (a.pair_count) atomicAdd(&a.pair_count[threadIdx.x], 1);
     }
     if (a.sh_sig != nullptr && threadIdx.x == 0) a.sh_sig[t] = 0;
   } else {
@@ -501,6 +503,7 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
         a.idx[static_cast<size_t>(t) * K + lane] = my;
         a.score[static_cast<size_t>(t) * K + lane] = f32_to_bf16(__fdiv_rn(pk, ssum));
         if (a.sorted_slot != nullptr) a.sorted_slot[static_cast<size_t>(t) * K + rank] = lane;
+        if (a.pair_count != nullptr) atomicAdd(&a.pair_count[my], 1);
       }
     }
   }
@@ -680,7 +683,7 @@ cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int co
 cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
                          uint16_t* score, int* err, cudaStream_t st) {
   RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-              0, 0, 0, 0, nullptr};
+              0, 0, 0, 0, nullptr, nullptr};
   return launch_route_kernel(a, st);
 }
 
@@ -699,6 +702,27 @@ cudaError_t launch_synth(uint64_t key, uint32_t /*tensor*/, uint64_t start, uint
   return cudaGetLastError();
 }
 
+cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& sc, const uint16_t* x, int T,
+                          cudaStream_t st) {
+  RouterArgs a{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T, sc.err};
+  const size_t smem = static_cast<size_t>(kRouterRows + kRouterTokens) * s.H * 2 + 16;
+  const dim3 grid((s.E + 1 + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
+  return launch_pdl(k_router, grid, dim3(kRouterRows * 32), smem, st, a);
+}
+
+cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& sc, int T, int32_t* topk_idx,
+                               uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st) {
+  RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
+              sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, schedule ? sc.sched : nullptr, sc.up_done,
+              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket, pair_count};
+  return launch_route_kernel(a, st);
+}
+
+cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st) {
+  CombineArgs a{s.H, s.K, T, sc.sorted_slot, sc.weighted, sc.gated_sh, y};
+  return launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
+}
+
 cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
                          const uint16_t* x, int T, uint16_t* y, int32_t* topk_idx,
                          uint16_t* topk_score, cudaStream_t st, cudaEvent_t* ev) {
@@ -707,30 +731,17 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
   if ((e = mark(0)) != cudaSuccess) return e;
   // 1. router logits + shared-gate logit
-  {
-    RouterArgs a{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T, sc.err};
-    const size_t smem = static_cast<size_t>(kRouterRows + kRouterTokens) * s.H * 2 + 16;
-    const dim3 grid((s.E + 1 + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
-    e = launch_pdl(k_router, grid, dim3(kRouterRows * 32), smem, st, a);
-    if (e != cudaSuccess || (e = mark(1)) != cudaSuccess) return e;
-  }
-  // 2. route + permute
-  {
-    RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
-                sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, sc.sched, sc.up_done,
-                experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket};
-    e = launch_route_kernel(a, st);
-    if (e != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
-  }
+  e = launch_router(s, w, sc, x, T, st);
+  if (e != cudaSuccess || (e = mark(1)) != cudaSuccess) return e;
+  // 2. route + expert schedule
+  e = launch_route_block(s, luts, sc, T, topk_idx, topk_score, true, nullptr, st);
+  if (e != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
   // 3. experts: gate_up + SwiGLU, then down + scale (one persistent kernel)
   e = launch_experts(s, w, luts, sc, x, T, topk_score, st);
   if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
   // 4. combine
-  {
-    CombineArgs a{s.H, s.K, T, sc.sorted_slot, sc.weighted, sc.gated_sh, y};
-    e = launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
-    if (e == cudaSuccess) e = mark(4);
-  }
+  e = launch_combine(s, sc, T, y, st);
+  if (e == cudaSuccess) e = mark(4);
   return e;
 }
 

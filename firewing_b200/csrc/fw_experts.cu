@@ -274,18 +274,19 @@ __device__ __forceinline__ void issue_stage(const Cursor& k, const Ctx& c, unsig
 
 // Accumulate one stage: 8 rows x `cols` columns from column col0, NT tokens
 // of bf16 activations (row stride xstride elements) in shared memory.
-// Reference layout: rows padded to cols*2+16 bytes.  Tiled layout: rows of
-// cols*2 bytes, 16-byte chunk c of row r at chunk c ^ r.
+// Reference layout: rows padded to cols*2+16 bytes.  Tiled layout: 1 KB
+// segments of 8 rows x 64 columns, row r at byte r*128 of a segment, its
+// 16-byte chunk j at chunk position j ^ r.
 template <int NT, bool kTiled>
 __device__ __forceinline__ void stage_fma(const unsigned char* buf, int cols, const uint16_t* xs, int xstride,
                                           int col0, int r, int q, float (&acc)[kMaxTGP][8]) {
-  const unsigned char* wrow = buf + r * (kTiled ? cols * 2 : cols * 2 + 16);
+  const unsigned char* wrow = buf + r * (kTiled ? 128 : cols * 2 + 16);
   const uint16_t* xq = xs + col0 + q * 8;
   const int nb = cols >> 5;
 #pragma unroll 4
   for (int b = 0; b < nb; ++b) {
-    const int chunk = kTiled ? ((4 * b + q) ^ r) : (4 * b + q);
-    const uint4 w = *reinterpret_cast<const uint4*>(wrow + chunk * 16);
+    const int off = kTiled ? ((b >> 1) * 1024 + (((4 * (b & 1) + q) ^ r) << 4)) : (4 * b + q) * 16;
+    const uint4 w = *reinterpret_cast<const uint4*>(wrow + off);
 #pragma unroll
     for (int t = 0; t < NT; ++t)
       fma8_bf16(w, *reinterpret_cast<const uint4*>(xq + t * xstride + b * 32), acc[t]);

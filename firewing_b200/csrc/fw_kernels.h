@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace fw {
@@ -48,21 +49,27 @@ struct LayerWeights {
   bool tiled = false;
 };
 
-// Columns per expert-kernel stage for a matrix of k columns: the largest
-// multiple of 32 that divides k, at most 512.
+// Columns per expert-kernel stage for a matrix of k columns (k a multiple
+// of 64): the largest multiple of 64 that divides k, at most 512.
 __host__ __device__ inline int chunk_cols(int k) {
-  for (int c = 512; c >= 32; c -= 32)
+  for (int c = 512; c >= 64; c -= 64)
     if (k % c == 0) return c;
-  return 32;
+  return 64;
 }
 
 // Tiled expert layout.  A matrix of R x K (reference, row-major) is stored
-// as tiles of 8 rows x cw columns (cw = chunk_cols(K)), tile-contiguous,
-// ordered row-group-major then column chunk.  Inside a tile, row r holds its
-// cw columns with 16-byte chunk c stored at chunk position c ^ r.  Paired
-// tiles (kind 0) hold the 4 gate rows 4g..4g+3 then the 4 matching up rows
-// of a gate_up bank; plain tiles (kind 1) hold rows 8g..8g+7.  One tile is
-// one expert-kernel stage: a single bulk copy, read conflict-free.
+// as 8-row groups; a group is K/64 segments of 8 rows x 64 columns (1 KB),
+// segment-contiguous along K, groups in row order, matrices (experts) in
+// order.  Inside a segment, row r occupies bytes r*128 .. r*128+127 and its
+// 16-byte chunk j (columns 8j..8j+7) sits at chunk position j ^ r.  Paired
+// groups (kind 0) hold the 4 gate rows 4g..4g+3 then the 4 matching up rows
+// of a gate_up bank; plain groups (kind 1) hold rows 8g..8g+7.
+//   - The decode expert kernel's stage is chunk_cols(K)/64 consecutive
+//     segments of one group: one bulk copy, read conflict-free.
+//   - A segment is exactly the 128-byte-swizzled K-major operand atom of the
+//     sm_100 tensor cores, so a 4-D tensor map (64 columns, 8 rows, K/64
+//     segments, groups) brings 16 groups = 128 rows x 64 columns into shared
+//     memory in that operand layout with no swizzle of its own.
 struct TiledSpec {
   int kind;                // 0: paired gate/up rows, 1: plain rows
   int K;                   // columns
@@ -86,6 +93,12 @@ struct Scratch {
   int* ticket = nullptr;         // route-kernel completion counter (kept at 0)
   int* err = nullptr;            // device status word
   int max_T = 0;
+  // Prefill path (expert-grouped tensor-core GEMMs), see launch_prefill.
+  int* pair_count = nullptr;     // [E] pairs per expert (zeroed per forward)
+  int* pair_fill = nullptr;      // [E] scatter cursors
+  int* pair_offset = nullptr;    // [E+1] first pair of each expert in grouped order
+  int* unit_prefix = nullptr;    // [2][E+2] GEMM work-unit prefix per slot, up and down phases
+  int32_t* pair_tk = nullptr;    // [T*K] grouped pairs: t*K + top-k position
 };
 
 // Schedule layout inside Scratch::sched (int32 words), written by the route
@@ -133,6 +146,38 @@ cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* i
                          uint16_t* score, int* err, cudaStream_t st);
 cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, long long n,
                           const uint16_t* silu_lut, uint16_t* out, cudaStream_t st);
+
+// ---- prefill path (fw_prefill.cu) ----------------------------------------
+// Tensor maps of one layer's tiled banks for the tensor-core GEMMs.
+struct PrefillWeightMaps {
+  CUtensorMap gate_up;     // routed gate/up bank, 128-row x 64-column boxes
+  CUtensorMap down;        // routed down bank
+  CUtensorMap sh_gate_up;  // shared expert gate/up
+  CUtensorMap sh_down;     // shared expert down
+};
+// Tensor maps of the fixed scratch (activations between the two GEMMs).
+struct PrefillScratchMaps {
+  CUtensorMap act;     // [T*K][I] grouped SwiGLU rows, 16-row boxes
+  CUtensorMap act_sh;  // [T][Is]
+};
+// Whether the prefill GEMMs support this shape (H, 2I, 2Is multiples of 128).
+bool prefill_supported(const Shape& s);
+// Encode the maps (host only; false on failure).
+bool make_prefill_weight_maps(const Shape& s, const LayerWeights& w, PrefillWeightMaps* out);
+bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratchMaps* out);
+// Whole block for T tokens through the prefill kernels: router, route with
+// pair counts, expert grouping, gate_up GEMM (+SwiGLU), down GEMM (+route
+// weight / shared gate), combine.  Stage events as launch_block.
+cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
+                           const PrefillScratchMaps& sm, const Luts& luts, const Scratch& sc, const uint16_t* x,
+                           int T, uint16_t* y, int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
+                           cudaEvent_t* stage_events = nullptr);
+// Stages shared with the decode path (fw_decode.cu).
+cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& sc, const uint16_t* x, int T,
+                          cudaStream_t st);
+cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& sc, int T, int32_t* topk_idx,
+                               uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st);
+cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st);
 
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.

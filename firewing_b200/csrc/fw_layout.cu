@@ -16,17 +16,14 @@ __device__ __forceinline__ uint64_t mix64_dev(uint64_t z) {
 
 // Source (0 / 1) and reference index of tiled element d.
 __device__ __forceinline__ void tiled_source(const TiledSpec& s, long long d, int& src, long long& ref) {
-  const int cw = chunk_cols(s.K);
   const long long m = d / s.mat_elems;
   const long long dl = d - m * s.mat_elems;
-  const long long tile_elems = 8LL * cw;
-  const long long tile = dl / tile_elems;
-  const int w = static_cast<int>(dl - tile * tile_elems);
-  const int r = w / cw, pc = w - r * cw;
-  const int col_in = (((pc >> 3) ^ r) << 3) | (pc & 7);
-  const int nch = s.K / cw;
-  const long long g = tile / nch;
-  const int col = static_cast<int>(tile - g * nch) * cw + col_in;
+  const long long seg = dl >> 9;  // 512 elements per 8 x 64 segment
+  const int w = static_cast<int>(dl & 511);
+  const int r = w >> 6, pc = w & 63;
+  const int nseg = s.K >> 6;
+  const long long g = seg / nseg;
+  const int col = static_cast<int>(seg - g * nseg) * 64 + ((((pc >> 3) ^ r) << 3) | (pc & 7));
   if (s.kind == 0) {
     const long long row = 4 * g + (r & 3);
     if (s.half > 0) {

@@ -87,6 +87,7 @@ def library() -> ctypes.CDLL:
     L.fw_moe_forward.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp]
     L.fw_moe_forward_async.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp, vp]
     L.fw_moe_sync.argtypes = [vp, vp]
+    L.fw_moe_set_prefill_min_tokens.argtypes = [vp, ctypes.c_int32]
     L.fw_moe_memory.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_profile.argtypes = [vp, ctypes.c_int32]
     L.fw_moe_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
@@ -100,7 +101,7 @@ def library() -> ctypes.CDLL:
                                           ctypes.POINTER(ctypes.c_size_t)]
     for name in ("fw_moe_create", "fw_moe_destroy", "fw_moe_load_layer", "fw_moe_synth_layer",
                  "fw_moe_forward", "fw_moe_forward_async", "fw_moe_sync", "fw_moe_memory",
-                 "fw_moe_profile", "fw_moe_profile_read",
+                 "fw_moe_profile", "fw_moe_profile_read", "fw_moe_set_prefill_min_tokens",
                  "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
@@ -211,6 +212,11 @@ class MoeBlock:
         _check(library().fw_moe_sync(self._h, _stream(stream)))
 
     STAGES = ("router", "route", "experts", "combine")
+
+    def set_prefill_min_tokens(self, min_tokens: int) -> None:
+        """Forwards of at least min_tokens tokens (and all above 256) take the
+        tensor-core prefill path; narrower ones the bit-exact decode path."""
+        _check(library().fw_moe_set_prefill_min_tokens(self._h, int(min_tokens)))
 
     def profile(self, enable: bool) -> None:
         _check(library().fw_moe_profile(self._h, 1 if enable else 0))

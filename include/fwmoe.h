@@ -49,7 +49,9 @@ typedef struct fw_moe fw_moe;
  * (src/decoder_layer.rs:14-17, 40-42; src/metal_moe.rs:15-21).
  * Constraints: hidden, intermediate and shared_intermediate multiples of
  * 64, at most 4096; experts % 32 == 0 and <= 1024;
- * 1 <= top_k <= min(32, experts); 1 <= max_tokens <= 256. */
+ * 1 <= top_k <= min(32, experts); 1 <= max_tokens <= 16384, and above 256
+ * only when hidden, 2*intermediate and 2*shared_intermediate are multiples
+ * of 128 (the prefill path's tile height). */
 typedef struct fw_moe_config {
     int32_t hidden;              /* H */
     int32_t intermediate;        /* I of a routed expert */
@@ -108,6 +110,16 @@ int fw_moe_forward(fw_moe* handle, int32_t layer, const uint16_t* x, int32_t tok
 int fw_moe_forward_async(fw_moe* handle, int32_t layer, const uint16_t* x, int32_t tokens,
                          uint16_t* y, int32_t* topk_idx, uint16_t* topk_scores,
                          void* stream);
+
+/* Forwards of at least `min_tokens` tokens (and every forward wider than
+ * 256 tokens) run the prefill path: the expert FFNs as grouped bf16 GEMMs on
+ * the tensor cores (f32 accumulation in the tensor core's own order, outputs
+ * within the block tolerance of the reference, selection exact).  Narrower
+ * forwards run the decode path, which reproduces the reference's dot
+ * schedule bit for bit.  Default 257.  No reference counterpart: the
+ * reference has one path for every width (src/decoder_layer.rs:460-586).
+ * FW_EINVAL when min_tokens <= 256 and the shape has no prefill path. */
+int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);
 
 /* Wait for `stream`, then report and clear device-side status. */
 int fw_moe_sync(fw_moe* handle, void* stream);
