@@ -99,6 +99,7 @@ struct Scratch {
   int* pair_offset = nullptr;    // [E+1] first pair of each expert in grouped order
   int* unit_prefix = nullptr;    // [2][E+2] GEMM work-unit prefix per slot, up and down phases
   int32_t* pair_tk = nullptr;    // [T*K] grouped pairs: t*K + top-k position
+  uint16_t* xg = nullptr;        // [T*K][H] input rows in grouped pair order
 };
 
 // Schedule layout inside Scratch::sched (int32 words), written by the route
@@ -157,6 +158,7 @@ struct PrefillWeightMaps {
 };
 // Tensor maps of the fixed scratch (activations between the two GEMMs).
 struct PrefillScratchMaps {
+  CUtensorMap xg;      // [T*K][H] grouped input rows, 16-row boxes
   CUtensorMap act;     // [T*K][I] grouped SwiGLU rows, 16-row boxes
   CUtensorMap act_sh;  // [T][Is]
 };

@@ -10,8 +10,9 @@
 //
 //   router (exact, shared with decode) -> route (+ per-expert pair counts)
 //   -> k_pf_offsets (one CTA: pair offsets, work-unit prefixes)
-//   -> k_pf_scatter (pairs grouped by expert)
-//   -> k_gemm<up>:   per expert, [2I x H] gate/up rows x gathered token rows,
+//   -> k_pf_scatter (pairs grouped by expert; token rows copied into the
+//                    grouped input xg [pairs][H])
+//   -> k_gemm<up>:   per expert, [2I x H] gate/up rows x its xg rows,
 //                    SwiGLU in the epilogue -> act [pairs][I] (bf16)
 //   -> k_gemm<down>: per expert, [H x I] down rows x act rows, route weight
 //                    (or the shared sigmoid gate) in the epilogue ->
@@ -20,20 +21,21 @@
 //
 // The shared expert is one more slot whose token list is all T tokens.
 //
-// GEMM kernel (k_gemm): persistent, one CTA per SM, 6 warps.
+// GEMM kernel (k_gemm): persistent, one CTA per SM, 10 warps.
 //   warp 0  producer: TMA loads of the weight tile (4-D map over the tiled
 //           bank: 128 rows x 64 columns = 16 KB, already in the 128-byte
-//           swizzled K-major operand layout) and of the token tile (routed
-//           up: tile::gather4 of x rows by token id; otherwise 16-row boxes
-//           of contiguous rows, 128-byte swizzle) into a 4-stage ring.
+//           swizzled K-major operand layout) and of the token tile (16-row
+//           boxes of contiguous rows, 128-byte swizzle) into a 4-stage ring;
+//           at each unit start it prefetches the weight tiles of its next
+//           unit into L2.
 //   warp 1  MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> f32),
 //           M = 128 weight rows, N = the unit's tokens rounded up to 16
 //           (<= 256), K = 64 per stage as 4 instructions; accumulators in
 //           TMEM, double-buffered (2 x 256 columns); tcgen05.commit frees
 //           ring stages and hands finished accumulators to the epilogue.
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
-//           lanes 32*(w%4)..+31), bf16 rounding points of the reference,
-//           stores.
+//   warps 2-9 epilogue, two sets of four: tcgen05.ld of the accumulator
+//           (warp w reads TMEM lanes 32*(w%4)..+31; the sets take alternate
+//           32-column groups), bf16 rounding points of the reference, stores.
 // Work unit = (slot, 256-token chunk, 128-row tile); units are numbered
 // slot-major and dealt round-robin to the CTAs.
 //
@@ -64,7 +66,9 @@ constexpr int kBN = 256;        // tokens per work unit (MMA N, max)
 constexpr int kRing = 4;        // ring stages
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kGemmThreads = 192;
+constexpr int kStageBytes = 32 * kBM * 2;  // epilogue staging per set: 32 tokens x 128 rows, bf16
+constexpr int kEpiSets = 2;                // epilogue warp sets (4 warps each, alternate column groups)
+constexpr int kGemmThreads = 64 + kEpiSets * 128;
 constexpr int kAccCols = 256;   // TMEM columns per accumulator buffer
 constexpr uint64_t kWaitNs = 2000000000ull;
 
@@ -79,21 +83,17 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map), "r"(c0), "r"(c1),
+               "r"(c2), "r"(c3)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
       "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Four rows (r0..r3) of a 2-D map whose box is 64 columns x 1 row.
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int col, int r0, int r1, int r2,
-                                            int r3, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -144,6 +144,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Named barrier 1 + set over one epilogue set's four warps (128 threads).
+__device__ __forceinline__ void epi_sync(int set) { asm volatile("bar.sync %0, 128;" ::"r"(1 + set) : "memory"); }
+// Same barrier with an OR over the set's 128 threads: keeps a set's
+// decisions uniform, so none of its warps can leave while the others wait
+// at epi_sync.
+__device__ __forceinline__ bool epi_any(int set, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, 128, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(1 + set)
+      : "memory");
+  return r != 0;
 }
 
 // ---- work units ---------------------------------------------------------------
@@ -220,10 +238,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   unsigned char* ring_a = smem;                         // [kRing][16 KB]
   unsigned char* ring_b = smem + kRing * kABytes;       // [kRing][32 KB]
-  GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(ring_b + kRing * kBBytes);
-  int* s_tok = reinterpret_cast<int*>(tail + 1);        // [kBN] producer's gather rows
-  int* s_prefix = s_tok + kBN;                          // [E+2]
+  uint16_t* s_stage = reinterpret_cast<uint16_t*>(ring_b + kRing * kBBytes);   // [sets][32][128] epilogue staging
+  GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(ring_b + kRing * kBBytes + kEpiSets * kStageBytes);
+  int* s_prefix = reinterpret_cast<int*>(tail + 1);     // [E+2]
   int* s_offset = s_prefix + a.E + 2;                   // [E+1]
+  int* s_col_row = s_offset + a.E + 1;                  // [kBN] epilogue: destination row per column
+  float* s_col_scale = reinterpret_cast<float*>(s_col_row + kBN);  // [kBN] epilogue: scale per column
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -233,7 +253,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tail->acc_full[i], 1);
-      mbar_init(&tail->acc_empty[i], 4);
+      mbar_init(&tail->acc_empty[i], 4 * kEpiSets);
     }
     mbar_init(&tail->mma_done, 1);
     tail->abort = 0;
@@ -265,16 +285,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
       if (__any_sync(0xffffffffu, aborted(tail))) break;  // warp-uniform
       const Unit w = decode_unit(a, s_prefix, s_offset, u);
-      const bool gather = a.phase == 0 && w.routed;
-      if (gather) {
-        __syncwarp();
-        for (int j = lane; j < w.bn; j += 32) s_tok[j] = a.pair_tk[w.n0 + min(j, w.nvalid - 1)] / a.K;
-        __syncwarp();
-      }
       const int grp0 = (w.routed ? w.slot * a.groups_r : 0) + w.m * (kBM / 8);
       const CUtensorMap* ma = w.routed ? &map_a_r : &map_a_s;
       const CUtensorMap* mb = w.routed ? &map_b_r : &map_b_s;
       const uint32_t bytes = kABytes + w.bn * kBK * 2;
+      {
+        // Pull the weight tiles of this CTA's next unit into L2 while this
+        // one streams, so its loads meet L2 instead of HBM latency.
+        const int un = u + gridDim.x;
+        if (un < total) {
+          const Unit nx = decode_unit(a, s_prefix, s_offset, un);
+          const int ngrp = (nx.routed ? nx.slot * a.groups_r : 0) + nx.m * (kBM / 8);
+          const CUtensorMap* nma = nx.routed ? &map_a_r : &map_a_s;
+          for (int kb = lane; kb < nx.kblocks; kb += 32) tma_prefetch_4d(nma, 0, 0, kb, ngrp);
+        }
+      }
       for (int kb = 0; kb < w.kblocks; ++kb, ++it) {
         const int st = it % kRing;
         const uint32_t ph = (it / kRing) & 1;
@@ -292,13 +317,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         unsigned char* sa = ring_a + st * kABytes;
         unsigned char* sb = ring_b + st * kBBytes;
         if (lane == 0) tma_load_4d(sa, ma, 0, 0, kb, grp0, &tail->full[st], policy);
-        if (gather) {
-          for (int j = lane * 4; j < w.bn; j += 128)
-            tma_gather4(sb + j * 128, mb, kb * kBK, s_tok[j], s_tok[j + 1], s_tok[j + 2], s_tok[j + 3],
-                        &tail->full[st]);
-        } else {
-          for (int j = lane * 16; j < w.bn; j += 512) tma_load_2d(sb + j * 128, mb, kb * kBK, w.n0 + j, &tail->full[st]);
-        }
+        for (int j = lane * 16; j < w.bn; j += 512) tma_load_2d(sb + j * 128, mb, kb * kBK, w.n0 + j, &tail->full[st]);
       }
     }
     // Let the copies already issued land before the CTA can exit.
@@ -347,71 +366,102 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait_bounded(&tail->mma_done, 0, kWaitNs)) raise_abort(tail, a.err);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may read
-    const int row = q * 32 + lane;  // accumulator row (weight row within the tile)
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Two sets of four warps (one warp per TMEM lane quarter in each set);
+    // set s handles the 32-column groups s, s+2, ...  Per group: tcgen05.ld,
+    // the reference's rounding points, the bf16 results into the set's
+    // shared staging tile, then 16-byte stores of whole output rows by the
+    // set's 128 threads.
+    const int ew = warp - 2;
+    const int set = ew >> 2;
+    const int q = warp & 3;             // TMEM lane quarter this warp may read
+    const int row = q * 32 + lane;      // accumulator row (weight row within the tile)
+    const int et = (ew & 3) * 32 + lane;  // 0..127 within the set
+    uint16_t* stage = s_stage + set * (kStageBytes / 2);
     int ai = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++ai) {
-      // Decisions stay warp-uniform: tcgen05.ld below is warp-collective.
-      if (__any_sync(0xffffffffu, aborted(tail))) break;
+      // Decisions stay uniform over the set's 128 threads (tcgen05.ld is
+      // warp-collective; epi_sync waits for all four warps of the set).
+      if (epi_any(set, aborted(tail))) break;
       const Unit w = decode_unit(a, s_prefix, s_offset, u);
       const int buf = ai & 1;
       const uint32_t aph = (ai >> 1) & 1;
+      if (a.phase == 1) {
+        // Column tables (this set's groups): destination row and f32 scale.
+        for (int j = et; j < w.nvalid; j += 128) {
+          if (((j >> 5) & 1) != set) continue;
+          if (w.routed) {
+            const int tk = a.pair_tk[w.n0 + j];
+            s_col_row[j] = tk;
+            s_col_scale[j] = bf16_to_f32(a.score[tk]);
+          } else {
+            s_col_row[j] = w.n0 + j;
+            s_col_scale[j] = bf16_to_f32(a.sh_sig[w.n0 + j]);
+          }
+        }
+      }
       const bool got = mbar_wait_bounded(&tail->acc_full[buf], aph, kWaitNs);
-      if (!__all_sync(0xffffffffu, got)) {
-        if (lane == 0) raise_abort(tail, a.err);
+      if (epi_any(set, !got)) {  // also orders the table writes above before their use
+        if (et == 0) raise_abort(tail, a.err);
         break;
       }
       tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * kAccCols;
-      if (a.phase == 0) {
-        // Rows alternate 4 gate / 4 up per 8-row group: intermediate
-        // 4 * group + (row & 3); lanes with (row & 7) < 4 own the gate value
-        // and fetch the matching up value from lane + 4.
-        const bool gate_lane = (lane & 7) < 4;
-        const int inter = 4 * (w.m * (kBM / 8) + (row >> 3)) + (lane & 3);
-        uint16_t* dst = w.routed ? a.act : a.act_sh;
-        const int width = w.routed ? a.I : a.Is;
-        for (int c0 = 0; c0 < w.bn; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c0, v);
+      for (int c0 = 32 * set; c0 < w.bn; c0 += 32 * kEpiSets) {
+        uint32_t v[32];
+        tmem_ld32(tbase + c0, v);
+        if (a.phase == 0) {
+          // Rows alternate 4 gate / 4 up per 8-row group; lanes with
+          // (row & 7) < 4 own a gate row and take the matching up value
+          // from lane + 4.  swiglu_bf16 (src/expert.rs:562-571) on the bf16
+          // outputs of linear_bf16: bf16(bf16(silu(g)) * u).
+          uint32_t gb[32];
+          float ub[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float g = __uint_as_float(v[j]);
             const float up = __shfl_down_sync(0xffffffffu, g, 4);
-            const int n = c0 + j;
-            if (gate_lane && n < w.nvalid) {
-              // swiglu_bf16 (src/expert.rs:562-571) on the bf16 gate / up
-              // outputs of linear_bf16: bf16(bf16(silu(g)) * u).
-              const uint16_t gb = f32_to_bf16(g);
-              const float s = bf16_to_f32(a.silu[gb]);
-              const float ub = bf16_to_f32(f32_to_bf16(up));
-              dst[static_cast<size_t>(w.n0 + n) * width + inter] = f32_to_bf16(s * ub);
-            }
+            gb[j] = f32_to_bf16(g);
+            ub[j] = bf16_to_f32(f32_to_bf16(up));
           }
-        }
-      } else {
-        const int h = w.m * kBM + row;
-        for (int c0 = 0; c0 < w.bn; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c0, v);
+          if ((lane & 7) < 4) {
+            uint16_t sl[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sl[j] = a.silu[gb[j]];
+            const int il = 16 * q + 4 * (lane >> 3) + (lane & 3);  // intermediate within the tile
+#pragma unroll
+            for (int j = 0; j < 32; ++j) stage[j * 64 + il] = f32_to_bf16(bf16_to_f32(sl[j]) * ub[j]);
+          }
+        } else {
+          // routed: bf16(bf16(down) * route weight) (src/expert.rs:748-751);
+          // shared: bf16(sigmoid * bf16(down)) (src/expert.rs:1144-1147)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int n = c0 + j;
-            if (n < w.nvalid) {
-              const float d = bf16_to_f32(f32_to_bf16(__uint_as_float(v[j])));
-              if (w.routed) {
-                // bf16(down * route weight) (src/expert.rs:748-751)
-                const int tk = a.pair_tk[w.n0 + n];
-                a.weighted[static_cast<size_t>(tk) * a.H + h] = f32_to_bf16(d * bf16_to_f32(a.score[tk]));
-              } else {
-                // bf16(sigmoid * down) (src/expert.rs:1144-1147)
-                const int t = w.n0 + n;
-                a.gated_sh[static_cast<size_t>(t) * a.H + h] = f32_to_bf16(d * bf16_to_f32(a.sh_sig[t]));
-              }
-            }
+            const float dv = bf16_to_f32(f32_to_bf16(__uint_as_float(v[j])));
+            stage[j * 128 + row] = f32_to_bf16(dv * s_col_scale[c0 + j]);
           }
         }
+        epi_sync(set);
+        const int rows_here = min(32, w.nvalid - c0);
+        if (a.phase == 0) {
+          // [32 tokens][64 intermediates]: 8 chunks of 16 bytes per token.
+          uint16_t* dst = w.routed ? a.act : a.act_sh;
+          const int width = w.routed ? a.I : a.Is;
+          for (int ch = et; ch < rows_here * 8; ch += 128) {
+            const int r = ch >> 3, c = ch & 7;
+            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(w.n0 + c0 + r) * width + w.m * 64 + c * 8) =
+                *reinterpret_cast<const uint4*>(stage + r * 64 + c * 8);
+          }
+        } else {
+          // [32 tokens][128 output rows]: 16 chunks of 16 bytes per token.
+          uint16_t* dst = w.routed ? a.weighted : a.gated_sh;
+          for (int ch = et; ch < rows_here * 16; ch += 128) {
+            const int r = ch >> 4, c = ch & 15;
+            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(s_col_row[c0 + r]) * a.H + w.m * kBM + c * 8) =
+                *reinterpret_cast<const uint4*>(stage + r * 128 + c * 8);
+          }
+        }
+        epi_sync(set);
       }
       tc_fence_before();
       __syncwarp();
@@ -423,6 +473,195 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kAccCols) : "memory");
+}
+
+// ---- exact router for prefill widths -------------------------------------------
+//
+// logits[t][e] = bf16(dot(router[e], x[t])) with the reference's dot schedule
+// (src/expert.rs:514-552): 32 f32 partials, partial j summing columns
+// j, j+32, ... in order, then the tree +16, +8, +4, (0+1)+(2+3).  Row E is
+// the shared-expert gate vector (its logit goes to sh_logit).
+//
+// CTA: 32 tokens x 16 rows, 8 warps = 16 half-warps; half-warp h owns tokens
+// 4*(h&7)..+3 and rows 8*(h>>3)..+7, and its lane l the partials 2l and 2l+1
+// (one 32-bit load per operand row and 32-column block), so a thread keeps
+// 4 x 8 x 2 f32 accumulators.  Columns stream through shared memory in
+// chunks of chunk_cols(H), double-buffered with bulk copies (rows padded by
+// 16 bytes so the two half-warps of a warp, 4 tokens apart, hit different
+// banks).
+constexpr int kRtTok = 32, kRtRows = 16, kRtPad = 8;
+
+struct PfRouterArgs {
+  const uint16_t* w;          // [E][H]
+  const uint16_t* extra_row;  // [H]
+  const float* bias;          // [E] or null
+  const uint16_t* x;          // [T][H]
+  uint16_t* logits;           // [T][E]
+  uint16_t* extra_out;        // [T]
+  int E, H, T, kc;            // kc: columns per chunk
+  int* err;
+};
+
+// {a0, a1} += {w0, w1} * {x0, x1}: two f32 fused multiply-adds, each
+// rounded to nearest even (sm_100 packed f32x2 FMA).  With bf16-valued
+// operands every product is exact, so each lane of the pair rounds like the
+// reference's multiply followed by its add.
+__device__ __forceinline__ void fma_f32x2(float w0, float w1, float x0, float x1, float& a0, float& a1) {
+  asm("{\n\t.reg .b64 pa, pb, pc;\n\t"
+      "mov.b64 pa, {%2, %3};\n\t"
+      "mov.b64 pb, {%4, %5};\n\t"
+      "mov.b64 pc, {%0, %1};\n\t"
+      "fma.rn.f32x2 pc, pa, pb, pc;\n\t"
+      "mov.b64 {%0, %1}, pc;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(w0), "f"(w1), "f"(x0), "f"(x1));
+}
+
+__global__ void __launch_bounds__(256, 2) k_router_pf(PfRouterArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int pitch = a.kc + kRtPad;  // elements per staged row
+  uint16_t* buf[2];
+  buf[0] = reinterpret_cast<uint16_t*>(smem);
+  buf[1] = buf[0] + (kRtTok + kRtRows) * pitch;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf[1] + (kRtTok + kRtRows) * pitch);
+  const int row0 = blockIdx.x * kRtRows, t0 = blockIdx.y * kRtTok;
+  const int nrows = min(kRtRows, a.E + 1 - row0), nt = min(kRtTok, a.T - t0);
+  const int nchunks = a.H / a.kc;
+  const uint32_t cbytes = static_cast<uint32_t>(a.kc) * 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Chunk c of the weight rows / token rows into buffer b (thread 0 posts
+  // the byte count; lanes of warp 0 issue one row copy each).
+  auto issue_rows = [&](int c, int b) {
+    if (lane < nrows) {
+      const int row = row0 + lane;
+      const uint16_t* src = (row < a.E ? a.w + static_cast<size_t>(row) * a.H : a.extra_row) + c * a.kc;
+      bulk_g2s(buf[b] + (kRtTok + lane) * pitch, src, cbytes, &bars[b], l2_evict_first_policy());
+    }
+  };
+  auto issue_tokens = [&](int c, int b) {
+    if (lane < nt)
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(buf[b] + lane * pitch)),
+          "l"(a.x + static_cast<size_t>(t0 + lane) * a.H + c * a.kc), "r"(cbytes), "r"(smem_u32(&bars[b]))
+          : "memory");
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_init(&bars[0], 1);
+      mbar_init(&bars[1], 1);
+      fence_mbar_init();
+      for (int b = 0; b < 2 && b < nchunks; ++b) mbar_arrive_expect_tx(&bars[b], cbytes * (nrows + nt));
+    }
+    __syncwarp();
+    // Weights do not depend on the previous kernel: copy them before the
+    // grid-dependency wait.
+    for (int b = 0; b < 2 && b < nchunks; ++b) issue_rows(b, b);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  if (warp == 0)
+    for (int b = 0; b < 2 && b < nchunks; ++b) issue_tokens(b, b);
+  __syncthreads();
+
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const int tg = hw & 7, rg = hw >> 3;
+  float acc[4][8][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc[i][r][0] = acc[i][r][1] = 0.0f;
+  bool ok = true;
+  for (int c = 0; c < nchunks; ++c) {
+    const int b = c & 1;
+    if (!mbar_wait_bounded(&bars[b], (c >> 1) & 1, 2000000000ull)) ok = false;
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0) set_error(a.err, kErrTimeout);
+      ok = false;
+      // Let issued copies land before the CTA exits (bounded).
+      if (threadIdx.x == 0)
+        for (int cc = c; cc < nchunks && cc < c + 2; ++cc) mbar_wait_bounded(&bars[cc & 1], (cc >> 1) & 1, 2000000000ull);
+      break;
+    }
+    const uint16_t* xs = buf[b] + (4 * tg) * pitch + 2 * l;
+    const uint16_t* ws = buf[b] + (kRtTok + 8 * rg) * pitch + 2 * l;
+#pragma unroll 2
+    for (int k = 0; k < a.kc; k += 32) {
+      float xl[4], xh[4], wl[8], wh[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(xs + i * pitch + k);
+        xl[i] = lo_bf16(v);
+        xh[i] = hi_bf16(v);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(ws + r * pitch + k);
+        wl[r] = lo_bf16(v);
+        wh[r] = hi_bf16(v);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int r = 0; r < 8; ++r) fma_f32x2(wl[r], wh[r], xl[i], xh[i], acc[i][r][0], acc[i][r][1]);
+    }
+    __syncthreads();  // buffer b fully read
+    if (warp == 0 && c + 2 < nchunks) {
+      if (lane == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&bars[b], cbytes * (nrows + nt));
+      }
+      __syncwarp();
+      fence_proxy_async_smem();
+      issue_rows(c + 2, b);
+      issue_tokens(c + 2, b);
+    }
+  }
+  if (!ok) return;
+  // Reference tree over the half-warp: lane l holds partials 2l, 2l+1.
+  uint32_t out[4][4];  // per token: 8 bf16 logits packed
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      float p0 = acc[i][r][0], p1 = acc[i][r][1];
+      p0 += __shfl_down_sync(0xffffffffu, p0, 8, 16);  // j += j + 16
+      p1 += __shfl_down_sync(0xffffffffu, p1, 8, 16);
+      p0 += __shfl_down_sync(0xffffffffu, p0, 4, 16);  // j += j + 8
+      p1 += __shfl_down_sync(0xffffffffu, p1, 4, 16);
+      p0 += __shfl_down_sync(0xffffffffu, p0, 2, 16);  // j += j + 4
+      p1 += __shfl_down_sync(0xffffffffu, p1, 2, 16);
+      const float s = p0 + p1;                         // lane 0: 0+1, lane 1: 2+3
+      const float dot = s + __shfl_down_sync(0xffffffffu, s, 1, 16);
+      const uint32_t v = f32_to_bf16(dot);
+      if (r & 1) out[i][r >> 1] |= v << 16;
+      else out[i][r >> 1] = v;
+    }
+  }
+  if (l != 0) return;
+  const int rbase = row0 + 8 * rg;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + 4 * tg + i;
+    if (4 * tg + i >= nt) continue;
+    if (rbase + 8 <= a.E && a.bias == nullptr) {
+      *reinterpret_cast<uint4*>(a.logits + static_cast<size_t>(t) * a.E + rbase) =
+          make_uint4(out[i][0], out[i][1], out[i][2], out[i][3]);
+      continue;
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int row = rbase + r;
+      uint16_t v = static_cast<uint16_t>((out[i][r >> 1] >> (16 * (r & 1))) & 0xffffu);
+      if (row < a.E) {
+        // build-defined extension: f32 logit bias, re-rounded to bf16
+        if (a.bias != nullptr) v = f32_to_bf16(bf16_to_f32(v) + a.bias[row]);
+        a.logits[static_cast<size_t>(t) * a.E + row] = v;
+      } else if (row == a.E) {
+        a.extra_out[t] = v;
+      }
+    }
+  }
 }
 
 // ---- grouping kernels -----------------------------------------------------------
@@ -492,19 +731,31 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
   }
 }
 
-// One thread per (token, top-k position): its slot in its expert's group.
-__global__ void k_pf_scatter(const int32_t* idx, int TK, int E, const int* offset, int* fill, int32_t* pair_tk,
-                             int* err) {
+// One warp per (token, top-k position): its slot in its expert's group, and
+// a copy of the token's input row into the grouped input (so the gate/up
+// GEMM reads each expert's token rows as one contiguous block).
+__global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, const int* offset, int* fill,
+                             int32_t* pair_tk, const uint16_t* x, uint16_t* xg, int* err) {
   pdl_wait();
   pdl_launch_dependents();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (i >= TK) return;
-  const int e = idx[i];
-  if (e < 0 || e >= E) {
-    set_error(err, kErrBadIndex);
-    return;
+  int p = 0;
+  if (lane == 0) {
+    const int e = idx[i];
+    if (e < 0 || e >= E) {
+      set_error(err, kErrBadIndex);
+      p = -1;
+    } else {
+      p = offset[e] + atomicAdd(&fill[e], 1);
+      pair_tk[p] = i;
+    }
   }
-  pair_tk[offset[e] + atomicAdd(&fill[e], 1)] = i;
+  p = __shfl_sync(0xffffffffu, p, 0);
+  if (p < 0) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(i / K) * H);
+  uint4* dst = reinterpret_cast<uint4*>(xg + static_cast<size_t>(p) * H);
+  for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
 }
 
 template <typename Kern, typename... Args>
@@ -528,8 +779,8 @@ cudaError_t launch_pdl_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStr
 }
 
 size_t gemm_smem_bytes(int E) {
-  return 1024 + static_cast<size_t>(kRing) * (kABytes + kBBytes) + sizeof(GemmSmemTail) +
-         sizeof(int) * (kBN + 2 * static_cast<size_t>(E) + 3);
+  return 1024 + static_cast<size_t>(kRing) * (kABytes + kBBytes) + kEpiSets * kStageBytes + sizeof(GemmSmemTail) +
+         sizeof(int) * (2 * kBN + 2 * static_cast<size_t>(E) + 3);
 }
 
 // ---- tensor maps (host) --------------------------------------------------------------
@@ -602,7 +853,8 @@ bool make_prefill_weight_maps(const Shape& s, const LayerWeights& w, PrefillWeig
 
 bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratchMaps* out) {
   if (!prefill_supported(s)) return false;
-  return rows_map(&out->act, sc.act, s.I, static_cast<long long>(sc.max_T) * s.K, 16) &&
+  return rows_map(&out->xg, sc.xg, s.H, static_cast<long long>(sc.max_T) * s.K, 16) &&
+         rows_map(&out->act, sc.act, s.I, static_cast<long long>(sc.max_T) * s.K, 16) &&
          rows_map(&out->act_sh, sc.act_sh, s.Is, sc.max_T, 16);
 }
 
@@ -613,13 +865,19 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   if (T <= 0) return cudaSuccess;
   cudaError_t e;
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
-  // Per-forward maps of the input rows: gathered (routed up) and plain
-  // 16-row boxes (shared up).
-  CUtensorMap x_gather, x_rows;
-  if (!rows_map(&x_gather, x, s.H, T, 1) || !rows_map(&x_rows, x, s.H, T, 16)) return cudaErrorInvalidValue;
+  // Per-forward map of the input rows (the shared expert's token tiles).
+  CUtensorMap x_rows;
+  if (!rows_map(&x_rows, x, s.H, T, 16)) return cudaErrorInvalidValue;
   if ((e = mark(0)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * s.E, st)) != cudaSuccess) return e;
-  if ((e = launch_router(s, w, sc, x, T, st)) != cudaSuccess || (e = mark(1)) != cudaSuccess) return e;
+  {
+    const int kc = chunk_cols(s.H);
+    PfRouterArgs ra{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T, kc, sc.err};
+    const size_t rsm = 2 * static_cast<size_t>(kRtTok + kRtRows) * (kc + kRtPad) * 2 + 16;
+    const dim3 rgrid((s.E + 1 + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
+    if ((e = launch_pdl_ex(k_router_pf, rgrid, dim3(256), rsm, st, ra)) != cudaSuccess || (e = mark(1)) != cudaSuccess)
+      return e;
+  }
   if ((e = launch_route_block(s, luts, sc, T, topk_idx, topk_score, false, sc.pair_count, st)) != cudaSuccess)
     return e;
   {
@@ -628,9 +886,10 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
     const int threads = (s.E + 31) / 32 * 32;
     if ((e = launch_pdl_ex(k_pf_offsets, dim3(1), dim3(threads), 0, st, oa)) != cudaSuccess) return e;
     const int TK = T * s.K;
-    if ((e = launch_pdl_ex(k_pf_scatter, dim3((TK + 255) / 256), dim3(256), 0, st,
-                           static_cast<const int32_t*>(topk_idx), TK, s.E, static_cast<const int*>(sc.pair_offset),
-                           sc.pair_fill, sc.pair_tk, sc.err)) != cudaSuccess)
+    if ((e = launch_pdl_ex(k_pf_scatter, dim3((TK + 7) / 8), dim3(256), 0, st,
+                           static_cast<const int32_t*>(topk_idx), TK, s.K, s.E, s.H,
+                           static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x, sc.xg,
+                           sc.err)) != cudaSuccess)
       return e;
   }
   if ((e = mark(2)) != cudaSuccess) return e;
@@ -661,7 +920,7 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   g.mt_s = 2 * s.Is / kBM;
   g.groups_r = 2 * s.I / 8;
   g.prefix = sc.unit_prefix;
-  if ((e = launch_pdl_ex(k_gemm, grid, block, smem, st, wm.gate_up, wm.sh_gate_up, x_gather, x_rows, g)) !=
+  if ((e = launch_pdl_ex(k_gemm, grid, block, smem, st, wm.gate_up, wm.sh_gate_up, smaps.xg, x_rows, g)) !=
       cudaSuccess)
     return e;
   // down + route weight / shared gate
