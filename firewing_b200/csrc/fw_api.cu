@@ -198,7 +198,7 @@ int check_config(const fw_moe_config* c) {
     return fail(FW_EINVAL, "max_tokens must be in [1, 16384]");
   if (c->max_tokens > kDecodeMaxTokens &&
       !fw::prefill_supported(fw::Shape{c->hidden, c->intermediate, c->shared_intermediate, c->experts, c->top_k}))
-    return fail(FW_EINVAL, "max_tokens above 256 needs hidden and 2*intermediate sizes that are multiples of 128");
+    return fail(FW_EINVAL, "max_tokens above 256 needs hidden a multiple of 256 and 2*intermediate sizes multiples of 128");
   if (c->layers < 1) return fail(FW_EINVAL, "layers must be >= 1");
   // shared memory of the GEMV stages: 8 tokens x cols x f32
   if (8ull * c->hidden * 4 > 200 * 1024) return fail(FW_EINVAL, "hidden too large for staging");

@@ -162,7 +162,8 @@ struct PrefillScratchMaps {
   CUtensorMap act;     // [T*K][I] grouped SwiGLU rows, 16-row boxes
   CUtensorMap act_sh;  // [T][Is]
 };
-// Whether the prefill GEMMs support this shape (H, 2I, 2Is multiples of 128).
+// Whether the prefill kernels support this shape (H a multiple of 256, 2I
+// and 2Is multiples of 128).
 bool prefill_supported(const Shape& s);
 // Encode the maps (host only; false on failure).
 bool make_prefill_weight_maps(const Shape& s, const LayerWeights& w, PrefillWeightMaps* out);

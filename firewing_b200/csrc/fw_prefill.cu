@@ -63,12 +63,14 @@ namespace {
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kBK = 64;         // columns per ring stage (one 128-byte swizzle atom)
 constexpr int kBN = 256;        // tokens per work unit (MMA N, max)
-constexpr int kRing = 4;        // ring stages
+constexpr int kRingA = 6;       // weight-tile ring stages
+constexpr int kRingB = 3;       // token-tile ring stages
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kStageBytes = 32 * kBM * 2;  // epilogue staging per set: 32 tokens x 128 rows, bf16
 constexpr int kEpiSets = 2;                // epilogue warp sets (4 warps each, alternate column groups)
-constexpr int kGemmThreads = 64 + kEpiSets * 128;
+constexpr int kEpiWarp0 = 3;               // warps 0, 1: producers; 2: MMA; 3..: epilogue
+constexpr int kGemmThreads = 32 * kEpiWarp0 + kEpiSets * 128;
 constexpr int kAccCols = 256;   // TMEM columns per accumulator buffer
 constexpr uint64_t kWaitNs = 2000000000ull;
 
@@ -214,8 +216,10 @@ __device__ __forceinline__ Unit decode_unit(const GemmArgs& a, const int* s_pref
 }
 
 struct __align__(8) GemmSmemTail {
-  uint64_t full[kRing];
-  uint64_t empty[kRing];
+  uint64_t full_a[kRingA];
+  uint64_t empty_a[kRingA];
+  uint64_t full_b[kRingB];
+  uint64_t empty_b[kRingB];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t mma_done;
@@ -229,6 +233,45 @@ __device__ __forceinline__ void raise_abort(GemmSmemTail* t, int* err) {
 }
 __device__ __forceinline__ bool aborted(GemmSmemTail* t) { return *reinterpret_cast<volatile int*>(&t->abort) != 0; }
 
+// One producer warp feeding a ring of `depth` stages: per stage, lane 0
+// waits for the slot (bounded) and posts the byte count, then `issue`
+// (called by the whole warp) starts the copies.  Returns the number of
+// stages issued; on exit the copies still in flight have landed (bounded).
+template <typename Issue, typename Bytes>
+__device__ __forceinline__ void produce(const GemmArgs& a, const int* s_prefix, const int* s_offset, int total,
+                                        GemmSmemTail* tail, uint64_t* full, uint64_t* empty, int depth, int lane,
+                                        Bytes bytes_of, Issue issue) {
+  int it = 0;
+  bool ok = true;
+  for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
+    if (__any_sync(0xffffffffu, aborted(tail))) break;  // warp-uniform
+    const Unit w = decode_unit(a, s_prefix, s_offset, u);
+    const uint32_t bytes = bytes_of(w, u);
+    for (int kb = 0; kb < w.kblocks; ++kb, ++it) {
+      const int st = it % depth;
+      const uint32_t ph = (it / depth) & 1;
+      bool got = true;
+      if (lane == 0) {
+        got = mbar_wait_bounded(&empty[st], ph ^ 1u, kWaitNs);
+        if (got) mbar_arrive_expect_tx(&full[st], bytes);
+        else raise_abort(tail, a.err);
+      }
+      got = __shfl_sync(0xffffffffu, got, 0) != 0;  // lane 0 waited; the warp follows it
+      if (!got) {
+        ok = false;
+        break;
+      }
+      issue(w, kb, st, &full[st]);
+    }
+  }
+  // Let the copies already issued land before the CTA can exit.
+  if (lane == 0) {
+    const int first = it > depth ? it - depth : 0;
+    for (int j = first; j < it; ++j)
+      if (!mbar_wait_bounded(&full[j % depth], (j / depth) & 1, kWaitNs)) raise_abort(tail, a.err);
+  }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap map_a_r, const __grid_constant__ CUtensorMap map_a_s,
            const __grid_constant__ CUtensorMap map_b_r, const __grid_constant__ CUtensorMap map_b_s, GemmArgs a) {
@@ -236,10 +279,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // 1024-byte alignment for the swizzled operand tiles.
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  unsigned char* ring_a = smem;                         // [kRing][16 KB]
-  unsigned char* ring_b = smem + kRing * kABytes;       // [kRing][32 KB]
-  uint16_t* s_stage = reinterpret_cast<uint16_t*>(ring_b + kRing * kBBytes);   // [sets][32][128] epilogue staging
-  GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(ring_b + kRing * kBBytes + kEpiSets * kStageBytes);
+  unsigned char* ring_a = smem;                         // [kRingA][16 KB]
+  unsigned char* ring_b = smem + kRingA * kABytes;      // [kRingB][32 KB]
+  uint16_t* s_stage = reinterpret_cast<uint16_t*>(ring_b + kRingB * kBBytes);  // [sets][32][128] epilogue staging
+  GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(ring_b + kRingB * kBBytes + kEpiSets * kStageBytes);
   int* s_prefix = reinterpret_cast<int*>(tail + 1);     // [E+2]
   int* s_offset = s_prefix + a.E + 2;                   // [E+1]
   int* s_col_row = s_offset + a.E + 1;                  // [kBN] epilogue: destination row per column
@@ -247,9 +290,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRing; ++i) {
-      mbar_init(&tail->full[i], 1);
-      mbar_init(&tail->empty[i], 1);
+    for (int i = 0; i < kRingA; ++i) {
+      mbar_init(&tail->full_a[i], 1);
+      mbar_init(&tail->empty_a[i], 1);
+    }
+    for (int i = 0; i < kRingB; ++i) {
+      mbar_init(&tail->full_b[i], 1);
+      mbar_init(&tail->empty_b[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tail->acc_full[i], 1);
@@ -278,58 +325,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int total = s_prefix[a.E + 1];
 
   if (warp == 0) {
-    // ---------------- producer ----------------
+    // ---------------- weight-tile producer ----------------
     const uint64_t policy = l2_evict_first_policy();
-    int it = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; ok && u < total; u += gridDim.x) {
-      if (__any_sync(0xffffffffu, aborted(tail))) break;  // warp-uniform
-      const Unit w = decode_unit(a, s_prefix, s_offset, u);
-      const int grp0 = (w.routed ? w.slot * a.groups_r : 0) + w.m * (kBM / 8);
-      const CUtensorMap* ma = w.routed ? &map_a_r : &map_a_s;
-      const CUtensorMap* mb = w.routed ? &map_b_r : &map_b_s;
-      const uint32_t bytes = kABytes + w.bn * kBK * 2;
-      {
-        // Pull the weight tiles of this CTA's next unit into L2 while this
-        // one streams, so its loads meet L2 instead of HBM latency.
-        const int un = u + gridDim.x;
-        if (un < total) {
-          const Unit nx = decode_unit(a, s_prefix, s_offset, un);
-          const int ngrp = (nx.routed ? nx.slot * a.groups_r : 0) + nx.m * (kBM / 8);
-          const CUtensorMap* nma = nx.routed ? &map_a_r : &map_a_s;
-          for (int kb = lane; kb < nx.kblocks; kb += 32) tma_prefetch_4d(nma, 0, 0, kb, ngrp);
-        }
-      }
-      for (int kb = 0; kb < w.kblocks; ++kb, ++it) {
-        const int st = it % kRing;
-        const uint32_t ph = (it / kRing) & 1;
-        bool got = true;
-        if (lane == 0) {
-          got = mbar_wait_bounded(&tail->empty[st], ph ^ 1u, kWaitNs);
-          if (got) mbar_arrive_expect_tx(&tail->full[st], bytes);
-          else raise_abort(tail, a.err);
-        }
-        got = __shfl_sync(0xffffffffu, got, 0) != 0;  // lane 0 waited; the warp follows it
-        if (!got) {
-          ok = false;
-          break;
-        }
-        unsigned char* sa = ring_a + st * kABytes;
-        unsigned char* sb = ring_b + st * kBBytes;
-        if (lane == 0) tma_load_4d(sa, ma, 0, 0, kb, grp0, &tail->full[st], policy);
-        for (int j = lane * 16; j < w.bn; j += 512) tma_load_2d(sb + j * 128, mb, kb * kBK, w.n0 + j, &tail->full[st]);
-      }
-    }
-    // Let the copies already issued land before the CTA can exit.
-    if (lane == 0) {
-      const int first = it > kRing ? it - kRing : 0;
-      for (int j = first; j < it; ++j)
-        if (!mbar_wait_bounded(&tail->full[j % kRing], (j / kRing) & 1, kWaitNs)) raise_abort(tail, a.err);
-    }
+    produce(
+        a, s_prefix, s_offset, total, tail, tail->full_a, tail->empty_a, kRingA, lane,
+        [&](const Unit&, int u) {
+          // Pull the weight tiles of this CTA's next unit into L2 while this
+          // one streams, so its loads meet L2 instead of HBM latency.
+          const int un = u + gridDim.x;
+          if (un < total) {
+            const Unit nx = decode_unit(a, s_prefix, s_offset, un);
+            const int ngrp = (nx.routed ? nx.slot * a.groups_r : 0) + nx.m * (kBM / 8);
+            const CUtensorMap* nma = nx.routed ? &map_a_r : &map_a_s;
+            for (int kb = lane; kb < nx.kblocks; kb += 32) tma_prefetch_4d(nma, 0, 0, kb, ngrp);
+          }
+          return static_cast<uint32_t>(kABytes);
+        },
+        [&](const Unit& w, int kb, int st, uint64_t* bar) {
+          const int grp0 = (w.routed ? w.slot * a.groups_r : 0) + w.m * (kBM / 8);
+          if (lane == 0) tma_load_4d(ring_a + st * kABytes, w.routed ? &map_a_r : &map_a_s, 0, 0, kb, grp0, bar, policy);
+        });
   } else if (warp == 1) {
+    // ---------------- token-tile producer ----------------
+    produce(
+        a, s_prefix, s_offset, total, tail, tail->full_b, tail->empty_b, kRingB, lane,
+        [&](const Unit& w, int) { return static_cast<uint32_t>(w.bn * kBK * 2); },
+        [&](const Unit& w, int kb, int st, uint64_t* bar) {
+          unsigned char* sb = ring_b + st * kBBytes;
+          const CUtensorMap* mb = w.routed ? &map_b_r : &map_b_s;
+          for (int j = lane * 16; j < w.bn; j += 512) tma_load_2d(sb + j * 128, mb, kb * kBK, w.n0 + j, bar);
+        });
+  } else if (warp == 2) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      int it = 0, ai = 0;
+      int ia = 0, ib = 0, ai = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total; u += gridDim.x, ++ai) {
         if (aborted(tail)) break;
@@ -343,21 +372,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + buf * kAccCols;
         const uint32_t idesc = idesc_bf16(kBM, w.bn);
-        for (int kb = 0; kb < w.kblocks; ++kb, ++it) {
-          const int st = it % kRing;
-          const uint32_t ph = (it / kRing) & 1;
-          if (!mbar_wait_bounded(&tail->full[st], ph, kWaitNs)) {
+        for (int kb = 0; kb < w.kblocks; ++kb, ++ia, ++ib) {
+          const int sa_i = ia % kRingA, sb_i = ib % kRingB;
+          if (!mbar_wait_bounded(&tail->full_a[sa_i], (ia / kRingA) & 1, kWaitNs) ||
+              !mbar_wait_bounded(&tail->full_b[sb_i], (ib / kRingB) & 1, kWaitNs)) {
             raise_abort(tail, a.err);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(ring_a + st * kABytes);
-          const uint32_t sb = smem_u32(ring_b + st * kBBytes);
+          const uint32_t sa = smem_u32(ring_a + sa_i * kABytes);
+          const uint32_t sb = smem_u32(ring_b + sb_i * kBBytes);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
             umma_bf16(d, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&tail->empty[st]);
+          umma_commit(&tail->empty_a[sa_i]);
+          umma_commit(&tail->empty_b[sb_i]);
         }
         if (ok) umma_commit(&tail->acc_full[buf]);
       }
@@ -366,13 +396,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait_bounded(&tail->mma_done, 0, kWaitNs)) raise_abort(tail, a.err);
     }
   } else {
-    // ---------------- epilogue (warps 2..9) ----------------
+    // ---------------- epilogue (warps 3..10) ----------------
     // Two sets of four warps (one warp per TMEM lane quarter in each set);
     // set s handles the 32-column groups s, s+2, ...  Per group: tcgen05.ld,
     // the reference's rounding points, the bf16 results into the set's
     // shared staging tile, then 16-byte stores of whole output rows by the
     // set's 128 threads.
-    const int ew = warp - 2;
+    const int ew = warp - kEpiWarp0;
     const int set = ew >> 2;
     const int q = warp & 3;             // TMEM lane quarter this warp may read
     const int row = q * 32 + lane;      // accumulator row (weight row within the tile)
@@ -482,14 +512,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // j, j+32, ... in order, then the tree +16, +8, +4, (0+1)+(2+3).  Row E is
 // the shared-expert gate vector (its logit goes to sh_logit).
 //
-// CTA: 32 tokens x 16 rows, 8 warps = 16 half-warps; half-warp h owns tokens
-// 4*(h&7)..+3 and rows 8*(h>>3)..+7, and its lane l the partials 2l and 2l+1
-// (one 32-bit load per operand row and 32-column block), so a thread keeps
-// 4 x 8 x 2 f32 accumulators.  Columns stream through shared memory in
-// chunks of chunk_cols(H), double-buffered with bulk copies (rows padded by
-// 16 bytes so the two half-warps of a warp, 4 tokens apart, hit different
-// banks).
-constexpr int kRtTok = 32, kRtRows = 16, kRtPad = 8;
+// Persistent CTAs walk tiles of 32 tokens x 16 rows.  Warp 8 is the
+// producer: it streams column chunks of every tile (bf16, rows padded by 16
+// bytes) into a 2-stage ring with bulk copies, on across tile boundaries.
+// Warps 0-7 (16 half-warps) consume: half-warp h owns tokens 4*(h&7)..+3
+// and rows 8*(h>>3)..+7, its lane l the partials 2l and 2l+1 (one 32-bit
+// load per operand row per 32-column block, mixed-precision bf16 FMAs into
+// f32).  Full/empty mbarriers replace block-wide barriers, so each warp runs
+// at its own pace.
+constexpr int kRtTok = 32, kRtRows = 16, kRtMaxChunk = 512, kRtPad = 8, kRtComputeWarps = 8;
 
 struct PfRouterArgs {
   const uint16_t* w;          // [E][H]
@@ -498,167 +529,183 @@ struct PfRouterArgs {
   const uint16_t* x;          // [T][H]
   uint16_t* logits;           // [T][E]
   uint16_t* extra_out;        // [T]
-  int E, H, T, kc;            // kc: columns per chunk
+  int E, H, T;
+  int kc;                     // columns per chunk: 512, or 256 when H is not a multiple of 512
   int* err;
 };
 
-// {a0, a1} += {w0, w1} * {x0, x1}: two f32 fused multiply-adds, each
-// rounded to nearest even (sm_100 packed f32x2 FMA).  With bf16-valued
-// operands every product is exact, so each lane of the pair rounds like the
-// reference's multiply followed by its add.
-__device__ __forceinline__ void fma_f32x2(float w0, float w1, float x0, float x1, float& a0, float& a1) {
-  asm("{\n\t.reg .b64 pa, pb, pc;\n\t"
-      "mov.b64 pa, {%2, %3};\n\t"
-      "mov.b64 pb, {%4, %5};\n\t"
-      "mov.b64 pc, {%0, %1};\n\t"
-      "fma.rn.f32x2 pc, pa, pb, pc;\n\t"
-      "mov.b64 {%0, %1}, pc;\n\t}"
+// a0 += lo(w) * lo(x), a1 += hi(w) * hi(x): mixed-precision FMAs (bf16
+// operands, f32 accumulator, round to nearest even).  A bf16 x bf16 product
+// is exact in f32, so each rounds like the reference's multiply then add.
+__device__ __forceinline__ void fma2_bf16(uint32_t w, uint32_t x, float& a0, float& a1) {
+  asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+      "mov.b32 {w0, w1}, %2;\n\t"
+      "mov.b32 {x0, x1}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, w0, x0, %0;\n\t"
+      "fma.rn.f32.bf16 %1, w1, x1, %1;\n\t}"
       : "+f"(a0), "+f"(a1)
-      : "f"(w0), "f"(w1), "f"(x0), "f"(x1));
+      : "r"(w), "r"(x));
 }
 
-__global__ void __launch_bounds__(256, 2) k_router_pf(PfRouterArgs a) {
+size_t router_pf_smem() { return 2 * static_cast<size_t>(kRtTok + kRtRows) * (kRtMaxChunk + kRtPad) * 2 + 64; }
+
+__global__ void __launch_bounds__(32 * (kRtComputeWarps + 1), 2) k_router_pf(PfRouterArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const int pitch = a.kc + kRtPad;  // elements per staged row
-  uint16_t* buf[2];
-  buf[0] = reinterpret_cast<uint16_t*>(smem);
-  buf[1] = buf[0] + (kRtTok + kRtRows) * pitch;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(buf[1] + (kRtTok + kRtRows) * pitch);
-  const int row0 = blockIdx.x * kRtRows, t0 = blockIdx.y * kRtTok;
-  const int nrows = min(kRtRows, a.E + 1 - row0), nt = min(kRtTok, a.T - t0);
-  const int nchunks = a.H / a.kc;
-  const uint32_t cbytes = static_cast<uint32_t>(a.kc) * 2;
+  constexpr int kRowsAll = kRtTok + kRtRows;
+  const int kRtChunk = a.kc, kRtPitch = a.kc + kRtPad;
+  uint16_t* stage[2];
+  stage[0] = reinterpret_cast<uint16_t*>(smem);
+  stage[1] = stage[0] + kRowsAll * kRtPitch;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage[1] + kRowsAll * kRtPitch);  // [2]
+  uint64_t* empty = full + 2;                                                     // [2]
+  const int row_tiles = (a.E + 1 + kRtRows - 1) / kRtRows;
+  const int tiles = row_tiles * ((a.T + kRtTok - 1) / kRtTok);
+  const int nchunks = a.H / kRtChunk;
+  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int nstream = my_tiles * nchunks;
+  const uint32_t cbytes = kRtChunk * 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Chunk c of the weight rows / token rows into buffer b (thread 0 posts
-  // the byte count; lanes of warp 0 issue one row copy each).
-  auto issue_rows = [&](int c, int b) {
-    if (lane < nrows) {
-      const int row = row0 + lane;
-      const uint16_t* src = (row < a.E ? a.w + static_cast<size_t>(row) * a.H : a.extra_row) + c * a.kc;
-      bulk_g2s(buf[b] + (kRtTok + lane) * pitch, src, cbytes, &bars[b], l2_evict_first_policy());
-    }
+  auto tile_geom = [&](int i, int& row0, int& nrows, int& t0, int& nt) {
+    const int tile = blockIdx.x + i * gridDim.x;
+    const int tr = tile % row_tiles, tt = tile / row_tiles;
+    row0 = tr * kRtRows;
+    nrows = min(kRtRows, a.E + 1 - row0);
+    t0 = tt * kRtTok;
+    nt = min(kRtTok, a.T - t0);
   };
-  auto issue_tokens = [&](int c, int b) {
-    if (lane < nt)
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-              smem_u32(buf[b] + lane * pitch)),
-          "l"(a.x + static_cast<size_t>(t0 + lane) * a.H + c * a.kc), "r"(cbytes), "r"(smem_u32(&bars[b]))
-          : "memory");
-  };
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_init(&bars[0], 1);
-      mbar_init(&bars[1], 1);
-      fence_mbar_init();
-      for (int b = 0; b < 2 && b < nchunks; ++b) mbar_arrive_expect_tx(&bars[b], cbytes * (nrows + nt));
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&full[b], 1);
+      mbar_init(&empty[b], kRtComputeWarps);
     }
-    __syncwarp();
-    // Weights do not depend on the previous kernel: copy them before the
-    // grid-dependency wait.
-    for (int b = 0; b < 2 && b < nchunks; ++b) issue_rows(b, b);
+    fence_mbar_init();
   }
-  pdl_wait();
-  pdl_launch_dependents();
-  if (warp == 0)
-    for (int b = 0; b < 2 && b < nchunks; ++b) issue_tokens(b, b);
   __syncthreads();
 
+  if (warp == kRtComputeWarps) {
+    // ---------------- producer ----------------
+    const uint64_t policy = l2_evict_first_policy();
+    bool waited = false;
+    int g = 0;
+    for (; g < nstream; ++g) {
+      const int b = g & 1;
+      int row0, nrows, t0, nt;
+      tile_geom(g / nchunks, row0, nrows, t0, nt);
+      const int c = g % nchunks;
+      bool ok = true;
+      if (lane == 0) {
+        ok = mbar_wait_bounded(&empty[b], ((g >> 1) & 1) ^ 1u, 2000000000ull);
+        if (ok) mbar_arrive_expect_tx(&full[b], cbytes * (nrows + nt));
+        else set_error(a.err, kErrTimeout);
+      }
+      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+      if (lane < nrows) {
+        const int row = row0 + lane;
+        const uint16_t* src = (row < a.E ? a.w + static_cast<size_t>(row) * a.H : a.extra_row) + c * kRtChunk;
+        bulk_g2s(stage[b] + (kRtTok + lane) * kRtPitch, src, cbytes, &full[b], policy);
+      }
+      // Weights do not depend on the previous kernel; token rows do.
+      if (!waited) {
+        pdl_wait();
+        pdl_launch_dependents();
+        waited = true;
+      }
+      if (lane < nt)
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(stage[b] + lane * kRtPitch)),
+            "l"(a.x + static_cast<size_t>(t0 + lane) * a.H + c * kRtChunk), "r"(cbytes), "r"(smem_u32(&full[b]))
+            : "memory");
+    }
+    if (!waited) {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    // Copies still in flight land before the CTA exits (bounded).
+    if (lane == 0)
+      for (int gg = g > 2 ? g - 2 : 0; gg < g; ++gg) mbar_wait_bounded(&full[gg & 1], (gg >> 1) & 1, 2000000000ull);
+    return;
+  }
+
+  // ---------------- compute warps ----------------
   const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int tg = hw & 7, rg = hw >> 3;
-  float acc[4][8][2];
+  int g = 0;  // chunk-stream position
+  for (int i = 0; i < my_tiles; ++i) {
+    int row0, nrows, t0, nt;
+    tile_geom(i, row0, nrows, t0, nt);
+    float acc[4][8][2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+    for (int ti = 0; ti < 4; ++ti)
 #pragma unroll
-    for (int r = 0; r < 8; ++r) acc[i][r][0] = acc[i][r][1] = 0.0f;
-  bool ok = true;
-  for (int c = 0; c < nchunks; ++c) {
-    const int b = c & 1;
-    if (!mbar_wait_bounded(&bars[b], (c >> 1) & 1, 2000000000ull)) ok = false;
-    if (__syncthreads_or(!ok)) {
-      if (threadIdx.x == 0) set_error(a.err, kErrTimeout);
-      ok = false;
-      // Let issued copies land before the CTA exits (bounded).
-      if (threadIdx.x == 0)
-        for (int cc = c; cc < nchunks && cc < c + 2; ++cc) mbar_wait_bounded(&bars[cc & 1], (cc >> 1) & 1, 2000000000ull);
-      break;
-    }
-    const uint16_t* xs = buf[b] + (4 * tg) * pitch + 2 * l;
-    const uint16_t* ws = buf[b] + (kRtTok + 8 * rg) * pitch + 2 * l;
+      for (int r = 0; r < 8; ++r) acc[ti][r][0] = acc[ti][r][1] = 0.0f;
+    for (int c = 0; c < nchunks; ++c, ++g) {
+      const int b = g & 1;
+      const bool ok = mbar_wait_bounded(&full[b], (g >> 1) & 1, 2000000000ull);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) set_error(a.err, kErrTimeout);
+        return;
+      }
+      const uint16_t* xs = stage[b] + (4 * tg) * kRtPitch + 2 * l;
+      const uint16_t* ws = stage[b] + (kRtTok + 8 * rg) * kRtPitch + 2 * l;
 #pragma unroll 2
-    for (int k = 0; k < a.kc; k += 32) {
-      float xl[4], xh[4], wl[8], wh[8];
+      for (int k = 0; k < kRtChunk; k += 32) {
+        uint32_t xv[4], wv[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t v = *reinterpret_cast<const uint32_t*>(xs + i * pitch + k);
-        xl[i] = lo_bf16(v);
-        xh[i] = hi_bf16(v);
-      }
+        for (int ti = 0; ti < 4; ++ti) xv[ti] = *reinterpret_cast<const uint32_t*>(xs + ti * kRtPitch + k);
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const uint32_t v = *reinterpret_cast<const uint32_t*>(ws + r * pitch + k);
-        wl[r] = lo_bf16(v);
-        wh[r] = hi_bf16(v);
-      }
+        for (int r = 0; r < 8; ++r) wv[r] = *reinterpret_cast<const uint32_t*>(ws + r * kRtPitch + k);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int ti = 0; ti < 4; ++ti)
 #pragma unroll
-        for (int r = 0; r < 8; ++r) fma_f32x2(wl[r], wh[r], xl[i], xh[i], acc[i][r][0], acc[i][r][1]);
-    }
-    __syncthreads();  // buffer b fully read
-    if (warp == 0 && c + 2 < nchunks) {
-      if (lane == 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bars[b], cbytes * (nrows + nt));
+          for (int r = 0; r < 8; ++r) fma2_bf16(wv[r], xv[ti], acc[ti][r][0], acc[ti][r][1]);
       }
       __syncwarp();
-      fence_proxy_async_smem();
-      issue_rows(c + 2, b);
-      issue_tokens(c + 2, b);
+      if (lane == 0) mbar_arrive(&empty[b]);
     }
-  }
-  if (!ok) return;
-  // Reference tree over the half-warp: lane l holds partials 2l, 2l+1.
-  uint32_t out[4][4];  // per token: 8 bf16 logits packed
+    // Reference tree over the half-warp: lane l holds partials 2l, 2l+1.
+    uint32_t out[4][4];  // per token: 8 bf16 logits packed
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+    for (int ti = 0; ti < 4; ++ti) {
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      float p0 = acc[i][r][0], p1 = acc[i][r][1];
-      p0 += __shfl_down_sync(0xffffffffu, p0, 8, 16);  // j += j + 16
-      p1 += __shfl_down_sync(0xffffffffu, p1, 8, 16);
-      p0 += __shfl_down_sync(0xffffffffu, p0, 4, 16);  // j += j + 8
-      p1 += __shfl_down_sync(0xffffffffu, p1, 4, 16);
-      p0 += __shfl_down_sync(0xffffffffu, p0, 2, 16);  // j += j + 4
-      p1 += __shfl_down_sync(0xffffffffu, p1, 2, 16);
-      const float s = p0 + p1;                         // lane 0: 0+1, lane 1: 2+3
-      const float dot = s + __shfl_down_sync(0xffffffffu, s, 1, 16);
-      const uint32_t v = f32_to_bf16(dot);
-      if (r & 1) out[i][r >> 1] |= v << 16;
-      else out[i][r >> 1] = v;
+      for (int r = 0; r < 8; ++r) {
+        float p0 = acc[ti][r][0], p1 = acc[ti][r][1];
+        p0 += __shfl_down_sync(0xffffffffu, p0, 8, 16);  // j += j + 16
+        p1 += __shfl_down_sync(0xffffffffu, p1, 8, 16);
+        p0 += __shfl_down_sync(0xffffffffu, p0, 4, 16);  // j += j + 8
+        p1 += __shfl_down_sync(0xffffffffu, p1, 4, 16);
+        p0 += __shfl_down_sync(0xffffffffu, p0, 2, 16);  // j += j + 4
+        p1 += __shfl_down_sync(0xffffffffu, p1, 2, 16);
+        const float s = p0 + p1;                         // lane 0: 0+1, lane 1: 2+3
+        const float dot = s + __shfl_down_sync(0xffffffffu, s, 1, 16);
+        const uint32_t v = f32_to_bf16(dot);
+        if (r & 1) out[ti][r >> 1] |= v << 16;
+        else out[ti][r >> 1] = v;
+      }
     }
-  }
-  if (l != 0) return;
-  const int rbase = row0 + 8 * rg;
+    if (l == 0) {
+      const int rbase = row0 + 8 * rg;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + 4 * tg + i;
-    if (4 * tg + i >= nt) continue;
-    if (rbase + 8 <= a.E && a.bias == nullptr) {
-      *reinterpret_cast<uint4*>(a.logits + static_cast<size_t>(t) * a.E + rbase) =
-          make_uint4(out[i][0], out[i][1], out[i][2], out[i][3]);
-      continue;
-    }
+      for (int ti = 0; ti < 4; ++ti) {
+        const int t = t0 + 4 * tg + ti;
+        if (4 * tg + ti >= nt) continue;
+        if (rbase + 8 <= a.E && a.bias == nullptr) {
+          *reinterpret_cast<uint4*>(a.logits + static_cast<size_t>(t) * a.E + rbase) =
+              make_uint4(out[ti][0], out[ti][1], out[ti][2], out[ti][3]);
+          continue;
+        }
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int row = rbase + r;
-      uint16_t v = static_cast<uint16_t>((out[i][r >> 1] >> (16 * (r & 1))) & 0xffffu);
-      if (row < a.E) {
-        // build-defined extension: f32 logit bias, re-rounded to bf16
-        if (a.bias != nullptr) v = f32_to_bf16(bf16_to_f32(v) + a.bias[row]);
-        a.logits[static_cast<size_t>(t) * a.E + row] = v;
-      } else if (row == a.E) {
-        a.extra_out[t] = v;
+        for (int r = 0; r < 8; ++r) {
+          const int row = rbase + r;
+          uint16_t v = static_cast<uint16_t>((out[ti][r >> 1] >> (16 * (r & 1))) & 0xffffu);
+          if (row < a.E) {
+            // build-defined extension: f32 logit bias, re-rounded to bf16
+            if (a.bias != nullptr) v = f32_to_bf16(bf16_to_f32(v) + a.bias[row]);
+            a.logits[static_cast<size_t>(t) * a.E + row] = v;
+          } else if (row == a.E) {
+            a.extra_out[t] = v;
+          }
+        }
       }
     }
   }
@@ -779,7 +826,8 @@ cudaError_t launch_pdl_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStr
 }
 
 size_t gemm_smem_bytes(int E) {
-  return 1024 + static_cast<size_t>(kRing) * (kABytes + kBBytes) + kEpiSets * kStageBytes + sizeof(GemmSmemTail) +
+  return 1024 + static_cast<size_t>(kRingA) * kABytes + static_cast<size_t>(kRingB) * kBBytes +
+         kEpiSets * kStageBytes + sizeof(GemmSmemTail) +
          sizeof(int) * (2 * kBN + 2 * static_cast<size_t>(E) + 3);
 }
 
@@ -841,7 +889,7 @@ int sm_count() {
 }  // namespace
 
 bool prefill_supported(const Shape& s) {
-  return s.H % kBM == 0 && (2 * s.I) % kBM == 0 && (2 * s.Is) % kBM == 0 && s.E <= 1024;
+  return s.H % (kRtMaxChunk / 2) == 0 && s.H % kBM == 0 && (2 * s.I) % kBM == 0 && (2 * s.Is) % kBM == 0 && s.E <= 1024;
 }
 
 bool make_prefill_weight_maps(const Shape& s, const LayerWeights& w, PrefillWeightMaps* out) {
@@ -871,11 +919,13 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   if ((e = mark(0)) != cudaSuccess) return e;
   if ((e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * s.E, st)) != cudaSuccess) return e;
   {
-    const int kc = chunk_cols(s.H);
-    PfRouterArgs ra{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T, kc, sc.err};
-    const size_t rsm = 2 * static_cast<size_t>(kRtTok + kRtRows) * (kc + kRtPad) * 2 + 16;
-    const dim3 rgrid((s.E + 1 + kRtRows - 1) / kRtRows, (T + kRtTok - 1) / kRtTok);
-    if ((e = launch_pdl_ex(k_router_pf, rgrid, dim3(256), rsm, st, ra)) != cudaSuccess || (e = mark(1)) != cudaSuccess)
+    PfRouterArgs ra{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T,
+                    s.H % kRtMaxChunk == 0 ? kRtMaxChunk : kRtMaxChunk / 2, sc.err};
+    const size_t rsm = router_pf_smem();
+    const int rtiles = (s.E + 1 + kRtRows - 1) / kRtRows * ((T + kRtTok - 1) / kRtTok);
+    const dim3 rgrid(rtiles < 2 * sm_count() ? rtiles : 2 * sm_count());
+    if ((e = launch_pdl_ex(k_router_pf, rgrid, dim3(32 * (kRtComputeWarps + 1)), rsm, st, ra)) != cudaSuccess ||
+        (e = mark(1)) != cudaSuccess)
       return e;
   }
   if ((e = launch_route_block(s, luts, sc, T, topk_idx, topk_score, false, sc.pair_count, st)) != cudaSuccess)

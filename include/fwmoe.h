@@ -50,8 +50,8 @@ typedef struct fw_moe fw_moe;
  * Constraints: hidden, intermediate and shared_intermediate multiples of
  * 64, at most 4096; experts % 32 == 0 and <= 1024;
  * 1 <= top_k <= min(32, experts); 1 <= max_tokens <= 16384, and above 256
- * only when hidden, 2*intermediate and 2*shared_intermediate are multiples
- * of 128 (the prefill path's tile height). */
+ * only when hidden is a multiple of 256 and 2*intermediate and
+ * 2*shared_intermediate are multiples of 128 (the prefill path's tiles). */
 typedef struct fw_moe_config {
     int32_t hidden;              /* H */
     int32_t intermediate;        /* I of a routed expert */
