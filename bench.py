@@ -33,6 +33,11 @@ WORKLOADS = {
                  layers=24, tokens=64, zipf=False,
                  name="cfg1: 24-layer stack of the config-0 block, decode"),
 }
+# Reported alongside (not the headline): BASELINE config 2, one block at
+# prefill width with the Zipf-biased router, on the tensor-core path.
+PREFILL = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10,
+               tokens=8192, zipf=True, seed=1,
+               name="cfg2: one config-0 block, prefill T=8192, Zipf-biased router")
 METRIC = "MoE-block tokens/s (token-layers per second through the block)"
 UNIT = "tokens/s"
 
@@ -373,6 +378,10 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
            "d2h_bytes_per_step": L * T * (H * 2 + K * 4 + K * 2),
            "api": "fw_moe_forward (synchronous, pinned host buffers), one call per layer"}
 
+    blk.close()
+    prefill = None if args.no_prefill else measure_prefill(args, rank, world, local_rank, peaks, stream,
+                                                          max_over_ranks, barrier)
+
     cpu = None
     parity = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -405,15 +414,82 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             "block_gbs": step_bytes * args.steps / el / 1e9 * world,
             "block_frac_hbm": step_bytes * args.steps / el / 1e9 / hbm_peak,
             "roofline": roofline,
-            "gpu_launches": 5 * L * args.steps,
+            "gpu_launches": 4 * L * args.steps,
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "parity_sample": parity,
             "t4": t4,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
+
+
+def measure_prefill(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier):
+    """BASELINE config 2 on the tensor-core prefill path: one block, T=8192
+    tokens, Zipf-biased router.  CUDA events around `steps` forwards with
+    device-resident inputs; a per-stage pass afterwards."""
+    import torch
+
+    import firewing_b200 as fw
+    from firewing_b200 import synth
+
+    p = PREFILL
+    T, H, K = p["tokens"], p["hidden"], p["top_k"]
+    cfg = fw.MoeConfig(H, p["intermediate"], p["shared_intermediate"], p["experts"], K,
+                       max_tokens=T, layers=1)
+    blk = fw.MoeBlock(cfg, device=local_rank)
+    blk.synth_layer(0, p["seed"], 0.02, p["zipf"])
+    x = torch.from_numpy(synth.synth_input(input_seed(rank, 0), T, H).view(np.int16)).cuda()
+    y = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    idx = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    sc = torch.empty((T, K), dtype=torch.int16, device="cuda")
+    steps = max(3, args.steps // 5)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            blk.forward_async(0, x, T, y, idx, sc, stream=stream)
+    blk.sync(stream)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        blk.forward_async(0, x, T, y, idx, sc, stream=stream)
+    e1.record(stream)
+    e1.synchronize()
+    blk.sync(stream)
+    el = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    blk.profile(True)
+    stages = {s_: 0.0 for s_ in fw.MoeBlock.STAGES}
+    for _ in range(3):
+        blk.forward_async(0, x, T, y, idx, sc, stream=stream)
+        for k_, v_ in blk.profile_read().items():
+            stages[k_] += v_ / 3
+    blk.profile(False)
+    ids = idx.cpu().numpy()
+    counts = np.bincount(ids.ravel(), minlength=p["experts"])
+    unique = int((counts > 0).sum())
+    I, Is = p["intermediate"], p["shared_intermediate"]
+    flops = 2 * 3 * H * I * T * K + 2 * 3 * H * Is * T
+    wbytes = unique * 3 * H * I * 2 + 3 * H * Is * 2
+    ex_s = stages["experts"] / 1e3
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0)) if peaks else 1590.0
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0)) if peaks else 6650.0
     blk.close()
+    return {
+        "workload": p["name"], "tokens": T, "layers": 1, "steps": steps,
+        "value": world * T * steps / el, "unit": UNIT, "ms_per_step": el / steps * 1e3,
+        "stage_ms": stages,
+        "experts_tflops": flops / ex_s / 1e12,
+        "experts_frac_tensor": flops / ex_s / 1e12 / tc_peak,
+        "experts_weight_gbs": wbytes / ex_s / 1e9,
+        "experts_frac_hbm": wbytes / ex_s / 1e9 / hbm_peak,
+        "peak_source": "measured bf16_tflops / hbm_gbs" if peaks else "fallback",
+        "hottest_expert_tokens": int(counts.max()), "distinct_experts": unique,
+        "gpu_launches_per_step": 7,
+        "kernels": "router (exact, CUDA cores), route, pair offsets, pair scatter, gate/up GEMM "
+                   "(tcgen05, SwiGLU epilogue), down GEMM (tcgen05, weight epilogue), combine",
+    }
 
 
 class _Null:
@@ -434,6 +510,7 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill line item")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--minimal", action="store_true",
                     help="timed steps only (no T=4 pass, e2e, stage profile or CPU leg); "
