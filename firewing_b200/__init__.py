@@ -9,10 +9,14 @@ importing the binding fails loudly when the library has not been built.
 from .moe import (  # noqa: F401
     FW_EINVAL,
     FW_ENAN,
+    FW_ENCCL,
     FW_OK,
     FwError,
     MoeBlock,
     MoeConfig,
+    ep_combine_row,
+    ep_expert_range,
+    ep_unique_id,
     forward_noalloc,
     library,
     library_path,

@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build")
-SOURCES = ["fw_api.cu", "fw_decode.cu", "fw_experts.cu", "fw_layout.cu", "fw_noalloc.cu", "fw_prefill.cu"]
+SOURCES = ["fw_api.cu", "fw_decode.cu", "fw_experts.cu", "fw_layout.cu", "fw_noalloc.cu", "fw_prefill.cu", "fw_ep.cu"]
 HEADERS = ["fw_common.cuh", "fw_kernels.h"]
 SO = os.path.join(HERE, "libfwmoe.so")
 LIB = os.path.join(HERE, "libfwmoe.a")
@@ -58,7 +58,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                 print(" ".join(cmd), flush=True)
             subprocess.run(cmd, check=True)
     if force or _stale(SO, objs):
-        subprocess.run([nvcc, *ARCH, "-Wno-deprecated-gpu-targets", "-shared", "-o", SO, *objs], check=True)
+        subprocess.run([nvcc, *ARCH, "-Wno-deprecated-gpu-targets", "-shared", "-o", SO, *objs, "-ldl"], check=True)
     if force or _stale(LIB, objs):
         subprocess.run([nvcc, *ARCH, "-Wno-deprecated-gpu-targets", "-lib", "-o", LIB, *objs], check=True)
     return SO

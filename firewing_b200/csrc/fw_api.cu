@@ -160,6 +160,14 @@ struct fw_moe {
   bool prefill_ok = false;            // shape supported and scratch maps built
   fw::PrefillScratchMaps pf_maps{};
   int prefill_min_tokens = kDecodeMaxTokens + 1;  // forwards this wide or wider take the prefill path
+  // Expert parallelism (fw_moe_ep_init): this rank's expert range, the NCCL
+  // communicator and the exchange buffers (world * max_tokens tokens).
+  fw::EpComm* ep = nullptr;
+  int ep_rank = 0, ep_world = 1;
+  uint16_t* ep_x_all = nullptr;      // [world*M][H] gathered token rows
+  int32_t* ep_idx_all = nullptr;     // [world*M][K] gathered top-k ids
+  uint16_t* ep_score_all = nullptr;  // [world*M][K] gathered route weights
+  uint16_t* ep_recv = nullptr;       // [world][M][K][H] weighted rows of this rank's tokens, per source
 };
 
 namespace {
@@ -212,6 +220,14 @@ int check_handle(const fw_moe* h, int32_t layer) {
   return FW_OK;
 }
 
+// Experts this handle holds: all of them, or this rank's contiguous share
+// under expert parallelism.
+void expert_range(const fw_moe* h, int* base, int* count) {
+  const int per = h->cfg.experts / h->ep_world;
+  *base = h->ep_rank * per;
+  *count = per;
+}
+
 int free_layer(OwnedLayer& L) {
   for (void* p : L.owned) cudaFree(p);
   L.owned.clear();
@@ -222,7 +238,98 @@ int free_layer(OwnedLayer& L) {
 
 }  // namespace
 
+namespace {
+
+// One layer under expert parallelism, stream-ordered (see fw_ep.cu): local
+// router and route, dispatch (all-gather), this rank's experts over every
+// rank's tokens plus the shared expert over its own, combine exchange, then
+// the ascending-id sum of its own tokens' rows.
+int ep_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
+               uint16_t* score, cudaStream_t cs, cudaEvent_t* ev) {
+  const fw::Shape& s = h->shape;
+  const int N = h->ep_world, T = N * T_l;
+  int base = 0, count = 0;
+  expert_range(h, &base, &count);
+  cudaError_t e = cudaSuccess;
+  auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], cs) : cudaSuccess; };
+  auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
+  if ((e = mark(0)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_router(s, L.w, h->sc, x, T_l, cs)) != cudaSuccess) return cuda_failed("router launch");
+  if ((e = mark(1)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_route_block(s, h->luts, h->sc, T_l, idx, score, false, nullptr, cs)) != cudaSuccess)
+    return cuda_failed("route launch");
+  const char* m = fw::ep_dispatch(h->ep, x, h->ep_x_all, static_cast<size_t>(T_l) * s.H, idx, h->ep_idx_all,
+                                  score, h->ep_score_all, static_cast<size_t>(T_l) * s.K, cs);
+  if (m != nullptr) return fail(FW_ENCCL, m);
+  if ((e = fw::launch_ep_schedule(s, h->sc, h->ep_idx_all, T, base, count, T_l, cs)) != cudaSuccess)
+    return cuda_failed("schedule launch");
+  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_experts(s, L.w, h->luts, h->sc, h->ep_x_all, T, h->ep_score_all, cs, x, T_l)) !=
+      cudaSuccess)
+    return cuda_failed("expert kernel launch");
+  if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
+  m = fw::ep_combine_exchange(h->ep, h->sc.weighted, h->ep_recv, static_cast<size_t>(T_l) * s.K * s.H, cs);
+  if (m != nullptr) return fail(FW_ENCCL, m);
+  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, idx, count, h->ep_recv)) != cudaSuccess)
+    return cuda_failed("combine launch");
+  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
+  return FW_OK;
+}
+
+// Replace a scratch buffer owned by the handle with one of `count` elements.
+template <typename T>
+int regrow(fw_moe* h, T** p, size_t count) {
+  auto& o = h->scratch_owned;
+  for (size_t i = 0; i < o.size(); ++i)
+    if (o[i] == static_cast<void*>(*p)) {
+      cudaFree(o[i]);
+      o.erase(o.begin() + static_cast<long>(i));
+      break;
+    }
+  *p = nullptr;
+  return alloc(h, p, count, o);
+}
+
+}  // namespace
+
 extern "C" {
+
+int fw_ep_unique_id(uint8_t id[128]) {
+  if (id == nullptr) return fail(FW_EINVAL, "id is null");
+  const char* m = fw::ep_unique_id(id);
+  return m == nullptr ? FW_OK : fail(FW_ENCCL, m);
+}
+
+int fw_moe_ep_init(fw_moe* h, int32_t rank, int32_t world, const uint8_t id[128]) {
+  if (h == nullptr || id == nullptr) return fail(FW_EINVAL, "handle / id is null");
+  if (h->ep != nullptr) return fail(FW_EINVAL, "expert parallelism is already initialised");
+  if (world < 2 || rank < 0 || rank >= world) return fail(FW_EINVAL, "need world >= 2 and 0 <= rank < world");
+  if (h->cfg.experts % world != 0) return fail(FW_EINVAL, "experts must divide evenly over the ranks");
+  if (h->cfg.max_tokens > kDecodeMaxTokens || static_cast<long long>(world) * h->cfg.max_tokens > 1024)
+    return fail(FW_EINVAL, "expert parallelism needs max_tokens <= 256 and world * max_tokens <= 1024");
+  for (const auto& L : h->layers)
+    if (L.loaded) return fail(FW_EINVAL, "initialise expert parallelism before loading layers");
+  FW_CUDA(cudaSetDevice(h->device));
+  const size_t M = h->cfg.max_tokens, G = static_cast<size_t>(world) * M;
+  const size_t K = h->cfg.top_k, H = h->cfg.hidden, I = h->cfg.intermediate, E = h->cfg.experts;
+  fw::Scratch& s = h->sc;
+  // Schedule, activations and the outgoing weighted rows cover every rank's
+  // tokens; the rest of the scratch stays per rank.
+  FW_TRY(regrow(h, &s.sched, fw::sched_words(static_cast<int>(E), static_cast<int>(G), static_cast<int>(K))));
+  FW_TRY(regrow(h, &s.act, G * K * 2 * I));
+  FW_TRY(regrow(h, &s.weighted, G * K * H));
+  FW_TRY(alloc(h, &h->ep_x_all, G * H, h->scratch_owned));
+  FW_TRY(alloc(h, &h->ep_idx_all, G * K, h->scratch_owned));
+  FW_TRY(alloc(h, &h->ep_score_all, G * K, h->scratch_owned));
+  FW_TRY(alloc(h, &h->ep_recv, G * K * H, h->scratch_owned));
+  fw::EpComm* c = nullptr;
+  const char* m = fw::ep_comm_init(rank, world, id, &c);
+  if (m != nullptr) return fail(FW_ENCCL, m);
+  h->ep = c;
+  h->ep_rank = rank;
+  h->ep_world = world;
+  return FW_OK;
+}
 
 const char* fw_last_error(void) { return g_last_error; }
 
@@ -307,6 +414,7 @@ int fw_moe_destroy(fw_moe* h) {
   if (h == nullptr) return FW_OK;
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
+  fw::ep_comm_destroy(h->ep);
   for (auto& L : h->layers) free_layer(L);
   for (void* p : h->scratch_owned) cudaFree(p);
   if (h->stream) cudaStreamDestroy(h->stream);
@@ -352,8 +460,10 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
     }
     *it.dst = d;
   }
-  // Expert banks and the shared expert go to the tiled layout through a
-  // bounded temporary buffer, a few experts at a time.
+  int ebase = 0, ecount = 0;
+  expert_range(h, &ebase, &ecount);
+  // Expert banks (this handle's experts) and the shared expert go to the
+  // tiled layout through a bounded temporary buffer, a few experts at a time.
   struct Tiled {
     fw::TiledSpec spec;
     long long n_mats;
@@ -363,9 +473,9 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
   } tiled[] = {
       {{0, static_cast<int>(H), static_cast<int>(I), static_cast<long long>(2 * I * H),
         static_cast<long long>(2 * I * H)},
-       static_cast<long long>(E), gate_up, nullptr, &L.w.gate_up},
+       ecount, gate_up + static_cast<size_t>(ebase) * 2 * I * H, nullptr, &L.w.gate_up},
       {{1, static_cast<int>(I), 0, static_cast<long long>(H * I), static_cast<long long>(H * I)},
-       static_cast<long long>(E), down, nullptr, &L.w.down},
+       ecount, down + static_cast<size_t>(ebase) * H * I, nullptr, &L.w.down},
       {{0, static_cast<int>(H), 0, static_cast<long long>(2 * Is * H), static_cast<long long>(Is * H)}, 1,
        shared_gate, shared_up, &L.w.sh_gate},
       {{1, static_cast<int>(Is), 0, static_cast<long long>(H * Is), static_cast<long long>(H * Is)}, 1,
@@ -416,9 +526,9 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
     }
     L.w.bias = d;
   }
-  L.w.expert_base = 0;
-  L.w.expert_count = static_cast<int>(E);
-  L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
+  L.w.expert_base = ebase;
+  L.w.expert_count = ecount;
+  L.prefill = h->ep == nullptr && h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
   return FW_OK;
 }
@@ -456,8 +566,11 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
     }
     *it.dst = d;
   }
-  // Expert banks and the shared expert: generated straight into the tiled
-  // layout (element values are those of their reference indices).
+  int ebase = 0, ecount = 0;
+  expert_range(h, &ebase, &ecount);
+  // Expert banks (this handle's experts) and the shared expert: generated
+  // straight into the tiled layout (element values are those of their
+  // reference indices).
   struct Tiled {
     fw::TiledSpec spec;
     long long n_mats;
@@ -466,14 +579,16 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
   } tiled[] = {
       {{0, static_cast<int>(H), static_cast<int>(I), static_cast<long long>(2 * I * H),
         static_cast<long long>(2 * I * H)},
-       static_cast<long long>(E), 1, 1, &L.w.gate_up},
+       ecount, 1, 1, &L.w.gate_up},
       {{1, static_cast<int>(I), 0, static_cast<long long>(H * I), static_cast<long long>(H * I)},
-       static_cast<long long>(E), 2, 2, &L.w.down},
+       ecount, 2, 2, &L.w.down},
       {{0, static_cast<int>(H), 0, static_cast<long long>(2 * Is * H), static_cast<long long>(Is * H)}, 1, 3, 4,
        &L.w.sh_gate},
       {{1, static_cast<int>(Is), 0, static_cast<long long>(H * Is), static_cast<long long>(H * Is)}, 1, 5, 5,
        &L.w.sh_down},
   };
+  tiled[0].spec.m0 = ebase;  // generator values of the held experts' global indices
+  tiled[1].spec.m0 = ebase;
   for (auto& t : tiled) {
     uint16_t* d = nullptr;
     const int rc = alloc(h, &d, static_cast<size_t>(t.n_mats * t.spec.mat_elems), L.owned);
@@ -512,9 +627,9 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
     free_layer(L);
     return fail(FW_ECUDA, std::string("synth: ") + cudaGetErrorString(e));
   }
-  L.w.expert_base = 0;
-  L.w.expert_count = static_cast<int>(E);
-  L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
+  L.w.expert_base = ebase;
+  L.w.expert_count = ecount;
+  L.prefill = h->ep == nullptr && h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
   return FW_OK;
 }
@@ -530,12 +645,13 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
     return fail(FW_EINVAL, "topk buffers must be 4-byte aligned");
   FW_CUDA(cudaSetDevice(h->device));
   const OwnedLayer& L = h->layers[layer];
-  const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
-  if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
   int32_t* idx = topk_idx ? topk_idx : h->idx_dev;
   uint16_t* sc = topk_scores ? topk_scores : h->score_dev;
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
   cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
+  if (h->ep != nullptr) return ep_forward(h, L, x, tokens, y, idx, sc, cs, ev);
+  const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
+  if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
   const cudaError_t e =
       prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev)
               : fw::launch_block(h->shape, L.w, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev);
@@ -546,6 +662,7 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
 int fw_moe_set_prefill_min_tokens(fw_moe* h, int32_t min_tokens) {
   if (h == nullptr) return fail(FW_EINVAL, "handle is null");
   if (min_tokens < 1) return fail(FW_EINVAL, "min_tokens must be >= 1");
+  if (h->ep != nullptr) return fail(FW_EINVAL, "the prefill path is single-GPU (expert parallelism is on)");
   if (min_tokens <= kDecodeMaxTokens && !h->prefill_ok)
     return fail(FW_EINVAL, "this block shape has no prefill path");
   h->prefill_min_tokens = min_tokens;
@@ -561,6 +678,10 @@ int fw_moe_sync(fw_moe* h, void* stream) {
   if (code != 0) {
     FW_CUDA(cudaMemset(h->sc.err, 0, sizeof(int)));
     return map_device_error(code);
+  }
+  if (h->ep != nullptr) {
+    const char* m = fw::ep_async_error(h->ep);
+    if (m != nullptr) return fail(FW_ENCCL, m);
   }
   return FW_OK;
 }

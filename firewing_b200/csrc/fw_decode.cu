@@ -275,6 +275,9 @@ struct RouteArgs {
   int tgp, qpr, qps, ops;    // expert-kernel pass size, quads/octets per slot
   int* ticket;               // CTA completion counter (zero between calls)
   int* pair_count;           // [E] prefill path: per-expert pair counts to add into (or null)
+  // Schedule scope: routed experts [ep_base, ep_base + ep_count) (expert
+  // parallelism: this GPU's experts), and the shared expert over sh_T tokens.
+  int ep_base, ep_count, sh_T;
 };
 
 // f32 total-order key with the index folded in (higher logit, then lower
@@ -348,6 +351,7 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     const int e = pidx[p];
+    if (e < a.ep_base || e >= a.ep_base + a.ep_count) continue;  // another GPU's expert
     const int t = p / K;
     atomicAdd(&cnt[e], 1);
     atomicOr(&mask[e * W + (t >> 6)], 1ull << (t & 63));
@@ -392,7 +396,7 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
     dn_pref[slot] = pd;
   }
   if (threadIdx.x == 0) {
-    const int sfull = T / a.tgp, srem = T % a.tgp;
+    const int sfull = a.sh_T / a.tgp, srem = a.sh_T % a.tgp;
     const int spad = srem <= 1 ? srem : srem <= 2 ? 2 : srem <= 4 ? 4 : 8;
     const int spcu = sfull * (4 + a.tgp) + (srem ? 4 + spad : 0);
     const int spcd = sfull * (4 + 4 * a.tgp) + (srem ? 4 + 4 * spad : 0);
@@ -406,6 +410,7 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
   // tokens that selected the same expert (an expert appears once per token).
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     const int ex_id = pidx[p];
+    if (ex_id < a.ep_base || ex_id >= a.ep_base + a.ep_count) continue;
     const int t = p / K;
     const unsigned long long* m = mask + ex_id * W;
     int rank = 0;
@@ -523,6 +528,15 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
   if (threadIdx.x == 0) *a.ticket = 0;  // ready for the next forward
 }
 
+// Expert parallelism: the schedule of this GPU's experts over every rank's
+// tokens (a.idx holds the gathered selections), built by one CTA.
+__global__ void __launch_bounds__(1024) k_schedule(RouteArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  pdl_wait();
+  pdl_launch_dependents();
+  build_schedule(a, smem);
+}
+
 // ---------------------------------------------------------------------------
 // Combine (src/decoder_layer.rs:475-545, 532-537): per token, the K weighted
 // rows are added into a bf16 accumulator in ascending expert id, rounding
@@ -530,6 +544,11 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
 struct CombineArgs {
   int H, K, T;
   const int32_t* sorted_slot;
+  // Weighted row of token t's top-k position k: t*K + k, or with expert
+  // parallelism ((idx[t][k] / ep_experts) * T + t) * K + k (rows arrive
+  // per source GPU, T tokens each).
+  const int32_t* idx;
+  int ep_experts;
   const uint16_t* weighted;
   const uint16_t* gated_sh;
   uint16_t* y;
@@ -552,10 +571,16 @@ __global__ void k_combine(CombineArgs a) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) sl[i] = n0 + i < a.K ? ss[n0 + i] : 0;
     uint4 v[8];
+    size_t row[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int src =
+          (a.idx != nullptr && n0 + i < a.K) ? a.idx[static_cast<size_t>(t) * a.K + sl[i]] / a.ep_experts : 0;
+      row[i] = (static_cast<size_t>(src) * a.T + t) * a.K + sl[i];
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      if (n0 + i < a.K)
-        v[i] = *reinterpret_cast<const uint4*>(a.weighted + (static_cast<size_t>(t) * a.K + sl[i]) * a.H + c);
+      if (n0 + i < a.K) v[i] = *reinterpret_cast<const uint4*>(a.weighted + row[i] * a.H + c);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (n0 + i < a.K) {
@@ -683,7 +708,7 @@ cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int co
 cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
                          uint16_t* score, int* err, cudaStream_t st) {
   RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-              0, 0, 0, 0, nullptr, nullptr};
+              0, 0, 0, 0, nullptr, nullptr, 0, E, T};
   return launch_route_kernel(a, st);
 }
 
@@ -714,12 +739,23 @@ cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& 
                                uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st) {
   RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
               sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, schedule ? sc.sched : nullptr, sc.up_done,
-              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket, pair_count};
+              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket, pair_count, 0, s.E, T};
   return launch_route_kernel(a, st);
 }
 
-cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st) {
-  CombineArgs a{s.H, s.K, T, sc.sorted_slot, sc.weighted, sc.gated_sh, y};
+cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_base,
+                               int ep_count, int sh_T, cudaStream_t st) {
+  RouteArgs a{nullptr, T, s.E, s.K, const_cast<int32_t*>(idx_all), nullptr, sc.err,
+              nullptr, nullptr, nullptr, nullptr, sc.sched, sc.up_done,
+              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, nullptr, nullptr, ep_base, ep_count, sh_T};
+  const int threads = (s.E + 31) / 32 * 32;
+  return launch_pdl(k_schedule, dim3(1), dim3(threads), route_smem(s.E, T, s.K, true), st, a);
+}
+
+cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
+                           const int32_t* ep_idx, int ep_experts, const uint16_t* ep_rows) {
+  CombineArgs a{s.H, s.K, T, sc.sorted_slot, ep_idx, ep_experts > 0 ? ep_experts : s.E,
+                ep_rows != nullptr ? ep_rows : sc.weighted, sc.gated_sh, y};
   return launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
 }
 
@@ -737,7 +773,7 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
   e = launch_route_block(s, luts, sc, T, topk_idx, topk_score, true, nullptr, st);
   if (e != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
   // 3. experts: gate_up + SwiGLU, then down + scale (one persistent kernel)
-  e = launch_experts(s, w, luts, sc, x, T, topk_score, st);
+  e = launch_experts(s, w, luts, sc, x, T, topk_score, st, x, T);
   if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
   // 4. combine
   e = launch_combine(s, sc, T, y, st);

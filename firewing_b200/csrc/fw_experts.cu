@@ -72,6 +72,8 @@ struct ExpertsArgs {
   uint16_t* gated_sh;          // [T][H]
   int* up_done;                // [E+1], zeroed by the route kernel
   int* err;
+  const uint16_t* sh_x;        // [sh_T][H] the shared expert's token rows
+  int sh_T;
 };
 
 // Per-launch constants, identical in every thread of a CTA.
@@ -114,7 +116,7 @@ __device__ __forceinline__ int unit_cost(int phase, int nt) { return 4 + (phase 
 
 __device__ __forceinline__ int slot_tokens(const Ctx& c, int s) {
   const ExpertsArgs& a = *c.a;
-  return s < c.n_active ? c.offs[s + 1] - c.offs[s] : a.T;
+  return s < c.n_active ? c.offs[s + 1] - c.offs[s] : a.sh_T;
 }
 
 // Slot whose cost range contains u (binary search over the prefix).
@@ -509,8 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
           uint4 out = make_uint4(0u, 0u, 0u, 0u);
           if (t < nt) {
             if (phase == 0) {
-              const int tok = routed ? pairs[t0 + t] / a.K : t0 + t;
-              out = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(tok) * a.H + c8);
+              const uint16_t* xr = routed ? a.x + static_cast<size_t>(pairs[t0 + t] / a.K) * a.H
+                                          : a.sh_x + static_cast<size_t>(t0 + t) * a.H;
+              out = *reinterpret_cast<const uint4*>(xr + c8);
             } else {
               const uint16_t* row = routed ? a.act + static_cast<size_t>(pairs[t0 + t]) * 2 * a.I
                                            : a.act_sh + static_cast<size_t>(t0 + t) * 2 * a.Is;
@@ -599,7 +602,8 @@ size_t experts_smem_bytes(const Shape& s, bool tiled) {
 }
 
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
-                           const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st) {
+                           const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st,
+                           const uint16_t* sh_x, int sh_T) {
   if (g_num_sms == 0) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -613,7 +617,7 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
   if (e != cudaSuccess) return e;
   ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, experts_tokens_per_pass(s), x, w.gate_up, w.down, w.sh_gate,
                 w.sh_up, w.sh_down, w.expert_base, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
-                sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err};
+                sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err, sh_x, sh_T};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g_num_sms);
   cfg.blockDim = dim3(kThreads);

@@ -76,6 +76,7 @@ struct TiledSpec {
   int half;                // kind 0, one source: up rows start at row `half` of it; 0: two sources
   long long mat_elems;     // elements per matrix (expert) in the tiled buffer
   long long src_mat_elems; // elements per matrix in the reference source
+  long long m0 = 0;        // synthetic generation: global index of the bank's first matrix
 };
 
 // Scratch for one forward of up to max_T tokens (device memory).
@@ -137,8 +138,11 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
 size_t experts_smem_bytes(const Shape& s, bool tiled);
 // Tokens the expert kernel stages per pass (8, or 4 for wide hidden sizes).
 int experts_tokens_per_pass(const Shape& s);
+// x / T: the routed pairs' token rows (all ranks' tokens under expert
+// parallelism); sh_x / sh_T: the tokens of the shared expert (this rank's).
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
-                           const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st);
+                           const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st,
+                           const uint16_t* sh_x, int sh_T);
 
 // Primitives (the reference crate's functions over device buffers).
 cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int cols, int T,
@@ -180,7 +184,30 @@ cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& 
                           cudaStream_t st);
 cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& sc, int T, int32_t* topk_idx,
                                uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st);
-cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st);
+// ep_idx / ep_experts / ep_rows: expert parallelism (rows per source GPU,
+// see CombineArgs); null / 0 / null on one GPU.
+cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
+                           const int32_t* ep_idx = nullptr, int ep_experts = 0, const uint16_t* ep_rows = nullptr);
+// Expert parallelism: schedule of experts [ep_base, ep_base + ep_count)
+// over the gathered selections idx_all [T][K], shared expert over sh_T tokens.
+cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_base,
+                               int ep_count, int sh_T, cudaStream_t st);
+
+// ---- expert parallelism (fw_ep.cu): NCCL, loaded at run time ---------------
+// Each returns null on success, else a message.
+struct EpComm;
+const char* ep_unique_id(unsigned char out[128]);
+const char* ep_comm_init(int rank, int world, const unsigned char id[128], EpComm** out);
+void ep_comm_destroy(EpComm* c);
+// All-gather of every rank's token rows (x_elems each), top-k ids and route
+// weights (k_elems each), one NCCL group on `st`.
+const char* ep_dispatch(EpComm* c, const uint16_t* x, uint16_t* x_all, size_t x_elems, const int32_t* idx,
+                        int32_t* idx_all, const uint16_t* score, uint16_t* score_all, size_t k_elems,
+                        cudaStream_t st);
+// Block p of `send` (block_elems bf16) to rank p, block p of `recv` from rank p.
+const char* ep_combine_exchange(EpComm* c, const uint16_t* send, uint16_t* recv, size_t block_elems,
+                                cudaStream_t st);
+const char* ep_async_error(EpComm* c);
 
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.

@@ -88,6 +88,8 @@ def library() -> ctypes.CDLL:
     L.fw_moe_forward_async.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp, vp]
     L.fw_moe_sync.argtypes = [vp, vp]
     L.fw_moe_set_prefill_min_tokens.argtypes = [vp, ctypes.c_int32]
+    L.fw_ep_unique_id.argtypes = [ctypes.c_char_p]
+    L.fw_moe_ep_init.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_char_p]
     L.fw_moe_memory.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_profile.argtypes = [vp, ctypes.c_int32]
     L.fw_moe_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
@@ -102,6 +104,7 @@ def library() -> ctypes.CDLL:
     for name in ("fw_moe_create", "fw_moe_destroy", "fw_moe_load_layer", "fw_moe_synth_layer",
                  "fw_moe_forward", "fw_moe_forward_async", "fw_moe_sync", "fw_moe_memory",
                  "fw_moe_profile", "fw_moe_profile_read", "fw_moe_set_prefill_min_tokens",
+                 "fw_ep_unique_id", "fw_moe_ep_init",
                  "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
@@ -213,6 +216,15 @@ class MoeBlock:
 
     STAGES = ("router", "route", "experts", "combine")
 
+    def ep_init(self, rank: int, world: int, unique_id: bytes) -> None:
+        """Expert parallelism: this handle holds experts [rank*E/world,
+        (rank+1)*E/world) and every forward becomes collective over the
+        `world` ranks that share `unique_id` (from ep_unique_id on one rank).
+        Call on every rank before loading layers."""
+        if len(unique_id) != 128:
+            raise ValueError("unique_id must be 128 bytes")
+        _check(library().fw_moe_ep_init(self._h, int(rank), int(world), bytes(unique_id)))
+
     def set_prefill_min_tokens(self, min_tokens: int) -> None:
         """Forwards of at least min_tokens tokens (and all above 256) take the
         tensor-core prefill path; narrower ones the bit-exact decode path."""
@@ -231,6 +243,30 @@ class MoeBlock:
         v = ctypes.c_uint64()
         _check(library().fw_moe_memory(self._h, ctypes.byref(v)))
         return int(v.value)
+
+
+def ep_expert_range(experts: int, world: int, rank: int):
+    """(first expert, count) held by `rank` under expert parallelism."""
+    if experts % world:
+        raise ValueError("experts must divide evenly over the ranks")
+    per = experts // world
+    return rank * per, per
+
+
+def ep_combine_row(expert: int, t_local: int, k: int, tokens_local: int, top_k: int,
+                   experts_per_rank: int) -> int:
+    """Row of the combine's receive buffer that holds the weighted output of
+    expert `expert` for the owner's token t_local at top-k position k: the
+    rows arrive as one [tokens_local][top_k] block per source rank."""
+    src = expert // experts_per_rank
+    return (src * tokens_local + t_local) * top_k + k
+
+
+def ep_unique_id() -> bytes:
+    """A fresh NCCL communicator id (128 bytes) for MoeBlock.ep_init."""
+    buf = ctypes.create_string_buffer(128)
+    _check(library().fw_ep_unique_id(buf))
+    return buf.raw
 
 
 def forward_noalloc(config: MoeConfig, weights: dict, x, tokens: int, y, topk_idx=None,

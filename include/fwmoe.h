@@ -121,6 +121,27 @@ int fw_moe_forward_async(fw_moe* handle, int32_t layer, const uint16_t* x, int32
  * FW_EINVAL when min_tokens <= 256 and the shape has no prefill path. */
 int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);
 
+/* Expert parallelism over the GPUs of one node (no reference counterpart:
+ * the reference runs the block on one device).  Rank r of `world` holds the
+ * routed experts [r*E/world, (r+1)*E/world) of every layer (router, shared
+ * expert and bias replicated) and brings its own tokens to each forward.
+ * Per layer: router and route on the rank's tokens, an all-gather of every
+ * rank's token rows, top-k ids and route weights, this rank's experts over
+ * all gathered tokens, a grouped send/recv that returns each token's
+ * weighted rows to its owner, and the owner's ascending-id sum, so outputs
+ * are bit-identical to the single-GPU decode path.  NCCL (libnccl.so.2) is
+ * loaded at run time.
+ *   fw_ep_unique_id: a communicator id; make it on one rank and hand the
+ *     128 bytes to every rank (any host transport).
+ *   fw_moe_ep_init: on every rank, collectively, after fw_moe_create and
+ *     before any layer is loaded.  Needs experts % world == 0,
+ *     max_tokens <= 256 and world * max_tokens <= 1024.  Afterwards every
+ *     forward on the handle is collective: all ranks call it for the same
+ *     layer with the same token count, in the same order; the prefill path
+ *     is not available (decode widths only).  FW_ENCCL on collective errors. */
+int fw_ep_unique_id(uint8_t id[128]);
+int fw_moe_ep_init(fw_moe* handle, int32_t rank, int32_t world, const uint8_t id[128]);
+
 /* Wait for `stream`, then report and clear device-side status. */
 int fw_moe_sync(fw_moe* handle, void* stream);
 

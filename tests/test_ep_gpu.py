@@ -1,0 +1,109 @@
+"""Expert parallelism on two GPUs through the C ABI: each rank holds half the
+experts (fw_moe_ep_init), brings its own tokens, and must return exactly the
+single-GPU decode result for them (the oracle's block output, bit for bit
+where scores match; the same selection everywhere).  Skipped with fewer than
+two GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import torch.multiprocessing as mp  # noqa: E402
+
+SMALL = dict(hidden=256, intermediate=128, shared_intermediate=192, experts=64, top_k=4)
+CFG0 = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, shape, t_local, layers, zipf, q):
+    import torch.distributed as dist
+
+    import firewing_b200 as fw
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    # No NVLink multicast objects in a test that may stop a rank early.
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        uid = [fw.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        cfg = fw.MoeConfig(**shape, max_tokens=t_local, layers=layers)
+        blk = fw.MoeBlock(cfg, device=rank)
+        blk.ep_init(rank, world, uid[0])
+        for l in range(layers):
+            blk.synth_layer(l, 40 + l, 0.02, zipf)
+        results = []
+        for l in range(layers):
+            x_all = O.synth_input(900 + l, world * t_local, shape["hidden"])
+            x = x_all[rank * t_local:(rank + 1) * t_local].copy()
+            y1, i1, s1 = blk.forward(l, x)
+            y2, i2, s2 = blk.forward(l, x)  # repeatable
+            results.append((l, x_all, y1, i1, s1, bool(np.array_equal(y1, y2) and np.array_equal(i1, i2))))
+        blk.close()
+        gathered = [None] * world
+        dist.all_gather_object(gathered, [(l, y, i, s, rep) for (l, _, y, i, s, rep) in results])
+        if rank == 0:
+            bshape = O.BlockShape(**shape)
+            report = []
+            for l in range(layers):
+                x_all = results[l][1]
+                y = np.concatenate([gathered[r][l][1] for r in range(world)])
+                i = np.concatenate([gathered[r][l][2] for r in range(world)])
+                s = np.concatenate([gathered[r][l][3] for r in range(world)])
+                rep = all(gathered[r][l][4] for r in range(world))
+                ry, ridx, rsc = O.block(bshape, O.SynthLayer(bshape, 40 + l, 0.02, zipf), x_all,
+                                        threads=os.cpu_count() or 1)
+                exact = np.all(s == rsc, axis=1)
+                report.append(dict(idx=bool(np.array_equal(i, ridx)),
+                                   score_ulp=int(np.abs(s.astype(np.int32) - rsc.astype(np.int32)).max()),
+                                   exact_tokens_equal=bool(np.array_equal(y[exact], ry[exact])),
+                                   n_exact=int(exact.sum()), repeat=rep))
+            q.put(report)
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(shape, t_local, layers, zipf):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, t_local, layers, zipf, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join(timeout=30)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return q.get(timeout=5)
+
+
+@pytest.mark.parametrize("t_local,zipf", [(1, False), (7, False), (32, True)])
+def test_ep_two_gpus_small_shape(t_local, zipf):
+    for r in _run(SMALL, t_local, 2, zipf):
+        assert r["idx"] and r["score_ulp"] <= 1 and r["exact_tokens_equal"] and r["repeat"], r
+
+
+def test_ep_two_gpus_config0_shape():
+    for r in _run(CFG0, 32, 1, False):
+        assert r["idx"] and r["score_ulp"] <= 1 and r["exact_tokens_equal"] and r["repeat"], r
