@@ -33,6 +33,12 @@ WORKLOADS = {
                  layers=24, tokens=64, zipf=False,
                  name="cfg1: 24-layer stack of the config-0 block, decode"),
 }
+# Reported alongside at N > 1 (not the headline): BASELINE config 3, expert
+# parallelism over the N GPUs.
+EP = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10,
+          tokens=256, layers=24, layers_8=48,
+          name="cfg3: {layers}-layer stack of the config-0 block, EP over {world} GPUs ({per} experts "
+               "per GPU), decode T=256 per layer, uniform routing")
 # Reported alongside (not the headline): BASELINE config 2, one block at
 # prefill width with the Zipf-biased router, on the tensor-core path.
 PREFILL = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10,
@@ -381,6 +387,9 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     blk.close()
     prefill = None if args.no_prefill else measure_prefill(args, rank, world, local_rank, peaks, stream,
                                                           max_over_ranks, barrier)
+    ep = None
+    if world > 1 and not args.no_ep:
+        ep = measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist)
 
     cpu = None
     parity = None
@@ -421,6 +430,7 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             "parity_sample": parity,
             "t4": t4,
             "prefill": prefill,
+            "ep": ep,
         }
         print(json.dumps(line), flush=True)
 
@@ -492,6 +502,75 @@ def measure_prefill(args, rank, world, local_rank, peaks, stream, max_over_ranks
     }
 
 
+def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist):
+    """BASELINE config 3 on `world` GPUs with expert parallelism: decode of
+    256 tokens per layer in total (256/world per rank), uniform routing, a
+    48-layer stack at 8 GPUs (64 experts per GPU), 24 layers at 2 or 4.
+    Rank r holds experts [r*512/world, (r+1)*512/world) of every layer; each
+    forward gathers every rank's tokens, runs the local experts, returns the
+    weighted rows to their owners over NCCL and sums them there."""
+    import torch
+
+    import firewing_b200 as fw
+    from firewing_b200 import synth
+
+    p = EP
+    T_l = p["tokens"] // world
+    L = p["layers_8"] if world >= 8 else p["layers"]
+    H, K, E, I, Is = p["hidden"], p["top_k"], p["experts"], p["intermediate"], p["shared_intermediate"]
+    uid = [fw.ep_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    blk = fw.MoeBlock(fw.MoeConfig(H, I, Is, E, K, max_tokens=T_l, layers=L), device=local_rank)
+    blk.ep_init(rank, world, uid[0])
+    for l in range(L):
+        blk.synth_layer(l, layer_seed(l), 0.02, False)
+    xs = np.stack([synth.synth_input(input_seed(rank, l), T_l, H) for l in range(L)])
+    x = torch.from_numpy(xs.view(np.int16)).cuda()
+    y = torch.empty((L, T_l, H), dtype=torch.int16, device="cuda")
+    idx = torch.empty((L, T_l, K), dtype=torch.int32, device="cuda")
+    sc = torch.empty((L, T_l, K), dtype=torch.int16, device="cuda")
+
+    def step():
+        for l in range(L):
+            blk.forward_async(l, x[l], T_l, y[l], idx[l], sc[l], stream=stream)
+
+    steps = max(3, args.steps // 2)
+    for _ in range(max(3, args.warmup)):
+        step()
+    blk.sync(stream)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    blk.sync(stream)
+    el = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    # this rank's distinct local experts per layer (from every rank's picks)
+    ids = idx.cpu().numpy()
+    t_ids = torch.from_numpy(ids.astype(np.int32)).cuda()
+    all_ids = [torch.empty_like(t_ids) for _ in range(world)]
+    dist.all_gather(all_ids, t_ids)
+    base, per = fw.ep_expert_range(E, world, rank)
+    cat = np.concatenate([a.cpu().numpy() for a in all_ids], axis=1)
+    local_u = [int(((np.unique(cat[l]) >= base) & (np.unique(cat[l]) < base + per)).sum()) for l in range(L)]
+    layer_bytes = [u * 3 * H * I * 2 + E * H * 2 + 3 * H * Is * 2 for u in local_u]
+    gbs = sum(layer_bytes) * steps / el / 1e9
+    gbs = max_over_ranks(-gbs) * -1  # slowest rank's streaming rate
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0)) if peaks else 6650.0
+    blk.close()
+    return {
+        "workload": p["name"].format(world=world, per=E // world, layers=L),
+        "tokens_per_layer": T_l * world, "tokens_per_rank": T_l, "layers": L, "steps": steps,
+        "value": T_l * world * L * steps / el, "unit": UNIT, "ms_per_step": el / steps * 1e3,
+        "per_gpu_gbs_min": gbs, "per_gpu_frac_hbm_min": gbs / hbm_peak,
+        "parallelism": f"ep{world} (experts {E // world} per GPU) + dp tokens",
+        "exchange": "NCCL all-gather (rows, ids, weights) + grouped send/recv of weighted rows",
+    }
+
+
 class _Null:
     def __enter__(self):
         return self
@@ -511,6 +590,7 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill line item")
+    ap.add_argument("--no-ep", action="store_true", help="skip the config-3 expert-parallel line item (N > 1)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--minimal", action="store_true",
                     help="timed steps only (no T=4 pass, e2e, stage profile or CPU leg); "
