@@ -63,8 +63,8 @@ namespace {
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kBK = 64;         // columns per ring stage (one 128-byte swizzle atom)
 constexpr int kBN = 256;        // tokens per work unit (MMA N, max)
-constexpr int kRingA = 6;       // weight-tile ring stages
-constexpr int kRingB = 3;       // token-tile ring stages
+constexpr int kRingA = 4;       // weight-tile ring stages
+constexpr int kRingB = 4;       // token-tile ring stages
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kStageBytes = 32 * kBM * 2;  // epilogue staging per set: 32 tokens x 128 rows, bf16
