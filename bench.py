@@ -591,6 +591,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill line item")
     ap.add_argument("--no-ep", action="store_true", help="skip the config-3 expert-parallel line item (N > 1)")
+    ap.add_argument("--only-prefill", action="store_true",
+                    help="run only the config-2 prefill measurement and print it (for ncu captures)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--minimal", action="store_true",
                     help="timed steps only (no T=4 pass, e2e, stage profile or CPU leg); "
@@ -601,6 +603,18 @@ def main() -> None:
     local_rank = env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         run_reference(args, w, rank)
+        return
+    if args.only_prefill:
+        import torch
+
+        torch.cuda.set_device(local_rank)
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except Exception:
+            pass
+        pre = measure_prefill(args, rank, 1, local_rank, peaks, torch.cuda.Stream(), lambda v: v, lambda: None)
+        print(json.dumps({"only_prefill": True, "prefill": pre}), flush=True)
         return
     if world > 1:
         import datetime

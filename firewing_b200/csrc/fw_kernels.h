@@ -86,8 +86,9 @@ struct Scratch {
   uint16_t* sh_sig = nullptr;    // [T]
   int32_t* sorted_slot = nullptr;  // [T][K] slots in ascending expert order
   int32_t* sched = nullptr;      // schedule words, see sched_* helpers
-  uint16_t* act = nullptr;       // [T*K][2I] gate | up rows (SwiGLU applied on staging)
-  uint16_t* act_sh = nullptr;    // [T][2Is]
+  uint16_t* act = nullptr;       // decode: [T*K][2I] gate | up rows (SwiGLU applied on staging);
+                                 // prefill: SwiGLU rows K-blocked, [I/64][T*K][64]
+  uint16_t* act_sh = nullptr;    // decode: [T][2Is]; prefill: [Is/64][T][64]
   uint16_t* weighted = nullptr;  // [T*K][H]
   uint16_t* gated_sh = nullptr;  // [T][H]
   int* up_done = nullptr;        // [E+1] per-slot SwiGLU completion counters
@@ -100,7 +101,7 @@ struct Scratch {
   int* pair_offset = nullptr;    // [E+1] first pair of each expert in grouped order
   int* unit_prefix = nullptr;    // [2][E+2] GEMM work-unit prefix per slot, up and down phases
   int32_t* pair_tk = nullptr;    // [T*K] grouped pairs: t*K + top-k position
-  uint16_t* xg = nullptr;        // [T*K][H] input rows in grouped pair order
+  uint16_t* xg = nullptr;        // input rows in grouped pair order, K-blocked: [H/64][T*K][64]
 };
 
 // Schedule layout inside Scratch::sched (int32 words), written by the route

@@ -25,9 +25,7 @@
 //   warp 0  producer: TMA loads of the weight tile (4-D map over the tiled
 //           bank: 128 rows x 64 columns = 16 KB, already in the 128-byte
 //           swizzled K-major operand layout) and of the token tile (16-row
-//           boxes of contiguous rows, 128-byte swizzle) into a 4-stage ring;
-//           at each unit start it prefetches the weight tiles of its next
-//           unit into L2.
+//           boxes of contiguous rows, 128-byte swizzle) into a 4-stage ring.
 //   warp 1  MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> f32),
 //           M = 128 weight rows, N = the unit's tokens rounded up to 16
 //           (<= 256), K = 64 per stage as 4 instructions; accumulators in
@@ -83,12 +81,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map), "r"(c0), "r"(c1),
-               "r"(c2), "r"(c3)
-               : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
@@ -174,6 +166,11 @@ struct GemmArgs {
   int kb_r, kb_s;          // 64-column stages per unit (routed, shared)
   int mt_r, mt_s;          // 128-row tiles per chunk (routed, shared)
   int groups_r;            // 8-row groups per routed expert matrix
+  // K-blocked token operands ([K/64][rows][64]): rows per 64-column block of
+  // the routed operand (xg / act: pair capacity) and of the shared one
+  // (act_sh: token capacity); b_blocked_s = 0 when the shared up operand is
+  // the row-major input x.
+  int rows_r, rows_s, b_blocked_s;
   const int* offset;       // [E+1] grouped pair offsets
   const int* prefix;       // [E+2] unit prefix of this phase (slot E = shared)
   const int32_t* pair_tk;  // [pairs] t*K + k
@@ -329,18 +326,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint64_t policy = l2_evict_first_policy();
     produce(
         a, s_prefix, s_offset, total, tail, tail->full_a, tail->empty_a, kRingA, lane,
-        [&](const Unit&, int u) {
-          // Pull the weight tiles of this CTA's next unit into L2 while this
-          // one streams, so its loads meet L2 instead of HBM latency.
-          const int un = u + gridDim.x;
-          if (un < total) {
-            const Unit nx = decode_unit(a, s_prefix, s_offset, un);
-            const int ngrp = (nx.routed ? nx.slot * a.groups_r : 0) + nx.m * (kBM / 8);
-            const CUtensorMap* nma = nx.routed ? &map_a_r : &map_a_s;
-            for (int kb = lane; kb < nx.kblocks; kb += 32) tma_prefetch_4d(nma, 0, 0, kb, ngrp);
-          }
-          return static_cast<uint32_t>(kABytes);
-        },
+        [&](const Unit&, int) { return static_cast<uint32_t>(kABytes); },
         [&](const Unit& w, int kb, int st, uint64_t* bar) {
           const int grp0 = (w.routed ? w.slot * a.groups_r : 0) + w.m * (kBM / 8);
           if (lane == 0) tma_load_4d(ring_a + st * kABytes, w.routed ? &map_a_r : &map_a_s, 0, 0, kb, grp0, bar, policy);
@@ -353,7 +339,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         [&](const Unit& w, int kb, int st, uint64_t* bar) {
           unsigned char* sb = ring_b + st * kBBytes;
           const CUtensorMap* mb = w.routed ? &map_b_r : &map_b_s;
-          for (int j = lane * 16; j < w.bn; j += 512) tma_load_2d(sb + j * 128, mb, kb * kBK, w.n0 + j, bar);
+          // K-blocked operands: block kb's rows n0.. are one contiguous run.
+          const bool blocked = w.routed || a.b_blocked_s;
+          const int c0 = blocked ? 0 : kb * kBK;
+          const int r0 = (blocked ? kb * (w.routed ? a.rows_r : a.rows_s) : 0) + w.n0;
+          for (int j = lane * 16; j < w.bn; j += 512) tma_load_2d(sb + j * 128, mb, c0, r0 + j, bar);
         });
   } else if (warp == 2) {
     // ---------------- MMA issuer ----------------
@@ -474,12 +464,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         epi_sync(set);
         const int rows_here = min(32, w.nvalid - c0);
         if (a.phase == 0) {
-          // [32 tokens][64 intermediates]: 8 chunks of 16 bytes per token.
-          uint16_t* dst = w.routed ? a.act : a.act_sh;
-          const int width = w.routed ? a.I : a.Is;
+          // [32 tokens][64 intermediates] = rows of K-block m of act
+          // ([I/64][rows][64]): 8 chunks of 16 bytes per token.
+          uint16_t* dst = (w.routed ? a.act : a.act_sh) +
+                          static_cast<size_t>(w.m) * (w.routed ? a.rows_r : a.rows_s) * 64;
           for (int ch = et; ch < rows_here * 8; ch += 128) {
             const int r = ch >> 3, c = ch & 7;
-            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(w.n0 + c0 + r) * width + w.m * 64 + c * 8) =
+            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(w.n0 + c0 + r) * 64 + c * 8) =
                 *reinterpret_cast<const uint4*>(stage + r * 64 + c * 8);
           }
         } else {
@@ -780,9 +771,10 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
 
 // One warp per (token, top-k position): its slot in its expert's group, and
 // a copy of the token's input row into the grouped input (so the gate/up
-// GEMM reads each expert's token rows as one contiguous block).
+// GEMM reads each expert's token rows of a 64-column block as one
+// contiguous run).
 __global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, const int* offset, int* fill,
-                             int32_t* pair_tk, const uint16_t* x, uint16_t* xg, int* err) {
+                             int32_t* pair_tk, const uint16_t* x, uint16_t* xg, long long xg_rows, int* err) {
   pdl_wait();
   pdl_launch_dependents();
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -800,9 +792,11 @@ __global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, co
   }
   p = __shfl_sync(0xffffffffu, p, 0);
   if (p < 0) return;
+  // xg is K-blocked, [H/64][xg_rows][64]: 16-byte chunk c of the row goes
+  // to block c / 8, row p, chunk c % 8.
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(i / K) * H);
-  uint4* dst = reinterpret_cast<uint4*>(xg + static_cast<size_t>(p) * H);
-  for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+  for (int c = lane; c < H / 8; c += 32)
+    *reinterpret_cast<uint4*>(xg + ((static_cast<size_t>(c >> 3) * xg_rows + p) * 64 + (c & 7) * 8)) = src[c];
 }
 
 template <typename Kern, typename... Args>
@@ -901,9 +895,10 @@ bool make_prefill_weight_maps(const Shape& s, const LayerWeights& w, PrefillWeig
 
 bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratchMaps* out) {
   if (!prefill_supported(s)) return false;
-  return rows_map(&out->xg, sc.xg, s.H, static_cast<long long>(sc.max_T) * s.K, 16) &&
-         rows_map(&out->act, sc.act, s.I, static_cast<long long>(sc.max_T) * s.K, 16) &&
-         rows_map(&out->act_sh, sc.act_sh, s.Is, sc.max_T, 16);
+  // K-blocked [K/64][rows][64] operands as 64-column row-major views.
+  const long long P = static_cast<long long>(sc.max_T) * s.K, M = sc.max_T;
+  return rows_map(&out->xg, sc.xg, 64, (s.H / 64) * P, 16) && rows_map(&out->act, sc.act, 64, (s.I / 64) * P, 16) &&
+         rows_map(&out->act_sh, sc.act_sh, 64, (s.Is / 64) * M, 16);
 }
 
 cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
@@ -939,7 +934,7 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
     if ((e = launch_pdl_ex(k_pf_scatter, dim3((TK + 7) / 8), dim3(256), 0, st,
                            static_cast<const int32_t*>(topk_idx), TK, s.K, s.E, s.H,
                            static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x, sc.xg,
-                           sc.err)) != cudaSuccess)
+                           static_cast<long long>(sc.max_T) * s.K, sc.err)) != cudaSuccess)
       return e;
   }
   if ((e = mark(2)) != cudaSuccess) return e;
@@ -969,6 +964,9 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   g.mt_r = 2 * s.I / kBM;
   g.mt_s = 2 * s.Is / kBM;
   g.groups_r = 2 * s.I / 8;
+  g.rows_r = sc.max_T * s.K;
+  g.rows_s = sc.max_T;
+  g.b_blocked_s = 0;  // shared up: the row-major input
   g.prefix = sc.unit_prefix;
   if ((e = launch_pdl_ex(k_gemm, grid, block, smem, st, wm.gate_up, wm.sh_gate_up, smaps.xg, x_rows, g)) !=
       cudaSuccess)
@@ -980,6 +978,7 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   g.mt_r = s.H / kBM;
   g.mt_s = s.H / kBM;
   g.groups_r = s.H / 8;
+  g.b_blocked_s = 1;  // shared down: K-blocked act_sh
   g.prefix = sc.unit_prefix + s.E + 2;
   if ((e = launch_pdl_ex(k_gemm, grid, block, smem, st, wm.down, wm.sh_down, smaps.act, smaps.act_sh, g)) !=
       cudaSuccess)

@@ -174,6 +174,16 @@ def test_block_config0_shape(T, zipf):
     assert_block_close(got[0], ref[0], got[1], ref[1], got[2], ref[2], ref[3]["logits"])
 
 
+CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512, top_k=10)
+
+
+@pytest.mark.parametrize("T", [1, 4, 33])
+def test_block_config4_shape_zipf(T):
+    # BASELINE config 4's block (H=3072, I=Is=768) on the decode path.
+    _, _, _, got, ref = run_pair(CFG4, 3, T, zipf=True)
+    assert_block_close(got[0], ref[0], got[1], ref[1], got[2], ref[2], ref[3]["logits"])
+
+
 def test_block_all_ties_input():
     # x = 0 -> every logit 0: selection 0..K-1, equal scores (tie rule).
     x = np.zeros((2, SMALL["hidden"]), dtype=np.uint16)

@@ -24,6 +24,8 @@ REL_L2 = 1e-3
 # H, 2I and 2Is multiples of 128 (the prefill tile height).
 SMALL = dict(hidden=256, intermediate=128, shared_intermediate=192, experts=64, top_k=4)
 CFG0 = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10)
+# BASELINE config 4's block: wider hidden and expert FFNs, Zipf-biased router.
+CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512, top_k=10)
 
 
 def errors(y, y_ref):
@@ -79,6 +81,12 @@ def test_prefill_small_shape_zipf_multi_chunk():
 @pytest.mark.parametrize("T,zipf", [(64, False), (257, False), (640, True)])
 def test_prefill_config0_shape(T, zipf):
     _, _, got, ref = run(CFG0, 0, T, zipf=zipf, min_tokens=1)
+    assert_prefill_close(got, ref)
+
+
+@pytest.mark.parametrize("T", [48, 300])
+def test_prefill_config4_shape(T):
+    _, _, got, ref = run(CFG4, 2, T, zipf=True, min_tokens=1)
     assert_prefill_close(got, ref)
 
 
