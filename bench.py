@@ -339,21 +339,24 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
                 "stage_ms_per_layer": {k_: v_ / prof_n for k_, v_ in stage_tot.items()}}
 
     # secondary: T=4 (MTP-verify width) on the same stack
-    t4 = None
-    if T != 4:
-        bufs4 = make_bufs(4)
-        el4 = timed(4, bufs4, args.steps, args.warmup)
-        idx4 = bufs4[2].cpu().numpy()
-        u4 = [len(np.unique(idx4[l])) for l in range(L)]
-        b4 = sum(algorithmic_bytes(w, 4, u) for u in u4)
-        st4, kb4, n4 = stage_profile(4, bufs4, u4)
-        t4 = {"tokens": 4, "value": world * 4 * L * args.steps / el4,
-              "ms_per_step": el4 / args.steps * 1e3,
-              "block_gbs": b4 * args.steps / el4 / 1e9 * (1 if world == 1 else world),
-              "block_frac_hbm": b4 * args.steps / el4 / 1e9 / hbm_peak,
-              "experts_gbs": kb4 / (st4["experts"] / 1e3) / 1e9,
-              "stage_ms_per_layer": {k_: v_ / n4 for k_, v_ in st4.items()}}
-        del bufs4
+    # secondary widths on the same stack: T=4 (MTP-verify width) and T=1
+    # (batch-1 decode, config 0's width)
+    def narrow(tokens):
+        bufs_n = make_bufs(tokens)
+        el_n = timed(tokens, bufs_n, args.steps, args.warmup)
+        idx_n = bufs_n[2].cpu().numpy()
+        u_n = [len(np.unique(idx_n[l])) for l in range(L)]
+        b_n = sum(algorithmic_bytes(w, tokens, u) for u in u_n)
+        st_n, kb_n, n_n = stage_profile(tokens, bufs_n, u_n)
+        return {"tokens": tokens, "value": world * tokens * L * args.steps / el_n,
+                "ms_per_step": el_n / args.steps * 1e3,
+                "block_gbs": b_n * args.steps / el_n / 1e9 * (1 if world == 1 else world),
+                "block_frac_hbm": b_n * args.steps / el_n / 1e9 / hbm_peak,
+                "experts_gbs": kb_n / (st_n["experts"] / 1e3) / 1e9,
+                "stage_ms_per_layer": {k_: v_ / n_n for k_, v_ in st_n.items()}}
+
+    t4 = narrow(4) if T != 4 else None
+    t1 = narrow(1) if T != 1 else None
 
     # end to end through the C ABI with HOST buffers (fw_moe_forward per layer)
     xh = torch.from_numpy(np.stack([synth.synth_input(input_seed(rank, l), T, H)
@@ -429,6 +432,7 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             "cpu_baseline": cpu,
             "parity_sample": parity,
             "t4": t4,
+            "t1": t1,
             "prefill": prefill,
             "ep": ep,
         }

@@ -167,7 +167,14 @@ struct fw_moe {
   uint16_t* ep_x_all = nullptr;      // [world*M][H] gathered token rows
   int32_t* ep_idx_all = nullptr;     // [world*M][K] gathered top-k ids
   uint16_t* ep_score_all = nullptr;  // [world*M][K] gathered route weights
-  uint16_t* ep_recv = nullptr;       // [world][M][K][H] weighted rows of this rank's tokens, per source
+  uint16_t* ep_recv = nullptr;       // weighted rows of this rank's tokens, per source
+  int ep_decode_max = 0;             // widest forward the expert-parallel decode path takes
+  // expert-parallel prefill: packed exchange positions and counts
+  int32_t* ep_send_pos = nullptr;    // [world*M*K]
+  int32_t* ep_recv_pos = nullptr;    // [M*K]
+  int* ep_counts = nullptr;          // device [4][world]: send rows, send offsets, recv rows, recv offsets
+  int* ep_counts_host = nullptr;     // pinned copy
+  cudaEvent_t ep_counts_ev = nullptr;
 };
 
 namespace {
@@ -276,6 +283,57 @@ int ep_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint1
   return FW_OK;
 }
 
+// One layer of the prefill path under expert parallelism: local router and
+// route, dispatch (all-gather), this rank's experts grouped over every rank's
+// pairs and run as the tensor-core GEMMs (plus the shared expert over its own
+// tokens), the weighted rows packed per destination in (token, k) order,
+// a row-sized exchange (counts read on the host while the GEMMs run), then
+// the owner's ascending-id sum.
+int ep_prefill_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
+                       uint16_t* score, cudaStream_t cs, cudaEvent_t* ev) {
+  const fw::Shape& s = h->shape;
+  const int N = h->ep_world, T = N * T_l;
+  int base = 0, count = 0;
+  expert_range(h, &base, &count);
+  cudaError_t e = cudaSuccess;
+  auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], cs) : cudaSuccess; };
+  auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
+  if ((e = mark(0)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_prefill_front(s, L.w, h->luts, h->sc, x, T_l, idx, score, false, cs)) != cudaSuccess)
+    return cuda_failed("router / route launch");
+  if ((e = mark(1)) != cudaSuccess) return cuda_failed("event");
+  const char* m = fw::ep_dispatch(h->ep, x, h->ep_x_all, static_cast<size_t>(T_l) * s.H, idx, h->ep_idx_all,
+                                  score, h->ep_score_all, static_cast<size_t>(T_l) * s.K, cs);
+  if (m != nullptr) return fail(FW_ENCCL, m);
+  if ((e = fw::launch_prefill_group(s, h->sc, h->ep_idx_all, T * s.K, h->ep_x_all, base, count, T_l, true, cs)) !=
+      cudaSuccess)
+    return cuda_failed("grouping launch");
+  int* cnt = h->ep_counts;
+  if ((e = fw::launch_ep_positions(h->ep_idx_all, T * s.K, T_l * s.K, count, h->ep_rank, N, false, h->ep_send_pos,
+                                   cnt, cnt + N, cs)) != cudaSuccess ||
+      (e = fw::launch_ep_positions(idx, T_l * s.K, T_l * s.K, count, h->ep_rank, N, true, h->ep_recv_pos, cnt + 2 * N,
+                                   cnt + 3 * N, cs)) != cudaSuccess)
+    return cuda_failed("exchange positions launch");
+  if ((e = cudaMemcpyAsync(h->ep_counts_host, cnt, 4 * N * sizeof(int), cudaMemcpyDeviceToHost, cs)) != cudaSuccess ||
+      (e = cudaEventRecord(h->ep_counts_ev, cs)) != cudaSuccess)
+    return cuda_failed("exchange counts");
+  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_prefill_gemms(s, L.maps, h->pf_maps, h->luts, h->sc, x, T_l, count, h->ep_score_all,
+                                    h->ep_send_pos, h->sc.weighted, cs)) != cudaSuccess)
+    return cuda_failed("GEMM launch");
+  if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
+  // The GEMMs keep running while the host reads the exchange sizes.
+  if ((e = cudaEventSynchronize(h->ep_counts_ev)) != cudaSuccess) return cuda_failed("exchange counts");
+  const int* hc = h->ep_counts_host;
+  m = fw::ep_exchange_rows(h->ep, h->sc.weighted, hc, hc + N, h->ep_recv, hc + 2 * N, hc + 3 * N,
+                           static_cast<size_t>(s.H), cs);
+  if (m != nullptr) return fail(FW_ENCCL, m);
+  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, nullptr, 0, h->ep_recv, h->ep_recv_pos)) != cudaSuccess)
+    return cuda_failed("combine launch");
+  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
+  return FW_OK;
+}
+
 // Replace a scratch buffer owned by the handle with one of `count` elements.
 template <typename T>
 int regrow(fw_moe* h, T** p, size_t count) {
@@ -303,31 +361,51 @@ int fw_ep_unique_id(uint8_t id[128]) {
 int fw_moe_ep_init(fw_moe* h, int32_t rank, int32_t world, const uint8_t id[128]) {
   if (h == nullptr || id == nullptr) return fail(FW_EINVAL, "handle / id is null");
   if (h->ep != nullptr) return fail(FW_EINVAL, "expert parallelism is already initialised");
-  if (world < 2 || rank < 0 || rank >= world) return fail(FW_EINVAL, "need world >= 2 and 0 <= rank < world");
+  if (world < 2 || world > 8 || rank < 0 || rank >= world)
+    return fail(FW_EINVAL, "need 2 <= world <= 8 and 0 <= rank < world");
   if (h->cfg.experts % world != 0) return fail(FW_EINVAL, "experts must divide evenly over the ranks");
-  if (h->cfg.max_tokens > kDecodeMaxTokens || static_cast<long long>(world) * h->cfg.max_tokens > 1024)
-    return fail(FW_EINVAL, "expert parallelism needs max_tokens <= 256 and world * max_tokens <= 1024");
   for (const auto& L : h->layers)
     if (L.loaded) return fail(FW_EINVAL, "initialise expert parallelism before loading layers");
   FW_CUDA(cudaSetDevice(h->device));
-  const size_t M = h->cfg.max_tokens, G = static_cast<size_t>(world) * M;
+  const size_t M = h->cfg.max_tokens, W = static_cast<size_t>(world);
+  // Decode width under expert parallelism: the schedule spans every rank's
+  // tokens and is built by one CTA (at most 1024 tokens in total).
+  const size_t Md = std::min<size_t>(std::min<size_t>(M, kDecodeMaxTokens), 1024 / W);
+  // Prefill buffers whenever the shape has the path: fw_moe_set_prefill_min_tokens
+  // can send any width there.
+  const bool prefill = h->prefill_ok;
   const size_t K = h->cfg.top_k, H = h->cfg.hidden, I = h->cfg.intermediate, E = h->cfg.experts;
   fw::Scratch& s = h->sc;
   // Schedule, activations and the outgoing weighted rows cover every rank's
   // tokens; the rest of the scratch stays per rank.
-  FW_TRY(regrow(h, &s.sched, fw::sched_words(static_cast<int>(E), static_cast<int>(G), static_cast<int>(K))));
-  FW_TRY(regrow(h, &s.act, G * K * 2 * I));
-  FW_TRY(regrow(h, &s.weighted, G * K * H));
-  FW_TRY(alloc(h, &h->ep_x_all, G * H, h->scratch_owned));
-  FW_TRY(alloc(h, &h->ep_idx_all, G * K, h->scratch_owned));
-  FW_TRY(alloc(h, &h->ep_score_all, G * K, h->scratch_owned));
-  FW_TRY(alloc(h, &h->ep_recv, G * K * H, h->scratch_owned));
+  const size_t Gd = W * Md, Gp = prefill ? W * M : 0;
+  FW_TRY(regrow(h, &s.sched, fw::sched_words(static_cast<int>(E), static_cast<int>(Gd), static_cast<int>(K))));
+  FW_TRY(regrow(h, &s.act, std::max(Gd * K * 2 * I, Gp * K * I)));
+  FW_TRY(regrow(h, &s.weighted, std::max(Gd * K * H, Gp * K * H)));
+  FW_TRY(alloc(h, &h->ep_x_all, W * M * H, h->scratch_owned));
+  FW_TRY(alloc(h, &h->ep_idx_all, W * M * K, h->scratch_owned));
+  FW_TRY(alloc(h, &h->ep_score_all, W * M * K, h->scratch_owned));
+  FW_TRY(alloc(h, &h->ep_recv, std::max(Gd * K * H, prefill ? M * K * H : 0), h->scratch_owned));
+  if (prefill) {
+    FW_TRY(regrow(h, &s.pair_tk, Gp * K));
+    FW_TRY(regrow(h, &s.xg, Gp * K * H));
+    s.pair_cap = static_cast<long long>(Gp * K);
+    FW_TRY(alloc(h, &h->ep_send_pos, Gp * K, h->scratch_owned));
+    FW_TRY(alloc(h, &h->ep_recv_pos, M * K, h->scratch_owned));
+    FW_TRY(alloc(h, &h->ep_counts, 4 * W, h->scratch_owned));
+    FW_CUDA(cudaMallocHost(&h->ep_counts_host, 4 * W * sizeof(int)));
+    FW_CUDA(cudaEventCreateWithFlags(&h->ep_counts_ev, cudaEventDisableTiming));
+  }
+  // act / xg moved: re-encode the scratch tensor maps
+  if (h->prefill_ok && !fw::make_prefill_scratch_maps(h->shape, s, &h->pf_maps))
+    return fail(FW_ECUDA, "prefill tensor maps could not be encoded");
   fw::EpComm* c = nullptr;
   const char* m = fw::ep_comm_init(rank, world, id, &c);
   if (m != nullptr) return fail(FW_ENCCL, m);
   h->ep = c;
   h->ep_rank = rank;
   h->ep_world = world;
+  h->ep_decode_max = static_cast<int>(Md);
   return FW_OK;
 }
 
@@ -382,6 +460,7 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &s.unit_prefix, 2 * (static_cast<size_t>(E) + 2), o)) != FW_OK) break;
     if ((rc = alloc(h, &s.pair_tk, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.xg, static_cast<size_t>(M) * K * H, o)) != FW_OK) break;
+    s.pair_cap = static_cast<long long>(M) * K;
     if ((rc = alloc(h, &h->x_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->y_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->idx_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
@@ -415,6 +494,8 @@ int fw_moe_destroy(fw_moe* h) {
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
   fw::ep_comm_destroy(h->ep);
+  if (h->ep_counts_host) cudaFreeHost(h->ep_counts_host);
+  if (h->ep_counts_ev) cudaEventDestroy(h->ep_counts_ev);
   for (auto& L : h->layers) free_layer(L);
   for (void* p : h->scratch_owned) cudaFree(p);
   if (h->stream) cudaStreamDestroy(h->stream);
@@ -528,7 +609,7 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
   }
   L.w.expert_base = ebase;
   L.w.expert_count = ecount;
-  L.prefill = h->ep == nullptr && h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
+  L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
   return FW_OK;
 }
@@ -629,7 +710,7 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
   }
   L.w.expert_base = ebase;
   L.w.expert_count = ecount;
-  L.prefill = h->ep == nullptr && h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
+  L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
   return FW_OK;
 }
@@ -649,7 +730,13 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   uint16_t* sc = topk_scores ? topk_scores : h->score_dev;
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
   cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
-  if (h->ep != nullptr) return ep_forward(h, L, x, tokens, y, idx, sc, cs, ev);
+  if (h->ep != nullptr) {
+    const bool ep_prefill = tokens > h->ep_decode_max || tokens >= h->prefill_min_tokens;
+    if (!ep_prefill) return ep_forward(h, L, x, tokens, y, idx, sc, cs, ev);
+    if (!L.prefill || h->ep_send_pos == nullptr)
+      return fail(FW_EINVAL, "this many tokens need the prefill path, which this handle's shape lacks");
+    return ep_prefill_forward(h, L, x, tokens, y, idx, sc, cs, ev);
+  }
   const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
   if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
   const cudaError_t e =
@@ -662,7 +749,6 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
 int fw_moe_set_prefill_min_tokens(fw_moe* h, int32_t min_tokens) {
   if (h == nullptr) return fail(FW_EINVAL, "handle is null");
   if (min_tokens < 1) return fail(FW_EINVAL, "min_tokens must be >= 1");
-  if (h->ep != nullptr) return fail(FW_EINVAL, "the prefill path is single-GPU (expert parallelism is on)");
   if (min_tokens <= kDecodeMaxTokens && !h->prefill_ok)
     return fail(FW_EINVAL, "this block shape has no prefill path");
   h->prefill_min_tokens = min_tokens;

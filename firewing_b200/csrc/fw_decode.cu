@@ -549,6 +549,7 @@ struct CombineArgs {
   // per source GPU, T tokens each).
   const int32_t* idx;
   int ep_experts;
+  const int32_t* row_of;  // if set: the row of (t, k) is row_of[t * K + k]
   const uint16_t* weighted;
   const uint16_t* gated_sh;
   uint16_t* y;
@@ -576,7 +577,9 @@ __global__ void k_combine(CombineArgs a) {
     for (int i = 0; i < 8; ++i) {
       const int src =
           (a.idx != nullptr && n0 + i < a.K) ? a.idx[static_cast<size_t>(t) * a.K + sl[i]] / a.ep_experts : 0;
-      row[i] = (static_cast<size_t>(src) * a.T + t) * a.K + sl[i];
+      row[i] = a.row_of != nullptr
+                   ? static_cast<size_t>(n0 + i < a.K ? a.row_of[static_cast<size_t>(t) * a.K + sl[i]] : 0)
+                   : (static_cast<size_t>(src) * a.T + t) * a.K + sl[i];
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -753,8 +756,8 @@ cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t*
 }
 
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
-                           const int32_t* ep_idx, int ep_experts, const uint16_t* ep_rows) {
-  CombineArgs a{s.H, s.K, T, sc.sorted_slot, ep_idx, ep_experts > 0 ? ep_experts : s.E,
+                           const int32_t* ep_idx, int ep_experts, const uint16_t* ep_rows, const int32_t* row_of) {
+  CombineArgs a{s.H, s.K, T, sc.sorted_slot, ep_idx, ep_experts > 0 ? ep_experts : s.E, row_of,
                 ep_rows != nullptr ? ep_rows : sc.weighted, sc.gated_sh, y};
   return launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
 }

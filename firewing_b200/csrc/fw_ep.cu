@@ -160,6 +160,29 @@ const char* ep_combine_exchange(EpComm* c, const uint16_t* send, uint16_t* recv,
   return nullptr;
 }
 
+const char* ep_exchange_rows(EpComm* c, const uint16_t* send, const int* rows_send, const int* off_send,
+                             uint16_t* recv, const int* rows_recv, const int* off_recv, size_t row_elems,
+                             cudaStream_t st) {
+  const NcclApi& a = api();
+  ncclResult_t r = a.group_start();
+  if (r != ncclSuccess) return nccl_fail("ncclGroupStart", r);
+  ncclResult_t bad = ncclSuccess;
+  for (int p = 0; p < c->world; ++p) {
+    ncclResult_t s1 = ncclSuccess, s2 = ncclSuccess;
+    if (rows_send[p] > 0)
+      s1 = a.send(send + static_cast<size_t>(off_send[p]) * row_elems, static_cast<size_t>(rows_send[p]) * row_elems,
+                  ncclBfloat16, p, c->comm, st);
+    if (rows_recv[p] > 0)
+      s2 = a.recv(recv + static_cast<size_t>(off_recv[p]) * row_elems, static_cast<size_t>(rows_recv[p]) * row_elems,
+                  ncclBfloat16, p, c->comm, st);
+    if (bad == ncclSuccess) bad = s1 != ncclSuccess ? s1 : s2;
+  }
+  r = a.group_end();
+  if (bad != ncclSuccess) return nccl_fail("ncclSend / ncclRecv", bad);
+  if (r != ncclSuccess) return nccl_fail("ncclGroupEnd", r);
+  return nullptr;
+}
+
 const char* ep_async_error(EpComm* c) {
   if (c == nullptr || !api().ok) return nullptr;
   ncclResult_t e = ncclSuccess;

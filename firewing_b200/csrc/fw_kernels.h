@@ -101,7 +101,8 @@ struct Scratch {
   int* pair_offset = nullptr;    // [E+1] first pair of each expert in grouped order
   int* unit_prefix = nullptr;    // [2][E+2] GEMM work-unit prefix per slot, up and down phases
   int32_t* pair_tk = nullptr;    // [T*K] grouped pairs: t*K + top-k position
-  uint16_t* xg = nullptr;        // input rows in grouped pair order, K-blocked: [H/64][T*K][64]
+  uint16_t* xg = nullptr;        // input rows in grouped pair order, K-blocked: [H/64][pair_cap][64]
+  long long pair_cap = 0;        // pair rows of xg / act / pair_tk (max_T * K; more under expert parallelism)
 };
 
 // Schedule layout inside Scratch::sched (int32 words), written by the route
@@ -180,6 +181,30 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
                            const PrefillScratchMaps& sm, const Luts& luts, const Scratch& sc, const uint16_t* x,
                            int T, uint16_t* y, int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
                            cudaEvent_t* stage_events = nullptr);
+// Prefill stages, composed by launch_prefill (one GPU) and by the
+// expert-parallel prefill forward (fw_api.cu):
+//   front: router + route of T tokens (pair counts when count_pairs);
+//   group: pairs of idx [n_pairs] with experts in [ebase, ebase + ecount)
+//          grouped by expert, their rows (x_src: row i / K) into xg; counts
+//          computed here when count_here; shared expert over sh_T tokens;
+//   gemms: gate/up and down GEMMs; weighted rows to out_rows at row t*K+k,
+//          or at send_pos[t*K+k] when send_pos is given.
+cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
+                                 const uint16_t* x, int T, int32_t* topk_idx, uint16_t* topk_score, bool count_pairs,
+                                 cudaStream_t st);
+cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_t* idx, int n_pairs,
+                                 const uint16_t* x_src, int ebase, int ecount, int sh_T, bool count_here,
+                                 cudaStream_t st);
+cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, const PrefillScratchMaps& smaps,
+                                 const Luts& luts, const Scratch& sc, const uint16_t* x_own, int T_own, int ecount,
+                                 const uint16_t* score, const int32_t* send_pos, uint16_t* out_rows,
+                                 cudaStream_t st);
+// Packed positions of weighted rows for the expert-parallel exchange (see
+// k_ep_positions): send side over the gathered ids (group = token owner),
+// receive side over this rank's ids (group = computing GPU).
+cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int ep, int me, int world, bool recv,
+                                int32_t* pos, int* count, int* offset, cudaStream_t st);
+
 // Stages shared with the decode path (fw_decode.cu).
 cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& sc, const uint16_t* x, int T,
                           cudaStream_t st);
@@ -187,8 +212,10 @@ cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& 
                                uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st);
 // ep_idx / ep_experts / ep_rows: expert parallelism (rows per source GPU,
 // see CombineArgs); null / 0 / null on one GPU.
+// row_of: explicit row of every (t, k) in ep_rows (expert-parallel prefill).
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
-                           const int32_t* ep_idx = nullptr, int ep_experts = 0, const uint16_t* ep_rows = nullptr);
+                           const int32_t* ep_idx = nullptr, int ep_experts = 0, const uint16_t* ep_rows = nullptr,
+                           const int32_t* row_of = nullptr);
 // Expert parallelism: schedule of experts [ep_base, ep_base + ep_count)
 // over the gathered selections idx_all [T][K], shared expert over sh_T tokens.
 cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_base,
@@ -209,6 +236,12 @@ const char* ep_dispatch(EpComm* c, const uint16_t* x, uint16_t* x_all, size_t x_
 const char* ep_combine_exchange(EpComm* c, const uint16_t* send, uint16_t* recv, size_t block_elems,
                                 cudaStream_t st);
 const char* ep_async_error(EpComm* c);
+// Row-sized exchange: rows_send[p] rows of `row_elems` bf16 from send at
+// row off_send[p] to rank p; rows_recv[p] rows from rank p into recv at
+// row off_recv[p] (counts on the host).
+const char* ep_exchange_rows(EpComm* c, const uint16_t* send, const int* rows_send, const int* off_send,
+                             uint16_t* recv, const int* rows_recv, const int* off_recv, size_t row_elems,
+                             cudaStream_t st);
 
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.

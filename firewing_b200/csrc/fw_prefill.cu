@@ -46,6 +46,7 @@
 // Every wait is bounded (2 s of globaltimer); on expiry the CTA records
 // kErrTimeout, stops issuing, lets its copies and MMAs drain (bounded), frees
 // its TMEM and exits.
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -171,6 +172,9 @@ struct GemmArgs {
   // (act_sh: token capacity); b_blocked_s = 0 when the shared up operand is
   // the row-major input x.
   int rows_r, rows_s, b_blocked_s;
+  // Expert parallelism: destination row of pair t*K+k's weighted output in
+  // the packed send buffer (null: row t*K+k of `weighted`).
+  const int32_t* send_pos;
   const int* offset;       // [E+1] grouped pair offsets
   const int* prefix;       // [E+2] unit prefix of this phase (slot E = shared)
   const int32_t* pair_tk;  // [pairs] t*K + k
@@ -412,7 +416,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (((j >> 5) & 1) != set) continue;
           if (w.routed) {
             const int tk = a.pair_tk[w.n0 + j];
-            s_col_row[j] = tk;
+            s_col_row[j] = a.send_pos != nullptr ? a.send_pos[tk] : tk;
             s_col_scale[j] = bf16_to_f32(a.score[tk]);
           } else {
             s_col_row[j] = w.n0 + j;
@@ -773,8 +777,12 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
 // a copy of the token's input row into the grouped input (so the gate/up
 // GEMM reads each expert's token rows of a 64-column block as one
 // contiguous run).
-__global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, const int* offset, int* fill,
-                             int32_t* pair_tk, const uint16_t* x, uint16_t* xg, long long xg_rows, int* err) {
+// Only pairs whose expert lies in [ebase, ebase + ecount) are grouped (this
+// GPU's experts under expert parallelism; all of them otherwise); slots are
+// relative to ebase.
+__global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, int ebase, int ecount,
+                             const int* offset, int* fill, int32_t* pair_tk, const uint16_t* x, uint16_t* xg,
+                             long long xg_rows, int* err) {
   pdl_wait();
   pdl_launch_dependents();
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -785,8 +793,10 @@ __global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, co
     if (e < 0 || e >= E) {
       set_error(err, kErrBadIndex);
       p = -1;
+    } else if (e < ebase || e >= ebase + ecount) {
+      p = -1;  // another GPU's expert
     } else {
-      p = offset[e] + atomicAdd(&fill[e], 1);
+      p = offset[e - ebase] + atomicAdd(&fill[e - ebase], 1);
       pair_tk[p] = i;
     }
   }
@@ -797,6 +807,90 @@ __global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, co
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(i / K) * H);
   for (int c = lane; c < H / 8; c += 32)
     *reinterpret_cast<uint4*>(xg + ((static_cast<size_t>(c >> 3) * xg_rows + p) * 64 + (c & 7) * 8)) = src[c];
+}
+
+// Expert parallelism: per-expert pair counts of this GPU's experts over
+// every rank's gathered selections.
+__global__ void k_ep_count(const int32_t* idx, int n, int ebase, int ecount, int* count) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int e = idx[i] - ebase;
+    if (e >= 0 && e < ecount) atomicAdd(&count[e], 1);
+  }
+}
+
+// Expert parallelism: packed positions of weighted rows.  Entry i of idx
+// (a top-k id) belongs to group g with flag f:
+//   send mode: g = i / group_len (the token owner), f = (idx / ep == me);
+//   recv mode: g = idx / ep (the GPU that computed the row), f = 1.
+// pos[i] = offset[g] + (flagged entries of group g before i), else -1;
+// count[g], offset[g] (exclusive over g).  Entries in index order keep each
+// group's rows in (token, k) order on both sides.  One CTA of 1024 threads.
+constexpr int kEpMaxWorld = 8;
+__global__ void __launch_bounds__(1024) k_ep_positions(const int32_t* idx, int n, int group_len, int ep, int me,
+                                                        int world, int recv_mode, int32_t* pos, int* count,
+                                                        int* offset) {
+  __shared__ int part[kEpMaxWorld][1025];
+  __shared__ int tot[kEpMaxWorld], off[kEpMaxWorld];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int per = (n + nt - 1) / nt, i0 = tid * per, i1 = min(n, i0 + per);
+  auto key = [&](int i) {
+    const int owner = idx[i] / ep;
+    if (recv_mode) return owner;
+    return owner == me ? i / group_len : -1;
+  };
+  int c[kEpMaxWorld];
+#pragma unroll
+  for (int g = 0; g < kEpMaxWorld; ++g) c[g] = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int k = key(i);
+#pragma unroll
+    for (int g = 0; g < kEpMaxWorld; ++g) c[g] += (k == g) ? 1 : 0;
+  }
+  for (int g = 0; g < world; ++g) part[g][tid] = c[g];
+  __syncthreads();
+  // exclusive scan over threads, one group per warp (world <= 8 <= warps)
+  const int warp = tid >> 5, lane = tid & 31;
+  if (warp < world) {
+    int run = 0;
+    for (int b = 0; b < nt; b += 32) {
+      const int v = b + lane < nt ? part[warp][b + lane] : 0;
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (b + lane < nt) part[warp][b + lane] = run + x - v;
+      run += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0) tot[warp] = run;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int g = 0; g < world; ++g) {
+      off[g] = acc;
+      count[g] = tot[g];
+      offset[g] = acc;
+      acc += tot[g];
+    }
+  }
+  __syncthreads();
+  int cur[kEpMaxWorld];
+#pragma unroll
+  for (int g = 0; g < kEpMaxWorld; ++g) cur[g] = g < world ? off[g] + part[g][tid] : 0;
+  for (int i = i0; i < i1; ++i) {
+    const int k = key(i);
+    int p = -1;
+#pragma unroll
+    for (int g = 0; g < kEpMaxWorld; ++g)
+      if (k == g) p = cur[g]++;
+    pos[i] = p;
+  }
 }
 
 template <typename Kern, typename... Args>
@@ -896,67 +990,75 @@ bool make_prefill_weight_maps(const Shape& s, const LayerWeights& w, PrefillWeig
 bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratchMaps* out) {
   if (!prefill_supported(s)) return false;
   // K-blocked [K/64][rows][64] operands as 64-column row-major views.
-  const long long P = static_cast<long long>(sc.max_T) * s.K, M = sc.max_T;
+  const long long P = sc.pair_cap, M = sc.max_T;
   return rows_map(&out->xg, sc.xg, 64, (s.H / 64) * P, 16) && rows_map(&out->act, sc.act, 64, (s.I / 64) * P, 16) &&
          rows_map(&out->act_sh, sc.act_sh, 64, (s.Is / 64) * M, 16);
 }
 
-cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
-                           const PrefillScratchMaps& smaps, const Luts& luts, const Scratch& sc, const uint16_t* x,
-                           int T, uint16_t* y, int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
-                           cudaEvent_t* ev) {
-  if (T <= 0) return cudaSuccess;
+cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
+                                 const uint16_t* x, int T, int32_t* topk_idx, uint16_t* topk_score, bool count_pairs,
+                                 cudaStream_t st) {
   cudaError_t e;
-  auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
-  // Per-forward map of the input rows (the shared expert's token tiles).
-  CUtensorMap x_rows;
-  if (!rows_map(&x_rows, x, s.H, T, 16)) return cudaErrorInvalidValue;
-  if ((e = mark(0)) != cudaSuccess) return e;
-  if ((e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * s.E, st)) != cudaSuccess) return e;
-  {
-    PfRouterArgs ra{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T,
-                    s.H % kRtMaxChunk == 0 ? kRtMaxChunk : kRtMaxChunk / 2, sc.err};
-    const size_t rsm = router_pf_smem();
-    const int rtiles = (s.E + 1 + kRtRows - 1) / kRtRows * ((T + kRtTok - 1) / kRtTok);
-    const dim3 rgrid(rtiles < 2 * sm_count() ? rtiles : 2 * sm_count());
-    if ((e = launch_pdl_ex(k_router_pf, rgrid, dim3(32 * (kRtComputeWarps + 1)), rsm, st, ra)) != cudaSuccess ||
-        (e = mark(1)) != cudaSuccess)
-      return e;
-  }
-  if ((e = launch_route_block(s, luts, sc, T, topk_idx, topk_score, false, sc.pair_count, st)) != cudaSuccess)
+  if (count_pairs && (e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * s.E, st)) != cudaSuccess) return e;
+  PfRouterArgs ra{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T,
+                  s.H % kRtMaxChunk == 0 ? kRtMaxChunk : kRtMaxChunk / 2, sc.err};
+  const int rtiles = (s.E + 1 + kRtRows - 1) / kRtRows * ((T + kRtTok - 1) / kRtTok);
+  const dim3 rgrid(rtiles < 2 * sm_count() ? rtiles : 2 * sm_count());
+  if ((e = launch_pdl_ex(k_router_pf, rgrid, dim3(32 * (kRtComputeWarps + 1)), router_pf_smem(), st, ra)) !=
+      cudaSuccess)
     return e;
-  {
-    OffsetsArgs oa{s.E, T, 2 * s.I / kBM, 2 * s.Is / kBM, s.H / kBM, sc.pair_count, sc.pair_fill, sc.pair_offset,
-                   sc.unit_prefix};
-    const int threads = (s.E + 31) / 32 * 32;
-    if ((e = launch_pdl_ex(k_pf_offsets, dim3(1), dim3(threads), 0, st, oa)) != cudaSuccess) return e;
-    const int TK = T * s.K;
-    if ((e = launch_pdl_ex(k_pf_scatter, dim3((TK + 7) / 8), dim3(256), 0, st,
-                           static_cast<const int32_t*>(topk_idx), TK, s.K, s.E, s.H,
-                           static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x, sc.xg,
-                           static_cast<long long>(sc.max_T) * s.K, sc.err)) != cudaSuccess)
+  return launch_route_block(s, luts, sc, T, topk_idx, topk_score, false, count_pairs ? sc.pair_count : nullptr, st);
+}
+
+cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_t* idx, int n_pairs,
+                                 const uint16_t* x_src, int ebase, int ecount, int sh_T, bool count_here,
+                                 cudaStream_t st) {
+  cudaError_t e;
+  if (count_here) {
+    if ((e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * ecount, st)) != cudaSuccess) return e;
+    const int blocks = std::min(4 * sm_count(), (n_pairs + 255) / 256 > 0 ? (n_pairs + 255) / 256 : 1);
+    if ((e = launch_pdl_ex(k_ep_count, dim3(blocks), dim3(256), 0, st, idx, n_pairs, ebase, ecount, sc.pair_count)) !=
+        cudaSuccess)
       return e;
   }
-  if ((e = mark(2)) != cudaSuccess) return e;
-  const size_t smem = gemm_smem_bytes(s.E);
+  OffsetsArgs oa{ecount, sh_T, 2 * s.I / kBM, 2 * s.Is / kBM, s.H / kBM, sc.pair_count, sc.pair_fill, sc.pair_offset,
+                 sc.unit_prefix};
+  if ((e = launch_pdl_ex(k_pf_offsets, dim3(1), dim3((ecount + 31) / 32 * 32), 0, st, oa)) != cudaSuccess) return e;
+  return launch_pdl_ex(k_pf_scatter, dim3((n_pairs + 7) / 8), dim3(256), 0, st, idx, n_pairs, s.K, s.E, s.H, ebase,
+                       ecount, static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x_src, sc.xg,
+                       static_cast<long long>(sc.pair_cap), sc.err);
+}
+
+cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, const PrefillScratchMaps& smaps,
+                                 const Luts& luts, const Scratch& sc, const uint16_t* x_own, int T_own, int ecount,
+                                 const uint16_t* score, const int32_t* send_pos, uint16_t* out_rows,
+                                 cudaStream_t st) {
+  // Per-forward map of this rank's input rows (the shared expert's token tiles).
+  CUtensorMap x_rows;
+  if (!rows_map(&x_rows, x_own, s.H, T_own, 16)) return cudaErrorInvalidValue;
+  cudaError_t e;
+  const size_t smem = gemm_smem_bytes(ecount);
   const dim3 grid(sm_count()), block(kGemmThreads);
   GemmArgs g{};
-  g.E = s.E;
-  g.T = T;
+  g.E = ecount;
+  g.T = T_own;
   g.K = s.K;
   g.H = s.H;
   g.I = s.I;
   g.Is = s.Is;
   g.offset = sc.pair_offset;
   g.pair_tk = sc.pair_tk;
-  g.score = topk_score;
+  g.score = score;
   g.sh_sig = sc.sh_sig;
   g.silu = luts.silu;
   g.act = sc.act;
   g.act_sh = sc.act_sh;
-  g.weighted = sc.weighted;
+  g.weighted = out_rows;
   g.gated_sh = sc.gated_sh;
   g.err = sc.err;
+  g.send_pos = send_pos;
+  g.rows_r = sc.pair_cap;
+  g.rows_s = sc.max_T;
   // gate/up + SwiGLU
   g.phase = 0;
   g.kb_r = s.H / kBK;
@@ -964,8 +1066,6 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   g.mt_r = 2 * s.I / kBM;
   g.mt_s = 2 * s.Is / kBM;
   g.groups_r = 2 * s.I / 8;
-  g.rows_r = sc.max_T * s.K;
-  g.rows_s = sc.max_T;
   g.b_blocked_s = 0;  // shared up: the row-major input
   g.prefix = sc.unit_prefix;
   if ((e = launch_pdl_ex(k_gemm, grid, block, smem, st, wm.gate_up, wm.sh_gate_up, smaps.xg, x_rows, g)) !=
@@ -979,8 +1079,30 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   g.mt_s = s.H / kBM;
   g.groups_r = s.H / 8;
   g.b_blocked_s = 1;  // shared down: K-blocked act_sh
-  g.prefix = sc.unit_prefix + s.E + 2;
-  if ((e = launch_pdl_ex(k_gemm, grid, block, smem, st, wm.down, wm.sh_down, smaps.act, smaps.act_sh, g)) !=
+  g.prefix = sc.unit_prefix + ecount + 2;
+  return launch_pdl_ex(k_gemm, grid, block, smem, st, wm.down, wm.sh_down, smaps.act, smaps.act_sh, g);
+}
+
+cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int ep, int me, int world, bool recv,
+                                int32_t* pos, int* count, int* offset, cudaStream_t st) {
+  if (world > kEpMaxWorld) return cudaErrorInvalidValue;
+  return launch_pdl_ex(k_ep_positions, dim3(1), dim3(1024), 0, st, idx, n, group_len, ep, me, world, recv ? 1 : 0,
+                       pos, count, offset);
+}
+
+cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
+                           const PrefillScratchMaps& smaps, const Luts& luts, const Scratch& sc, const uint16_t* x,
+                           int T, uint16_t* y, int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
+                           cudaEvent_t* ev) {
+  if (T <= 0) return cudaSuccess;
+  cudaError_t e;
+  auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
+  if ((e = mark(0)) != cudaSuccess) return e;
+  if ((e = launch_prefill_front(s, w, luts, sc, x, T, topk_idx, topk_score, true, st)) != cudaSuccess) return e;
+  if ((e = mark(1)) != cudaSuccess) return e;
+  if ((e = launch_prefill_group(s, sc, topk_idx, T * s.K, x, 0, s.E, T, false, st)) != cudaSuccess) return e;
+  if ((e = mark(2)) != cudaSuccess) return e;
+  if ((e = launch_prefill_gemms(s, wm, smaps, luts, sc, x, T, s.E, topk_score, nullptr, sc.weighted, st)) !=
       cudaSuccess)
     return e;
   if ((e = mark(3)) != cudaSuccess) return e;

@@ -125,20 +125,26 @@ int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);
  * the reference runs the block on one device).  Rank r of `world` holds the
  * routed experts [r*E/world, (r+1)*E/world) of every layer (router, shared
  * expert and bias replicated) and brings its own tokens to each forward.
- * Per layer: router and route on the rank's tokens, an all-gather of every
- * rank's token rows, top-k ids and route weights, this rank's experts over
- * all gathered tokens, a grouped send/recv that returns each token's
- * weighted rows to its owner, and the owner's ascending-id sum, so outputs
- * are bit-identical to the single-GPU decode path.  NCCL (libnccl.so.2) is
- * loaded at run time.
+ * Per layer:
+ *   - router and route run on the rank's own tokens;
+ *   - an all-gather brings every rank's token rows, top-k ids and route
+ *     weights;
+ *   - this rank's experts run over all gathered tokens;
+ *   - each token's weighted rows return to its owner, which sums them in
+ *     ascending expert id.
+ * The decode path (widths up to min(256, 1024 / world) tokens per rank)
+ * returns fixed-size blocks and is bit-identical to one GPU.  Wider forwards
+ * take the prefill path's tensor-core GEMMs and a row-sized exchange;
+ * their outputs are within the block tolerance and the call waits once on
+ * the host for the exchange sizes.  NCCL (libnccl.so.2) is loaded at run
+ * time.
  *   fw_ep_unique_id: a communicator id; make it on one rank and hand the
  *     128 bytes to every rank (any host transport).
  *   fw_moe_ep_init: on every rank, collectively, after fw_moe_create and
- *     before any layer is loaded.  Needs experts % world == 0,
- *     max_tokens <= 256 and world * max_tokens <= 1024.  Afterwards every
- *     forward on the handle is collective: all ranks call it for the same
- *     layer with the same token count, in the same order; the prefill path
- *     is not available (decode widths only).  FW_ENCCL on collective errors. */
+ *     before any layer is loaded.  Needs 2 <= world <= 8 and
+ *     experts % world == 0.  Afterwards every forward on the handle is
+ *     collective: all ranks call it for the same layer with the same token
+ *     count, in the same order.  FW_ENCCL on collective errors. */
 int fw_ep_unique_id(uint8_t id[128]);
 int fw_moe_ep_init(fw_moe* handle, int32_t rank, int32_t world, const uint8_t id[128]);
 

@@ -27,7 +27,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, shape, t_local, layers, zipf, q):
+def _rank_main(rank, world, port, shape, t_local, layers, zipf, q, min_tokens=None):
     import torch.distributed as dist
 
     import firewing_b200 as fw
@@ -44,6 +44,8 @@ def _rank_main(rank, world, port, shape, t_local, layers, zipf, q):
         cfg = fw.MoeConfig(**shape, max_tokens=t_local, layers=layers)
         blk = fw.MoeBlock(cfg, device=rank)
         blk.ep_init(rank, world, uid[0])
+        if min_tokens is not None:
+            blk.set_prefill_min_tokens(min_tokens)
         for l in range(layers):
             blk.synth_layer(l, 40 + l, 0.02, zipf)
         results = []
@@ -68,23 +70,26 @@ def _rank_main(rank, world, port, shape, t_local, layers, zipf, q):
                 ry, ridx, rsc = O.block(bshape, O.SynthLayer(bshape, 40 + l, 0.02, zipf), x_all,
                                         threads=os.cpu_count() or 1)
                 exact = np.all(s == rsc, axis=1)
+                yf, rf = O.bf16_to_f32(y).astype(np.float64), O.bf16_to_f32(ry).astype(np.float64)
                 report.append(dict(idx=bool(np.array_equal(i, ridx)),
                                    score_ulp=int(np.abs(s.astype(np.int32) - rsc.astype(np.int32)).max()),
                                    exact_tokens_equal=bool(np.array_equal(y[exact], ry[exact])),
-                                   n_exact=int(exact.sum()), repeat=rep))
+                                   n_exact=int(exact.sum()), repeat=rep,
+                                   max_abs=float(np.abs(yf - rf).max()),
+                                   rel_l2=float(np.linalg.norm(yf - rf) / max(np.linalg.norm(rf), 1e-30))))
             q.put(report)
     finally:
         dist.destroy_process_group()
 
 
-def _run(shape, t_local, layers, zipf):
+def _run(shape, t_local, layers, zipf, min_tokens=None):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, t_local, layers, zipf, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, t_local, layers, zipf, q, min_tokens))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -107,3 +112,16 @@ def test_ep_two_gpus_small_shape(t_local, zipf):
 def test_ep_two_gpus_config0_shape():
     for r in _run(CFG0, 32, 1, False):
         assert r["idx"] and r["score_ulp"] <= 1 and r["exact_tokens_equal"] and r["repeat"], r
+
+
+# Prefill path under expert parallelism (tensor-core GEMMs, row-sized
+# exchange): the block tolerance of the north star, identical selection.
+CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512, top_k=10)
+
+
+@pytest.mark.parametrize("shape,t_local,min_tokens,zipf", [(SMALL, 300, None, True), (SMALL, 40, 1, False),
+                                                          (CFG4, 160, 1, True)])
+def test_ep_two_gpus_prefill(shape, t_local, min_tokens, zipf):
+    for r in _run(shape, t_local, 1, zipf, min_tokens):
+        assert r["idx"] and r["score_ulp"] <= 1 and r["repeat"], r
+        assert r["max_abs"] <= 2e-2 and r["rel_l2"] <= 1e-3, r
