@@ -39,6 +39,11 @@ EP = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, t
           tokens=256, layers=24, layers_8=48,
           name="cfg3: {layers}-layer stack of the config-0 block, EP over {world} GPUs ({per} experts "
                "per GPU), decode T=256 per layer, uniform routing")
+# Reported alongside (not the headline): BASELINE config 4, the larger block
+# at prefill width, 12 layers; one GPU at N = 1, expert-parallel at N > 1.
+CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512, top_k=10,
+            tokens=8192, layers=12, zipf=True,
+            name="cfg4: 12-layer stack, H=3072, I=Is=768, Zipf-biased router, prefill T=8192 per GPU")
 # Reported alongside (not the headline): BASELINE config 2, one block at
 # prefill width with the Zipf-biased router, on the tensor-core path.
 PREFILL = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10,
@@ -393,6 +398,9 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     ep = None
     if world > 1 and not args.no_ep:
         ep = measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist)
+    cfg4 = None
+    if not args.no_cfg4:
+        cfg4 = measure_cfg4(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist)
 
     cpu = None
     parity = None
@@ -435,6 +443,7 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             "t1": t1,
             "prefill": prefill,
             "ep": ep,
+            "cfg4": cfg4,
         }
         print(json.dumps(line), flush=True)
 
@@ -503,6 +512,65 @@ def measure_prefill(args, rank, world, local_rank, peaks, stream, max_over_ranks
         "gpu_launches_per_step": 7,
         "kernels": "router (exact, CUDA cores), route, pair offsets, pair scatter, gate/up GEMM "
                    "(tcgen05, SwiGLU epilogue), down GEMM (tcgen05, weight epilogue), combine",
+    }
+
+
+def measure_cfg4(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist):
+    """12 layers of the larger block at prefill width,
+    8192 tokens per GPU per layer, Zipf-biased router.  One GPU at N = 1;
+    expert parallelism over the N GPUs otherwise (rank r holds experts
+    [r*512/N, (r+1)*512/N)).  Whole-job token-layers/s and its per-GPU share,
+    from which the expert-parallel efficiency against N = 1 follows."""
+    import torch
+
+    import firewing_b200 as fw
+    from firewing_b200 import synth
+
+    p = CFG4
+    T, L = p["tokens"], p["layers"]
+    H, K, E, I, Is = p["hidden"], p["top_k"], p["experts"], p["intermediate"], p["shared_intermediate"]
+    blk = fw.MoeBlock(fw.MoeConfig(H, I, Is, E, K, max_tokens=T, layers=L), device=local_rank)
+    if world > 1:
+        uid = [fw.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        blk.ep_init(rank, world, uid[0])
+    for l in range(L):
+        blk.synth_layer(l, 100 + l, 0.02, p["zipf"])
+    x = torch.from_numpy(np.stack([synth.synth_input(input_seed(rank, l), T, H) for l in range(L)])
+                         .view(np.int16)).cuda()
+    y = torch.empty((L, T, H), dtype=torch.int16, device="cuda")
+    idx = torch.empty((L, T, K), dtype=torch.int32, device="cuda")
+    sc = torch.empty((L, T, K), dtype=torch.int16, device="cuda")
+
+    def step():
+        for l in range(L):
+            blk.forward_async(l, x[l], T, y[l], idx[l], sc[l], stream=stream)
+
+    steps = 3
+    for _ in range(2):
+        step()
+    blk.sync(stream)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    blk.sync(stream)
+    el = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    blk.close()
+    flops = 2 * 3 * H * I * T * K + 2 * 3 * H * Is * T  # per GPU per layer
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0)) if peaks else 1590.0
+    value = world * T * L * steps / el
+    return {
+        "workload": p["name"], "n_gpus": world, "tokens_per_gpu": T, "layers": L, "steps": steps,
+        "value": value, "per_gpu_value": value / world, "unit": UNIT, "ms_per_layer": el / steps / L * 1e3,
+        "expert_tflops_per_gpu": flops * L * steps / el / 1e12,
+        "expert_frac_tensor_per_gpu": flops * L * steps / el / 1e12 / tc_peak,
+        "parallelism": f"ep{world}" if world > 1 else "single",
+        "note": "expert-parallel efficiency = per_gpu_value at N / value at N = 1",
     }
 
 
@@ -595,6 +663,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill line item")
     ap.add_argument("--no-ep", action="store_true", help="skip the config-3 expert-parallel line item (N > 1)")
+    ap.add_argument("--no-cfg4", action="store_true", help="skip the config-4 prefill line item")
     ap.add_argument("--only-prefill", action="store_true",
                     help="run only the config-2 prefill measurement and print it (for ncu captures)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
