@@ -518,8 +518,8 @@ def measure_prefill(args, rank, world, local_rank, peaks, stream, max_over_ranks
 def measure_cfg4(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist):
     """12 layers of the larger block at prefill width,
     8192 tokens per GPU per layer, Zipf-biased router.  One GPU at N = 1;
-    expert parallelism over the N GPUs otherwise (rank r holds experts
-    [r*512/N, (r+1)*512/N)).  Whole-job token-layers/s and its per-GPU share,
+    expert parallelism over the N GPUs otherwise (rank r holds the experts
+    e with e % N == r).  Whole-job token-layers/s and its per-GPU share,
     from which the expert-parallel efficiency against N = 1 follows."""
     import torch
 
@@ -578,7 +578,7 @@ def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, bar
     """BASELINE config 3 on `world` GPUs with expert parallelism: decode of
     256 tokens per layer in total (256/world per rank), uniform routing, a
     48-layer stack at 8 GPUs (64 experts per GPU), 24 layers at 2 or 4.
-    Rank r holds experts [r*512/world, (r+1)*512/world) of every layer; each
+    Rank r holds the experts e with e % world == r of every layer; each
     forward gathers every rank's tokens, runs the local experts, returns the
     weighted rows to their owners over NCCL and sums them there."""
     import torch
@@ -625,9 +625,8 @@ def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, bar
     t_ids = torch.from_numpy(ids.astype(np.int32)).cuda()
     all_ids = [torch.empty_like(t_ids) for _ in range(world)]
     dist.all_gather(all_ids, t_ids)
-    base, per = fw.ep_expert_range(E, world, rank)
     cat = np.concatenate([a.cpu().numpy() for a in all_ids], axis=1)
-    local_u = [int(((np.unique(cat[l]) >= base) & (np.unique(cat[l]) < base + per)).sum()) for l in range(L)]
+    local_u = [int((np.unique(cat[l]) % world == rank).sum()) for l in range(L)]
     layer_bytes = [u * 3 * H * I * 2 + E * H * 2 + 3 * H * Is * 2 for u in local_u]
     gbs = sum(layer_bytes) * steps / el / 1e9
     gbs = max_over_ranks(-gbs) * -1  # slowest rank's streaming rate

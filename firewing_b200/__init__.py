@@ -15,7 +15,8 @@ from .moe import (  # noqa: F401
     MoeBlock,
     MoeConfig,
     ep_combine_row,
-    ep_expert_range,
+    ep_held_experts,
+    ep_owner,
     ep_unique_id,
     forward_noalloc,
     library,

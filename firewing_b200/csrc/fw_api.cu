@@ -229,11 +229,10 @@ int check_handle(const fw_moe* h, int32_t layer) {
 
 // Experts this handle holds: all of them, or this rank's contiguous share
 // under expert parallelism.
-void expert_range(const fw_moe* h, int* base, int* count) {
-  const int per = h->cfg.experts / h->ep_world;
-  *base = h->ep_rank * per;
-  *count = per;
-}
+// Experts this handle holds: all of them, or under expert parallelism those
+// e with e % world == rank (bank index e / world).  Interleaving spreads a
+// skewed router's hot low-id experts over the GPUs.
+int held_experts(const fw_moe* h) { return h->cfg.experts / h->ep_world; }
 
 int free_layer(OwnedLayer& L) {
   for (void* p : L.owned) cudaFree(p);
@@ -255,8 +254,6 @@ int ep_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint1
                uint16_t* score, cudaStream_t cs, cudaEvent_t* ev) {
   const fw::Shape& s = h->shape;
   const int N = h->ep_world, T = N * T_l;
-  int base = 0, count = 0;
-  expert_range(h, &base, &count);
   cudaError_t e = cudaSuccess;
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], cs) : cudaSuccess; };
   auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
@@ -268,7 +265,7 @@ int ep_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint1
   const char* m = fw::ep_dispatch(h->ep, x, h->ep_x_all, static_cast<size_t>(T_l) * s.H, idx, h->ep_idx_all,
                                   score, h->ep_score_all, static_cast<size_t>(T_l) * s.K, cs);
   if (m != nullptr) return fail(FW_ENCCL, m);
-  if ((e = fw::launch_ep_schedule(s, h->sc, h->ep_idx_all, T, base, count, T_l, cs)) != cudaSuccess)
+  if ((e = fw::launch_ep_schedule(s, h->sc, h->ep_idx_all, T, h->ep_rank, N, T_l, cs)) != cudaSuccess)
     return cuda_failed("schedule launch");
   if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
   if ((e = fw::launch_experts(s, L.w, h->luts, h->sc, h->ep_x_all, T, h->ep_score_all, cs, x, T_l)) !=
@@ -277,7 +274,7 @@ int ep_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint1
   if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
   m = fw::ep_combine_exchange(h->ep, h->sc.weighted, h->ep_recv, static_cast<size_t>(T_l) * s.K * s.H, cs);
   if (m != nullptr) return fail(FW_ENCCL, m);
-  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, idx, count, h->ep_recv)) != cudaSuccess)
+  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, idx, N, h->ep_recv)) != cudaSuccess)
     return cuda_failed("combine launch");
   if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
   return FW_OK;
@@ -293,8 +290,7 @@ int ep_prefill_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_
                        uint16_t* score, cudaStream_t cs, cudaEvent_t* ev) {
   const fw::Shape& s = h->shape;
   const int N = h->ep_world, T = N * T_l;
-  int base = 0, count = 0;
-  expert_range(h, &base, &count);
+  const int count = held_experts(h);
   cudaError_t e = cudaSuccess;
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], cs) : cudaSuccess; };
   auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
@@ -305,13 +301,14 @@ int ep_prefill_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_
   const char* m = fw::ep_dispatch(h->ep, x, h->ep_x_all, static_cast<size_t>(T_l) * s.H, idx, h->ep_idx_all,
                                   score, h->ep_score_all, static_cast<size_t>(T_l) * s.K, cs);
   if (m != nullptr) return fail(FW_ENCCL, m);
-  if ((e = fw::launch_prefill_group(s, h->sc, h->ep_idx_all, T * s.K, h->ep_x_all, base, count, T_l, true, cs)) !=
+  if ((e = fw::launch_prefill_group(s, h->sc, h->ep_idx_all, T * s.K, h->ep_x_all, h->ep_rank, N, count, T_l, true,
+                                    cs)) !=
       cudaSuccess)
     return cuda_failed("grouping launch");
   int* cnt = h->ep_counts;
-  if ((e = fw::launch_ep_positions(h->ep_idx_all, T * s.K, T_l * s.K, count, h->ep_rank, N, false, h->ep_send_pos,
+  if ((e = fw::launch_ep_positions(h->ep_idx_all, T * s.K, T_l * s.K, h->ep_rank, N, false, h->ep_send_pos,
                                    cnt, cnt + N, cs)) != cudaSuccess ||
-      (e = fw::launch_ep_positions(idx, T_l * s.K, T_l * s.K, count, h->ep_rank, N, true, h->ep_recv_pos, cnt + 2 * N,
+      (e = fw::launch_ep_positions(idx, T_l * s.K, T_l * s.K, h->ep_rank, N, true, h->ep_recv_pos, cnt + 2 * N,
                                    cnt + 3 * N, cs)) != cudaSuccess)
     return cuda_failed("exchange positions launch");
   if ((e = cudaMemcpyAsync(h->ep_counts_host, cnt, 4 * N * sizeof(int), cudaMemcpyDeviceToHost, cs)) != cudaSuccess ||
@@ -541,28 +538,30 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
     }
     *it.dst = d;
   }
-  int ebase = 0, ecount = 0;
-  expert_range(h, &ebase, &ecount);
+  const int ecount = held_experts(h), world = h->ep_world, rank = h->ep_rank;
   // Expert banks (this handle's experts) and the shared expert go to the
-  // tiled layout through a bounded temporary buffer, a few experts at a time.
+  // tiled layout through a bounded temporary buffer, a few experts at a time
+  // (one at a time when the held experts are interleaved in the source).
   struct Tiled {
     fw::TiledSpec spec;
     long long n_mats;
     const uint16_t* src0;
     const uint16_t* src1;
     const uint16_t** dst;
+    bool expert_bank;  // source holds every expert; this handle takes its own
   } tiled[] = {
       {{0, static_cast<int>(H), static_cast<int>(I), static_cast<long long>(2 * I * H),
         static_cast<long long>(2 * I * H)},
-       ecount, gate_up + static_cast<size_t>(ebase) * 2 * I * H, nullptr, &L.w.gate_up},
+       ecount, gate_up, nullptr, &L.w.gate_up, true},
       {{1, static_cast<int>(I), 0, static_cast<long long>(H * I), static_cast<long long>(H * I)},
-       ecount, down + static_cast<size_t>(ebase) * H * I, nullptr, &L.w.down},
+       ecount, down, nullptr, &L.w.down, true},
       {{0, static_cast<int>(H), 0, static_cast<long long>(2 * Is * H), static_cast<long long>(Is * H)}, 1,
-       shared_gate, shared_up, &L.w.sh_gate},
+       shared_gate, shared_up, &L.w.sh_gate, false},
       {{1, static_cast<int>(Is), 0, static_cast<long long>(H * Is), static_cast<long long>(H * Is)}, 1,
-       shared_down, nullptr, &L.w.sh_down},
+       shared_down, nullptr, &L.w.sh_down, false},
   };
   for (auto& t : tiled) {
+    const bool strided = t.expert_bank && world > 1;
     uint16_t* d = nullptr;
     int rc = alloc(h, &d, static_cast<size_t>(t.n_mats * t.spec.mat_elems), L.owned);
     if (rc != FW_OK) {
@@ -571,12 +570,13 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
     }
     const size_t src_elems = static_cast<size_t>(t.spec.src_mat_elems);
     const size_t per_chunk = std::max<size_t>(1, (size_t(256) << 20) / (src_elems * 2 * (t.src1 ? 2 : 1)));
-    const size_t chunk = std::min<size_t>(per_chunk, static_cast<size_t>(t.n_mats));
+    const size_t chunk = strided ? 1 : std::min<size_t>(per_chunk, static_cast<size_t>(t.n_mats));
     uint16_t* tmp = nullptr;
     cudaError_t e = cudaMalloc(&tmp, chunk * src_elems * 2 * (t.src1 ? 2 : 1));
     for (size_t m0 = 0; e == cudaSuccess && m0 < static_cast<size_t>(t.n_mats); m0 += chunk) {
       const size_t n = std::min(chunk, static_cast<size_t>(t.n_mats) - m0);
-      e = cudaMemcpy(tmp, t.src0 + m0 * src_elems, n * src_elems * 2, cudaMemcpyDefault);
+      const size_t sm = strided ? m0 * world + rank : m0;  // source matrix of local matrix m0
+      e = cudaMemcpy(tmp, t.src0 + sm * src_elems, n * src_elems * 2, cudaMemcpyDefault);
       if (e == cudaSuccess && t.src1)
         e = cudaMemcpy(tmp + n * src_elems, t.src1 + m0 * src_elems, n * src_elems * 2, cudaMemcpyDefault);
       if (e == cudaSuccess)
@@ -607,7 +607,8 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
     }
     L.w.bias = d;
   }
-  L.w.expert_base = ebase;
+  L.w.ep_rank = rank;
+  L.w.ep_world = world;
   L.w.expert_count = ecount;
   L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
@@ -647,8 +648,7 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
     }
     *it.dst = d;
   }
-  int ebase = 0, ecount = 0;
-  expert_range(h, &ebase, &ecount);
+  const int ecount = held_experts(h);
   // Expert banks (this handle's experts) and the shared expert: generated
   // straight into the tiled layout (element values are those of their
   // reference indices).
@@ -668,8 +668,10 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
       {{1, static_cast<int>(Is), 0, static_cast<long long>(H * Is), static_cast<long long>(H * Is)}, 1, 5, 5,
        &L.w.sh_down},
   };
-  tiled[0].spec.m0 = ebase;  // generator values of the held experts' global indices
-  tiled[1].spec.m0 = ebase;
+  for (int b = 0; b < 2; ++b) {  // generator values of the held experts' global indices
+    tiled[b].spec.m0 = h->ep_rank;
+    tiled[b].spec.m_stride = h->ep_world;
+  }
   for (auto& t : tiled) {
     uint16_t* d = nullptr;
     const int rc = alloc(h, &d, static_cast<size_t>(t.n_mats * t.spec.mat_elems), L.owned);
@@ -708,7 +710,8 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
     free_layer(L);
     return fail(FW_ECUDA, std::string("synth: ") + cudaGetErrorString(e));
   }
-  L.w.expert_base = ebase;
+  L.w.ep_rank = h->ep_rank;
+  L.w.ep_world = h->ep_world;
   L.w.expert_count = ecount;
   L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;

@@ -275,9 +275,9 @@ struct RouteArgs {
   int tgp, qpr, qps, ops;    // expert-kernel pass size, quads/octets per slot
   int* ticket;               // CTA completion counter (zero between calls)
   int* pair_count;           // [E] prefill path: per-expert pair counts to add into (or null)
-  // Schedule scope: routed experts [ep_base, ep_base + ep_count) (expert
+  // Schedule scope: routed experts e with e % ep_world == ep_rank (expert
   // parallelism: this GPU's experts), and the shared expert over sh_T tokens.
-  int ep_base, ep_count, sh_T;
+  int ep_rank, ep_world, sh_T;
 };
 
 // f32 total-order key with the index folded in (higher logit, then lower
@@ -351,7 +351,7 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     const int e = pidx[p];
-    if (e < a.ep_base || e >= a.ep_base + a.ep_count) continue;  // another GPU's expert
+    if (e % a.ep_world != a.ep_rank) continue;  // another GPU's expert
     const int t = p / K;
     atomicAdd(&cnt[e], 1);
     atomicOr(&mask[e * W + (t >> 6)], 1ull << (t & 63));
@@ -410,7 +410,7 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
   // tokens that selected the same expert (an expert appears once per token).
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     const int ex_id = pidx[p];
-    if (ex_id < a.ep_base || ex_id >= a.ep_base + a.ep_count) continue;
+    if (ex_id % a.ep_world != a.ep_rank) continue;
     const int t = p / K;
     const unsigned long long* m = mask + ex_id * W;
     int rank = 0;
@@ -545,10 +545,10 @@ struct CombineArgs {
   int H, K, T;
   const int32_t* sorted_slot;
   // Weighted row of token t's top-k position k: t*K + k, or with expert
-  // parallelism ((idx[t][k] / ep_experts) * T + t) * K + k (rows arrive
-  // per source GPU, T tokens each).
+  // parallelism ((idx[t][k] % ep_world) * T + t) * K + k (rows arrive per
+  // source GPU, T tokens each).
   const int32_t* idx;
-  int ep_experts;
+  int ep_world;
   const int32_t* row_of;  // if set: the row of (t, k) is row_of[t * K + k]
   const uint16_t* weighted;
   const uint16_t* gated_sh;
@@ -576,7 +576,7 @@ __global__ void k_combine(CombineArgs a) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int src =
-          (a.idx != nullptr && n0 + i < a.K) ? a.idx[static_cast<size_t>(t) * a.K + sl[i]] / a.ep_experts : 0;
+          (a.idx != nullptr && n0 + i < a.K) ? a.idx[static_cast<size_t>(t) * a.K + sl[i]] % a.ep_world : 0;
       row[i] = a.row_of != nullptr
                    ? static_cast<size_t>(n0 + i < a.K ? a.row_of[static_cast<size_t>(t) * a.K + sl[i]] : 0)
                    : (static_cast<size_t>(src) * a.T + t) * a.K + sl[i];
@@ -711,7 +711,7 @@ cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int co
 cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
                          uint16_t* score, int* err, cudaStream_t st) {
   RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-              0, 0, 0, 0, nullptr, nullptr, 0, E, T};
+              0, 0, 0, 0, nullptr, nullptr, 0, 1, T};
   return launch_route_kernel(a, st);
 }
 
@@ -742,22 +742,22 @@ cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& 
                                uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st) {
   RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
               sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, schedule ? sc.sched : nullptr, sc.up_done,
-              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket, pair_count, 0, s.E, T};
+              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket, pair_count, 0, 1, T};
   return launch_route_kernel(a, st);
 }
 
-cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_base,
-                               int ep_count, int sh_T, cudaStream_t st) {
+cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_rank,
+                               int ep_world, int sh_T, cudaStream_t st) {
   RouteArgs a{nullptr, T, s.E, s.K, const_cast<int32_t*>(idx_all), nullptr, sc.err,
               nullptr, nullptr, nullptr, nullptr, sc.sched, sc.up_done,
-              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, nullptr, nullptr, ep_base, ep_count, sh_T};
+              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, nullptr, nullptr, ep_rank, ep_world, sh_T};
   const int threads = (s.E + 31) / 32 * 32;
   return launch_pdl(k_schedule, dim3(1), dim3(threads), route_smem(s.E, T, s.K, true), st, a);
 }
 
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
-                           const int32_t* ep_idx, int ep_experts, const uint16_t* ep_rows, const int32_t* row_of) {
-  CombineArgs a{s.H, s.K, T, sc.sorted_slot, ep_idx, ep_experts > 0 ? ep_experts : s.E, row_of,
+                           const int32_t* ep_idx, int ep_world, const uint16_t* ep_rows, const int32_t* row_of) {
+  CombineArgs a{s.H, s.K, T, sc.sorted_slot, ep_idx, ep_world > 0 ? ep_world : 1, row_of,
                 ep_rows != nullptr ? ep_rows : sc.weighted, sc.gated_sh, y};
   return launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
 }

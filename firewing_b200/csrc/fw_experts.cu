@@ -61,7 +61,7 @@ struct ExpertsArgs {
   const uint16_t* sh_gate;  // [Is][H]
   const uint16_t* sh_up;    // [Is][H]
   const uint16_t* sh_down;  // [H][Is]
-  int expert_base;
+  int ep_world;             // bank index of expert e: e / ep_world
   const uint16_t* silu_lut;
   const int32_t* sched;
   const uint16_t* pair_score;  // [T*K]
@@ -192,14 +192,14 @@ __device__ void cursor_slot(Cursor& k, const Ctx& c) {
   k.cols = chunk_width(c, k.p.phase, s);
   if (k.p.phase == 0) {
     if (s < c.n_active) {
-      k.row0 = a.gate_up + static_cast<size_t>(c.act_ids[s] - a.expert_base) * 2 * a.I * a.H;
+      k.row0 = a.gate_up + static_cast<size_t>(c.act_ids[s] / a.ep_world) * 2 * a.I * a.H;
       k.row1 = k.row0 + static_cast<size_t>(a.I) * a.H;
     } else {
       k.row0 = a.sh_gate;  // tiled: the shared gate/up tiles
       k.row1 = a.sh_up;
     }
   } else {
-    k.row0 = s < c.n_active ? a.down + static_cast<size_t>(c.act_ids[s] - a.expert_base) * a.H * a.I
+    k.row0 = s < c.n_active ? a.down + static_cast<size_t>(c.act_ids[s] / a.ep_world) * a.H * a.I
                             : a.sh_down;
     k.row1 = nullptr;
   }
@@ -616,7 +616,7 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, experts_tokens_per_pass(s), x, w.gate_up, w.down, w.sh_gate,
-                w.sh_up, w.sh_down, w.expert_base, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
+                w.sh_up, w.sh_down, w.ep_world, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
                 sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err, sh_x, sh_T};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g_num_sms);

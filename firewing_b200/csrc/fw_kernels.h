@@ -41,7 +41,10 @@ struct LayerWeights {
   const uint16_t* sh_down = nullptr;
   const uint16_t* sh_gate_w = nullptr;
   const float* bias = nullptr;
-  int expert_base = 0;   // first expert id held (expert parallelism)
+  // Experts held: e with e % ep_world == ep_rank, bank index e / ep_world
+  // (expert parallelism interleaves the experts over the GPUs; one GPU
+  // holds all of them at their own index).
+  int ep_rank = 0, ep_world = 1;
   int expert_count = 0;  // experts held
   // Expert banks in the tiled layout (see TiledSpec) instead of the
   // reference layout; sh_gate then holds the shared gate/up tiles and sh_up
@@ -76,7 +79,8 @@ struct TiledSpec {
   int half;                // kind 0, one source: up rows start at row `half` of it; 0: two sources
   long long mat_elems;     // elements per matrix (expert) in the tiled buffer
   long long src_mat_elems; // elements per matrix in the reference source
-  long long m0 = 0;        // synthetic generation: global index of the bank's first matrix
+  long long m0 = 0;        // synthetic generation: global index of the bank's matrix 0 ...
+  long long m_stride = 1;  // ... and of matrix j: m0 + j * m_stride (interleaved expert placement)
 };
 
 // Scratch for one forward of up to max_T tokens (device memory).
@@ -184,17 +188,18 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
 // Prefill stages, composed by launch_prefill (one GPU) and by the
 // expert-parallel prefill forward (fw_api.cu):
 //   front: router + route of T tokens (pair counts when count_pairs);
-//   group: pairs of idx [n_pairs] with experts in [ebase, ebase + ecount)
-//          grouped by expert, their rows (x_src: row i / K) into xg; counts
-//          computed here when count_here; shared expert over sh_T tokens;
+//   group: pairs of idx [n_pairs] whose expert e has e % ep_world == ep_rank,
+//          grouped by bank index e / ep_world (ecount of them), their rows
+//          (x_src: row i / K) into xg; counts computed here when count_here;
+//          shared expert over sh_T tokens;
 //   gemms: gate/up and down GEMMs; weighted rows to out_rows at row t*K+k,
 //          or at send_pos[t*K+k] when send_pos is given.
 cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
                                  const uint16_t* x, int T, int32_t* topk_idx, uint16_t* topk_score, bool count_pairs,
                                  cudaStream_t st);
 cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_t* idx, int n_pairs,
-                                 const uint16_t* x_src, int ebase, int ecount, int sh_T, bool count_here,
-                                 cudaStream_t st);
+                                 const uint16_t* x_src, int ep_rank, int ep_world, int ecount, int sh_T,
+                                 bool count_here, cudaStream_t st);
 cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, const PrefillScratchMaps& smaps,
                                  const Luts& luts, const Scratch& sc, const uint16_t* x_own, int T_own, int ecount,
                                  const uint16_t* score, const int32_t* send_pos, uint16_t* out_rows,
@@ -202,7 +207,7 @@ cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, co
 // Packed positions of weighted rows for the expert-parallel exchange (see
 // k_ep_positions): send side over the gathered ids (group = token owner),
 // receive side over this rank's ids (group = computing GPU).
-cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int ep, int me, int world, bool recv,
+cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int me, int world, bool recv,
                                 int32_t* pos, int* count, int* offset, cudaStream_t st);
 
 // Stages shared with the decode path (fw_decode.cu).
@@ -210,16 +215,17 @@ cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& 
                           cudaStream_t st);
 cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& sc, int T, int32_t* topk_idx,
                                uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st);
-// ep_idx / ep_experts / ep_rows: expert parallelism (rows per source GPU,
+// ep_idx / ep_world / ep_rows: expert parallelism (rows per source GPU,
 // see CombineArgs); null / 0 / null on one GPU.
 // row_of: explicit row of every (t, k) in ep_rows (expert-parallel prefill).
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
-                           const int32_t* ep_idx = nullptr, int ep_experts = 0, const uint16_t* ep_rows = nullptr,
+                           const int32_t* ep_idx = nullptr, int ep_world = 0, const uint16_t* ep_rows = nullptr,
                            const int32_t* row_of = nullptr);
-// Expert parallelism: schedule of experts [ep_base, ep_base + ep_count)
-// over the gathered selections idx_all [T][K], shared expert over sh_T tokens.
-cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_base,
-                               int ep_count, int sh_T, cudaStream_t st);
+// Expert parallelism: schedule of this rank's experts (e % ep_world ==
+// ep_rank) over the gathered selections idx_all [T][K], shared expert over
+// sh_T tokens.
+cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_rank,
+                               int ep_world, int sh_T, cudaStream_t st);
 
 // ---- expert parallelism (fw_ep.cu): NCCL, loaded at run time ---------------
 // Each returns null on success, else a message.

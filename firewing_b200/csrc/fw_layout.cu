@@ -18,7 +18,7 @@ __device__ __forceinline__ uint64_t mix64_dev(uint64_t z) {
 __device__ __forceinline__ void tiled_source(const TiledSpec& s, long long d, int& src, long long& ref) {
   const long long ml = d / s.mat_elems;
   const long long dl = d - ml * s.mat_elems;
-  const long long m = ml + s.m0;
+  const long long m = ml * s.m_stride + s.m0;
   const long long seg = dl >> 9;  // 512 elements per 8 x 64 segment
   const int w = static_cast<int>(dl & 511);
   const int r = w >> 6, pc = w & 63;

@@ -196,7 +196,6 @@ extern "C" int fw_moe_forward_noalloc(const fw_moe_config* config, const fw_moe_
   lw.sh_down = w.shared_down;
   lw.sh_gate_w = w.shared_gate_w;
   lw.bias = w.logit_bias;
-  lw.expert_base = 0;
   lw.expert_count = c.experts;
   const fw::Luts luts{st->silu, st->sigmoid};
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);

@@ -777,10 +777,10 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
 // a copy of the token's input row into the grouped input (so the gate/up
 // GEMM reads each expert's token rows of a 64-column block as one
 // contiguous run).
-// Only pairs whose expert lies in [ebase, ebase + ecount) are grouped (this
-// GPU's experts under expert parallelism; all of them otherwise); slots are
-// relative to ebase.
-__global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, int ebase, int ecount,
+// Only pairs whose expert e has e % world == rank are grouped (this GPU's
+// experts under expert parallelism; all of them otherwise); the slot is the
+// bank index e / world.
+__global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, int rank, int world,
                              const int* offset, int* fill, int32_t* pair_tk, const uint16_t* x, uint16_t* xg,
                              long long xg_rows, int* err) {
   pdl_wait();
@@ -793,10 +793,10 @@ __global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, in
     if (e < 0 || e >= E) {
       set_error(err, kErrBadIndex);
       p = -1;
-    } else if (e < ebase || e >= ebase + ecount) {
+    } else if (e % world != rank) {
       p = -1;  // another GPU's expert
     } else {
-      p = offset[e - ebase] + atomicAdd(&fill[e - ebase], 1);
+      p = offset[e / world] + atomicAdd(&fill[e / world], 1);
       pair_tk[p] = i;
     }
   }
@@ -811,25 +811,25 @@ __global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, in
 
 // Expert parallelism: per-expert pair counts of this GPU's experts over
 // every rank's gathered selections.
-__global__ void k_ep_count(const int32_t* idx, int n, int ebase, int ecount, int* count) {
+__global__ void k_ep_count(const int32_t* idx, int n, int rank, int world, int ecount, int* count) {
   pdl_wait();
   pdl_launch_dependents();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int e = idx[i] - ebase;
-    if (e >= 0 && e < ecount) atomicAdd(&count[e], 1);
+    const int e = idx[i];
+    if (e >= 0 && e % world == rank && e / world < ecount) atomicAdd(&count[e / world], 1);
   }
 }
 
 // Expert parallelism: packed positions of weighted rows.  Entry i of idx
 // (a top-k id) belongs to group g with flag f:
-//   send mode: g = i / group_len (the token owner), f = (idx / ep == me);
-//   recv mode: g = idx / ep (the GPU that computed the row), f = 1.
+//   send mode: g = i / group_len (the token owner), f = (idx % world == me);
+//   recv mode: g = idx % world (the GPU that computed the row), f = 1.
 // pos[i] = offset[g] + (flagged entries of group g before i), else -1;
 // count[g], offset[g] (exclusive over g).  Entries in index order keep each
 // group's rows in (token, k) order on both sides.  One CTA of 1024 threads.
 constexpr int kEpMaxWorld = 8;
-__global__ void __launch_bounds__(1024) k_ep_positions(const int32_t* idx, int n, int group_len, int ep, int me,
-                                                        int world, int recv_mode, int32_t* pos, int* count,
+__global__ void __launch_bounds__(1024) k_ep_positions(const int32_t* idx, int n, int group_len, int me, int world,
+                                                        int recv_mode, int32_t* pos, int* count,
                                                         int* offset) {
   __shared__ int part[kEpMaxWorld][1025];
   __shared__ int tot[kEpMaxWorld], off[kEpMaxWorld];
@@ -838,7 +838,7 @@ __global__ void __launch_bounds__(1024) k_ep_positions(const int32_t* idx, int n
   const int tid = threadIdx.x, nt = blockDim.x;
   const int per = (n + nt - 1) / nt, i0 = tid * per, i1 = min(n, i0 + per);
   auto key = [&](int i) {
-    const int owner = idx[i] / ep;
+    const int owner = idx[i] % world;
     if (recv_mode) return owner;
     return owner == me ? i / group_len : -1;
   };
@@ -1011,21 +1011,22 @@ cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Lu
 }
 
 cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_t* idx, int n_pairs,
-                                 const uint16_t* x_src, int ebase, int ecount, int sh_T, bool count_here,
-                                 cudaStream_t st) {
+                                 const uint16_t* x_src, int ep_rank, int ep_world, int ecount, int sh_T,
+                                 bool count_here, cudaStream_t st) {
   cudaError_t e;
   if (count_here) {
     if ((e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * ecount, st)) != cudaSuccess) return e;
     const int blocks = std::min(4 * sm_count(), (n_pairs + 255) / 256 > 0 ? (n_pairs + 255) / 256 : 1);
-    if ((e = launch_pdl_ex(k_ep_count, dim3(blocks), dim3(256), 0, st, idx, n_pairs, ebase, ecount, sc.pair_count)) !=
+    if ((e = launch_pdl_ex(k_ep_count, dim3(blocks), dim3(256), 0, st, idx, n_pairs, ep_rank, ep_world, ecount,
+                           sc.pair_count)) !=
         cudaSuccess)
       return e;
   }
   OffsetsArgs oa{ecount, sh_T, 2 * s.I / kBM, 2 * s.Is / kBM, s.H / kBM, sc.pair_count, sc.pair_fill, sc.pair_offset,
                  sc.unit_prefix};
   if ((e = launch_pdl_ex(k_pf_offsets, dim3(1), dim3((ecount + 31) / 32 * 32), 0, st, oa)) != cudaSuccess) return e;
-  return launch_pdl_ex(k_pf_scatter, dim3((n_pairs + 7) / 8), dim3(256), 0, st, idx, n_pairs, s.K, s.E, s.H, ebase,
-                       ecount, static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x_src, sc.xg,
+  return launch_pdl_ex(k_pf_scatter, dim3((n_pairs + 7) / 8), dim3(256), 0, st, idx, n_pairs, s.K, s.E, s.H, ep_rank,
+                       ep_world, static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x_src, sc.xg,
                        static_cast<long long>(sc.pair_cap), sc.err);
 }
 
@@ -1083,10 +1084,10 @@ cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, co
   return launch_pdl_ex(k_gemm, grid, block, smem, st, wm.down, wm.sh_down, smaps.act, smaps.act_sh, g);
 }
 
-cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int ep, int me, int world, bool recv,
+cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int me, int world, bool recv,
                                 int32_t* pos, int* count, int* offset, cudaStream_t st) {
   if (world > kEpMaxWorld) return cudaErrorInvalidValue;
-  return launch_pdl_ex(k_ep_positions, dim3(1), dim3(1024), 0, st, idx, n, group_len, ep, me, world, recv ? 1 : 0,
+  return launch_pdl_ex(k_ep_positions, dim3(1), dim3(1024), 0, st, idx, n, group_len, me, world, recv ? 1 : 0,
                        pos, count, offset);
 }
 
@@ -1100,7 +1101,7 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   if ((e = mark(0)) != cudaSuccess) return e;
   if ((e = launch_prefill_front(s, w, luts, sc, x, T, topk_idx, topk_score, true, st)) != cudaSuccess) return e;
   if ((e = mark(1)) != cudaSuccess) return e;
-  if ((e = launch_prefill_group(s, sc, topk_idx, T * s.K, x, 0, s.E, T, false, st)) != cudaSuccess) return e;
+  if ((e = launch_prefill_group(s, sc, topk_idx, T * s.K, x, 0, 1, s.E, T, false, st)) != cudaSuccess) return e;
   if ((e = mark(2)) != cudaSuccess) return e;
   if ((e = launch_prefill_gemms(s, wm, smaps, luts, sc, x, T, s.E, topk_score, nullptr, sc.weighted, st)) !=
       cudaSuccess)

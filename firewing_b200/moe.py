@@ -245,21 +245,24 @@ class MoeBlock:
         return int(v.value)
 
 
-def ep_expert_range(experts: int, world: int, rank: int):
-    """(first expert, count) held by `rank` under expert parallelism."""
+def ep_owner(expert: int, world: int) -> int:
+    """Rank that holds `expert` under expert parallelism (interleaved
+    placement: expert e lives on rank e % world, at bank index e // world)."""
+    return expert % world
+
+
+def ep_held_experts(experts: int, world: int, rank: int):
+    """Experts held by `rank`, ascending."""
     if experts % world:
         raise ValueError("experts must divide evenly over the ranks")
-    per = experts // world
-    return rank * per, per
+    return list(range(rank, experts, world))
 
 
-def ep_combine_row(expert: int, t_local: int, k: int, tokens_local: int, top_k: int,
-                   experts_per_rank: int) -> int:
-    """Row of the combine's receive buffer that holds the weighted output of
-    expert `expert` for the owner's token t_local at top-k position k: the
+def ep_combine_row(expert: int, t_local: int, k: int, tokens_local: int, top_k: int, world: int) -> int:
+    """Row of the decode combine's receive buffer that holds the weighted
+    output of `expert` for the owner's token t_local at top-k position k: the
     rows arrive as one [tokens_local][top_k] block per source rank."""
-    src = expert // experts_per_rank
-    return (src * tokens_local + t_local) * top_k + k
+    return (ep_owner(expert, world) * tokens_local + t_local) * top_k + k
 
 
 def ep_unique_id() -> bytes:

@@ -5,8 +5,9 @@ for bit.
 
 Per rank: router and route on its own tokens; all-gather of token rows, top-k
 ids and route weights; its experts (ep_expert_range) over every gathered
-pair; the weighted rows returned to each token's owner in the receive layout
-of ep_combine_row; the owner's ascending-expert-id sum plus its shared expert.
+pair (ep_held_experts: interleaved placement); the weighted rows returned to
+each token's owner in the receive layout of ep_combine_row; the owner's
+ascending-expert-id sum plus its shared expert.
 """
 import os
 import socket
@@ -66,12 +67,12 @@ def _rank_main(rank: int, world: int, port: int, seed: int, t_local: int, zipf: 
         score_all = _gather(score, world)
         # 3. this rank's experts over every gathered pair: weighted rows in
         #    the [global token][K][H] send layout
-        base, per = fw.ep_expert_range(E, world, rank)
+        held = set(fw.ep_held_experts(E, world, rank))
         send = np.zeros((world * t_local * K, H), dtype=np.uint16)
         for t in range(world * t_local):
             for k in range(K):
                 e = int(idx_all[t, k])
-                if not (base <= e < base + per):
+                if e not in held:
                     continue
                 gu, dn = layer.expert(e)
                 g = O.linear_bf16(gu[: I * H], x_all[t], I, H)
@@ -89,7 +90,7 @@ def _rank_main(rank: int, world: int, port: int, seed: int, t_local: int, zipf: 
         for tl in range(t_local):
             acc = np.zeros(H, dtype=np.uint16)
             for k in np.argsort(idx[tl], kind="stable"):
-                row = fw.ep_combine_row(int(idx[tl, k]), tl, int(k), t_local, K, per)
+                row = fw.ep_combine_row(int(idx[tl, k]), tl, int(k), t_local, K, world)
                 acc = _bf16_add(acc, recv[row])
             sg = O.linear_bf16(layer.shared_gate, x[tl], Is, H)
             su = O.linear_bf16(layer.shared_up, x[tl], Is, H)
@@ -127,10 +128,11 @@ def test_ep_decomposition_matches_single_device_oracle(zipf):
 
 
 def test_ep_host_helpers():
-    assert fw.ep_expert_range(512, 8, 3) == (192, 64)
+    assert fw.ep_held_experts(512, 8, 3)[:3] == [3, 11, 19] and len(fw.ep_held_experts(512, 8, 3)) == 64
     with pytest.raises(ValueError):
-        fw.ep_expert_range(512, 3, 0)
-    # expert 70 lives on rank 1 of 8 (64 per rank): its rows arrive in block 1
-    assert fw.ep_combine_row(70, 5, 2, 32, 10, 64) == (1 * 32 + 5) * 10 + 2
+        fw.ep_held_experts(512, 3, 0)
+    # expert 70 lives on rank 70 % 8 = 6: its rows arrive in block 6
+    assert fw.ep_owner(70, 8) == 6
+    assert fw.ep_combine_row(70, 5, 2, 32, 10, 8) == (6 * 32 + 5) * 10 + 2
     # one rank: the single-GPU layout t*K + k
-    assert fw.ep_combine_row(511, 7, 9, 64, 10, 512) == 7 * 10 + 9
+    assert fw.ep_combine_row(511, 7, 9, 64, 10, 1) == 7 * 10 + 9
