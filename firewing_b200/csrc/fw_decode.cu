@@ -462,14 +462,17 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
     }
     __syncthreads();
     if (warp == 0) {
-      const int C = nw * K;
+      // Each warp's K candidates are in descending order: merge the nw lists
+      // as a tournament, lane w holding the head of warp w's list.  Keys
+      // are unique (the expert id is folded in), so one lane advances.
+      int head = 0;
+      uint32_t v = lane < nw ? cand[lane * K] : 0u;
       for (int k = 0; k < K; ++k) {
-        uint32_t best = 0;
-        for (int i = lane; i < C; i += 32) best = max(best, cand[i]);
-        const uint32_t m = __reduce_max_sync(0xffffffffu, best);
-        for (int i = lane; i < C; i += 32)
-          if (cand[i] == m) cand[i] = 0;
-        __syncwarp();
+        const uint32_t m = __reduce_max_sync(0xffffffffu, v);
+        if (v == m && m != 0u) {
+          ++head;
+          v = head < K ? cand[lane * K + head] : 0u;
+        }
         if (lane == 0) {
           sel[k] = 0xffff - static_cast<int>(m & 0xffffu);
           if (k == 0) ex[E + 1] = key_value(m);  // the largest logit
