@@ -40,6 +40,24 @@ int fail(int code, const std::string& msg) { return fail(code, msg.c_str()); }
                   cudaGetErrorString(e_));                                               \
   } while (0)
 
+// Host -> device copy that has landed when it returns.  A plain cudaMemcpy
+// from pageable memory may return once the bytes are staged, before the DMA
+// has written the destination, and it runs on the legacy default stream,
+// which a non-blocking stream does not wait for: a kernel launched there next
+// could read the destination early.  Copying on the consumer's stream and
+// synchronising that stream closes both gaps (cudaStreamLegacy where the
+// consumer's stream is not known yet).
+cudaError_t upload(void* dst, const void* src, size_t bytes, cudaStream_t st) {
+  const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, st);
+  return e != cudaSuccess ? e : cudaStreamSynchronize(st);
+}
+// Zero fill with the same guarantee (cudaMemset on device memory is
+// asynchronous with respect to the host).
+cudaError_t zero_fill(void* dst, size_t bytes, cudaStream_t st) {
+  const cudaError_t e = cudaMemsetAsync(dst, 0, bytes, st);
+  return e != cudaSuccess ? e : cudaStreamSynchronize(st);
+}
+
 // bf16 helpers with the reference arithmetic (src/expert.rs:315-322).
 uint16_t host_to_bf16(float v) {
   uint32_t b;
@@ -85,9 +103,9 @@ int device_common(int device, DeviceCommon** out) {
     FW_CUDA(cudaMalloc(&c.silu, 65536 * sizeof(uint16_t)));
     FW_CUDA(cudaMalloc(&c.sigmoid, 65536 * sizeof(uint16_t)));
     FW_CUDA(cudaMalloc(&c.err, sizeof(int)));
-    FW_CUDA(cudaMemcpy(c.silu, silu.data(), 65536 * sizeof(uint16_t), cudaMemcpyHostToDevice));
-    FW_CUDA(cudaMemcpy(c.sigmoid, sig.data(), 65536 * sizeof(uint16_t), cudaMemcpyHostToDevice));
-    FW_CUDA(cudaMemset(c.err, 0, sizeof(int)));
+    FW_CUDA(upload(c.silu, silu.data(), 65536 * sizeof(uint16_t), cudaStreamLegacy));
+    FW_CUDA(upload(c.sigmoid, sig.data(), 65536 * sizeof(uint16_t), cudaStreamLegacy));
+    FW_CUDA(zero_fill(c.err, sizeof(int), cudaStreamLegacy));
     it = g_common.emplace(device, c).first;
   }
   *out = &it->second;
@@ -127,6 +145,8 @@ struct OwnedLayer {
   bool loaded = false;
   bool prefill = false;           // tensor maps below are valid
   fw::PrefillWeightMaps maps{};   // the tiled banks as tensor-core operands
+  fw::HcWeights hc{};             // hyper-connection weights (fw_moe_load_hc)
+  std::vector<void*> hc_owned;
 };
 
 }  // namespace
@@ -175,6 +195,12 @@ struct fw_moe {
   int* ep_counts = nullptr;          // device [4][world]: send rows, send offsets, recv rows, recv offsets
   int* ep_counts_host = nullptr;     // pinned copy
   cudaEvent_t ep_counts_ev = nullptr;
+  // hyper-connection caller (allocated by the first fw_moe_load_hc)
+  fw::HcScratch hs{};
+  int hs_lowrank = 0;                // LR the scratch holds
+  uint16_t* hc_moe = nullptr;        // [M][H] block output inside a hyper-connection forward
+  uint16_t* hc_post_dev = nullptr;   // [M][4H] staging for fw_moe_forward_hc (host buffers)
+  uint16_t* hc_out_dev = nullptr;    // [M][4H]
 };
 
 namespace {
@@ -227,8 +253,6 @@ int check_handle(const fw_moe* h, int32_t layer) {
   return FW_OK;
 }
 
-// Experts this handle holds: all of them, or this rank's contiguous share
-// under expert parallelism.
 // Experts this handle holds: all of them, or under expert parallelism those
 // e with e % world == rank (bank index e / world).  Interleaving spreads a
 // skewed router's hot low-id experts over the GPUs.
@@ -427,12 +451,16 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
   auto& o = h->scratch_owned;
   int rc = FW_OK;
   do {
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      rc = fail(FW_ECUDA, "stream creation failed");
+      break;
+    }
     std::vector<uint16_t> silu, sig;
     build_tables(silu, sig);
     if ((rc = alloc(h, &h->silu, 65536, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->sigmoid, 65536, o)) != FW_OK) break;
-    if (cudaMemcpy(h->silu, silu.data(), 65536 * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(h->sigmoid, sig.data(), 65536 * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+    if (upload(h->silu, silu.data(), 65536 * 2, h->stream) != cudaSuccess ||
+        upload(h->sigmoid, sig.data(), 65536 * 2, h->stream) != cudaSuccess) {
       rc = fail(FW_ECUDA, "table upload failed");
       break;
     }
@@ -462,19 +490,16 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &h->y_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->idx_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->score_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
-    if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess || cudaMemset(s.ticket, 0, sizeof(int)) != cudaSuccess ||
-        cudaMemset(s.pair_count, 0, sizeof(int) * E) != cudaSuccess ||
-        cudaMemset(s.pair_fill, 0, sizeof(int) * E) != cudaSuccess) {
+    if (zero_fill(s.err, sizeof(int), h->stream) != cudaSuccess ||
+        zero_fill(s.ticket, sizeof(int), h->stream) != cudaSuccess ||
+        zero_fill(s.pair_count, sizeof(int) * E, h->stream) != cudaSuccess ||
+        zero_fill(s.pair_fill, sizeof(int) * E, h->stream) != cudaSuccess) {
       rc = fail(FW_ECUDA, "status reset failed");
       break;
     }
     h->prefill_ok = fw::prefill_supported(h->shape) && fw::make_prefill_scratch_maps(h->shape, s, &h->pf_maps);
     if (M > kDecodeMaxTokens && !h->prefill_ok) {
       rc = fail(FW_ECUDA, "prefill tensor maps could not be encoded");
-      break;
-    }
-    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
-      rc = fail(FW_ECUDA, "stream creation failed");
       break;
     }
   } while (false);
@@ -493,7 +518,10 @@ int fw_moe_destroy(fw_moe* h) {
   fw::ep_comm_destroy(h->ep);
   if (h->ep_counts_host) cudaFreeHost(h->ep_counts_host);
   if (h->ep_counts_ev) cudaEventDestroy(h->ep_counts_ev);
-  for (auto& L : h->layers) free_layer(L);
+  for (auto& L : h->layers) {
+    free_layer(L);
+    for (void* p : L.hc_owned) cudaFree(p);
+  }
   for (void* p : h->scratch_owned) cudaFree(p);
   if (h->stream) cudaStreamDestroy(h->stream);
   for (auto& ev : h->stage_ev)
@@ -531,7 +559,7 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
       free_layer(L);
       return rc;
     }
-    const cudaError_t e = cudaMemcpy(d, it.src, it.count * 2, cudaMemcpyDefault);
+    const cudaError_t e = upload(d, it.src, it.count * 2, h->stream);
     if (e != cudaSuccess) {
       free_layer(L);
       return fail(FW_ECUDA, "weight copy", cudaGetErrorString(e));
@@ -576,9 +604,11 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
     for (size_t m0 = 0; e == cudaSuccess && m0 < static_cast<size_t>(t.n_mats); m0 += chunk) {
       const size_t n = std::min(chunk, static_cast<size_t>(t.n_mats) - m0);
       const size_t sm = strided ? m0 * world + rank : m0;  // source matrix of local matrix m0
-      e = cudaMemcpy(tmp, t.src0 + sm * src_elems, n * src_elems * 2, cudaMemcpyDefault);
+      // copies and re-layout in order on the handle's stream
+      e = cudaMemcpyAsync(tmp, t.src0 + sm * src_elems, n * src_elems * 2, cudaMemcpyDefault, h->stream);
       if (e == cudaSuccess && t.src1)
-        e = cudaMemcpy(tmp + n * src_elems, t.src1 + m0 * src_elems, n * src_elems * 2, cudaMemcpyDefault);
+        e = cudaMemcpyAsync(tmp + n * src_elems, t.src1 + m0 * src_elems, n * src_elems * 2, cudaMemcpyDefault,
+                            h->stream);
       if (e == cudaSuccess)
         e = fw::launch_relayout(t.spec, static_cast<long long>(m0), static_cast<long long>(n), tmp,
                                 t.src1 ? tmp + n * src_elems : nullptr, d, h->stream);
@@ -601,7 +631,7 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
       free_layer(L);
       return rc;
     }
-    if (cudaMemcpy(d, logit_bias, E * 4, cudaMemcpyDefault) != cudaSuccess) {
+    if (upload(d, logit_bias, E * 4, h->stream) != cudaSuccess) {
       free_layer(L);
       return fail(FW_ECUDA, "bias copy failed");
     }
@@ -699,7 +729,7 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
       free_layer(L);
       return rc;
     }
-    if (cudaMemcpy(d, bias.data(), E * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    if (upload(d, bias.data(), E * 4, h->stream) != cudaSuccess) {
       free_layer(L);
       return fail(FW_ECUDA, "bias copy failed");
     }
@@ -765,7 +795,7 @@ int fw_moe_sync(fw_moe* h, void* stream) {
   int code = 0;
   FW_CUDA(cudaMemcpy(&code, h->sc.err, sizeof(int), cudaMemcpyDeviceToHost));
   if (code != 0) {
-    FW_CUDA(cudaMemset(h->sc.err, 0, sizeof(int)));
+    FW_CUDA(zero_fill(h->sc.err, sizeof(int), h->stream));
     return map_device_error(code);
   }
   if (h->ep != nullptr) {
@@ -787,6 +817,105 @@ int fw_moe_forward(fw_moe* h, int32_t layer, const uint16_t* x, int32_t tokens, 
   FW_TRY(fw_moe_forward_async(h, layer, h->x_dev, tokens, h->y_dev, h->idx_dev, h->score_dev,
                               h->stream));
   FW_CUDA(cudaMemcpyAsync(y, h->y_dev, tokens * H * 2, cudaMemcpyDefault, h->stream));
+  if (topk_idx)
+    FW_CUDA(cudaMemcpyAsync(topk_idx, h->idx_dev, tokens * K * 4, cudaMemcpyDefault, h->stream));
+  if (topk_scores)
+    FW_CUDA(cudaMemcpyAsync(topk_scores, h->score_dev, tokens * K * 2, cudaMemcpyDefault, h->stream));
+  return fw_moe_sync(h, h->stream);
+}
+
+int fw_moe_load_hc(fw_moe* h, int32_t layer, int32_t lowrank, const uint16_t* hc_norm, const uint16_t* mix_down,
+                   const uint16_t* mix_up, const uint16_t* inject) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  if (layer < 0 || layer >= h->cfg.layers) return fail(FW_EINVAL, "layer out of range");
+  if (lowrank <= 0 || lowrank % 32 != 0 || lowrank > 4096)
+    return fail(FW_EINVAL, "lowrank must be a positive multiple of 32, at most 4096");
+  if (!hc_norm || !mix_down || !mix_up || !inject) return fail(FW_EINVAL, "a hyper-connection weight is null");
+  if (h->cfg.hidden % 16 != 0) return fail(FW_EINVAL, "hidden must be a multiple of 16");
+  FW_CUDA(cudaSetDevice(h->device));
+  const size_t H = h->cfg.hidden, HH = 4 * H, LR = lowrank, M = h->cfg.max_tokens;
+  if (h->hs_lowrank < lowrank) {
+    // scratch for the largest lowrank seen (the other buffers once)
+    fw::HcScratch& s = h->hs;
+    if (h->hs_lowrank == 0) {
+      FW_TRY(alloc(h, &s.normed, M * HH, h->scratch_owned));
+      FW_TRY(alloc(h, &s.up, M * HH, h->scratch_owned));
+      FW_TRY(alloc(h, &s.inject, M * 4, h->scratch_owned));
+      FW_TRY(alloc(h, &s.mixed, M * H, h->scratch_owned));
+      FW_TRY(alloc(h, &s.inj_w, M * 4, h->scratch_owned));
+      FW_TRY(alloc(h, &h->hc_moe, M * H, h->scratch_owned));
+      FW_TRY(alloc(h, &h->hc_post_dev, M * HH, h->scratch_owned));
+      FW_TRY(alloc(h, &h->hc_out_dev, M * HH, h->scratch_owned));
+      FW_TRY(alloc(h, &s.down, M * LR, h->scratch_owned));
+    } else {
+      FW_TRY(regrow(h, &s.down, M * LR));
+    }
+    h->hs_lowrank = lowrank;
+  }
+  OwnedLayer& L = h->layers[layer];
+  for (void* p : L.hc_owned) cudaFree(p);
+  L.hc_owned.clear();
+  L.hc = fw::HcWeights{};
+  struct Item {
+    const uint16_t* src;
+    size_t count;
+    const uint16_t** dst;
+  } items[] = {{hc_norm, HH, &L.hc.norm}, {mix_down, LR * HH, &L.hc.mix_down}, {mix_up, HH * LR, &L.hc.mix_up},
+               {inject, 4 * HH, &L.hc.inject}};
+  for (auto& it : items) {
+    uint16_t* d = nullptr;
+    const int rc = alloc(h, &d, it.count, L.hc_owned);
+    if (rc != FW_OK) return rc;
+    FW_CUDA(upload(d, it.src, it.count * 2, h->stream));
+    *it.dst = d;
+  }
+  L.hc.lowrank = lowrank;
+  return FW_OK;
+}
+
+int fw_moe_forward_hc_async(fw_moe* h, int32_t layer, const uint16_t* post, int32_t tokens, uint16_t* out,
+                            int32_t* topk_idx, uint16_t* topk_scores, void* stream) {
+  FW_TRY(check_handle(h, layer));
+  const OwnedLayer& L = h->layers[layer];
+  if (L.hc.lowrank == 0) return fail(FW_EINVAL, "layer has no hyper-connection weights (fw_moe_load_hc)");
+  if (h->ep != nullptr) return fail(FW_EINVAL, "the hyper-connection forward is single-GPU");
+  if (tokens < 0 || tokens > h->cfg.max_tokens) return fail(FW_EINVAL, "tokens out of range");
+  if (tokens == 0) return FW_OK;
+  if (post == nullptr || out == nullptr) return fail(FW_EINVAL, "post / out is null");
+  if (!aligned16(post) || !aligned16(out)) return fail(FW_EINVAL, "post / out must be 16-byte aligned");
+  if (!aligned4(topk_idx) || !aligned4(topk_scores))
+    return fail(FW_EINVAL, "topk buffers must be 4-byte aligned");
+  FW_CUDA(cudaSetDevice(h->device));
+  const cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  cudaError_t e = fw::launch_hc_pre(L.hc, h->hs, h->luts, post, h->cfg.hidden, tokens, cs);
+  if (e != cudaSuccess) return fail(FW_ECUDA, std::string("hyper-connection launch: ") + cudaGetErrorString(e));
+  int32_t* idx = topk_idx ? topk_idx : h->idx_dev;
+  uint16_t* sc = topk_scores ? topk_scores : h->score_dev;
+  const fw::HcPost hp{post, h->hs.inj_w, out};
+  const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
+  if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
+  cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
+  e = prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, h->sc, h->hs.mixed, tokens, h->hc_moe,
+                                   idx, sc, cs, ev, &hp)
+              : fw::launch_block(h->shape, L.w, h->luts, h->sc, h->hs.mixed, tokens, h->hc_moe, idx, sc, cs, ev,
+                                 &hp);
+  if (e != cudaSuccess) return fail(FW_ECUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return FW_OK;
+}
+
+int fw_moe_forward_hc(fw_moe* h, int32_t layer, const uint16_t* post, int32_t tokens, uint16_t* out,
+                      int32_t* topk_idx, uint16_t* topk_scores) {
+  FW_TRY(check_handle(h, layer));
+  if (tokens < 0 || tokens > h->cfg.max_tokens) return fail(FW_EINVAL, "tokens out of range");
+  if (tokens == 0) return FW_OK;
+  if (post == nullptr || out == nullptr) return fail(FW_EINVAL, "post / out is null");
+  if (h->hc_post_dev == nullptr) return fail(FW_EINVAL, "no hyper-connection weights loaded (fw_moe_load_hc)");
+  FW_CUDA(cudaSetDevice(h->device));
+  const size_t HH = 4 * static_cast<size_t>(h->cfg.hidden), K = h->cfg.top_k;
+  FW_CUDA(cudaMemcpyAsync(h->hc_post_dev, post, tokens * HH * 2, cudaMemcpyDefault, h->stream));
+  FW_TRY(fw_moe_forward_hc_async(h, layer, h->hc_post_dev, tokens, h->hc_out_dev, h->idx_dev, h->score_dev,
+                                 h->stream));
+  FW_CUDA(cudaMemcpyAsync(out, h->hc_out_dev, tokens * HH * 2, cudaMemcpyDefault, h->stream));
   if (topk_idx)
     FW_CUDA(cudaMemcpyAsync(topk_idx, h->idx_dev, tokens * K * 4, cudaMemcpyDefault, h->stream));
   if (topk_scores)
@@ -863,7 +992,7 @@ int fw_route_bf16(const uint16_t* logits, int32_t tokens, int32_t experts, int32
   int code = 0;
   FW_CUDA(cudaMemcpy(&code, c->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (code != 0) {
-    FW_CUDA(cudaMemset(c->err, 0, sizeof(int)));
+    FW_CUDA(zero_fill(c->err, sizeof(int), st));
     return map_device_error(code);
   }
   return FW_OK;
@@ -878,7 +1007,7 @@ bool firewing_cuda_topk_bf16(const uint16_t* values, size_t count, size_t k, siz
   uint16_t* ds = nullptr;
   bool ok = cudaMalloc(&dv, count * 2) == cudaSuccess && cudaMalloc(&di, k * 4) == cudaSuccess &&
             cudaMalloc(&ds, k * 2) == cudaSuccess &&
-            cudaMemcpy(dv, values, count * 2, cudaMemcpyHostToDevice) == cudaSuccess;
+            upload(dv, values, count * 2, cudaStreamLegacy) == cudaSuccess;
   std::vector<int32_t> idx(k);
   if (ok) {
     ok = fw_route_bf16(dv, 1, static_cast<int32_t>(count), static_cast<int32_t>(k), di, ds, nullptr) ==

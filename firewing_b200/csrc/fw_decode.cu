@@ -556,6 +556,7 @@ struct CombineArgs {
   const uint16_t* weighted;
   const uint16_t* gated_sh;
   uint16_t* y;
+  HcPost hc;  // hyper-connection injection (hc.out null: none)
 };
 
 __global__ void k_combine(CombineArgs a) {
@@ -609,6 +610,26 @@ __global__ void k_combine(CombineArgs a) {
     o[i] = l | (h << 16);
   }
   *reinterpret_cast<uint4*>(a.y + static_cast<size_t>(t) * a.H + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  if (a.hc.out == nullptr) return;
+  // Hyper-connection injection (src/decoder_layer.rs:587-607):
+  // out[g*H + c] = add_bf16(post[g*H + c], bf16(moe[c] * w[g])).
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float wg = bf16_to_f32(a.hc.inj_w[static_cast<size_t>(t) * 4 + g]);
+    const size_t off = static_cast<size_t>(t) * 4 * a.H + static_cast<size_t>(g) * a.H + c;
+    const uint4 pv = *reinterpret_cast<const uint4*>(a.hc.post + off);
+    const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+    uint32_t r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t pl = f32_to_bf16(__fmul_rn(lo_bf16(o[i]), wg));
+      const uint32_t ph = f32_to_bf16(__fmul_rn(hi_bf16(o[i]), wg));
+      const uint32_t l = f32_to_bf16(__fadd_rn(lo_bf16(pw[i]), bf16_to_f32(pl)));
+      const uint32_t h = f32_to_bf16(__fadd_rn(hi_bf16(pw[i]), bf16_to_f32(ph)));
+      r[i] = l | (h << 16);
+    }
+    *reinterpret_cast<uint4*>(a.hc.out + off) = make_uint4(r[0], r[1], r[2], r[3]);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -759,15 +780,16 @@ cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t*
 }
 
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
-                           const int32_t* ep_idx, int ep_world, const uint16_t* ep_rows, const int32_t* row_of) {
+                           const int32_t* ep_idx, int ep_world, const uint16_t* ep_rows, const int32_t* row_of,
+                           const HcPost* hc) {
   CombineArgs a{s.H, s.K, T, sc.sorted_slot, ep_idx, ep_world > 0 ? ep_world : 1, row_of,
-                ep_rows != nullptr ? ep_rows : sc.weighted, sc.gated_sh, y};
+                ep_rows != nullptr ? ep_rows : sc.weighted, sc.gated_sh, y, hc != nullptr ? *hc : HcPost{}};
   return launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
 }
 
 cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
                          const uint16_t* x, int T, uint16_t* y, int32_t* topk_idx,
-                         uint16_t* topk_score, cudaStream_t st, cudaEvent_t* ev) {
+                         uint16_t* topk_score, cudaStream_t st, cudaEvent_t* ev, const HcPost* hc) {
   if (T <= 0) return cudaSuccess;
   cudaError_t e;
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
@@ -782,7 +804,7 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
   e = launch_experts(s, w, luts, sc, x, T, topk_score, st, x, T);
   if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
   // 4. combine
-  e = launch_combine(s, sc, T, y, st);
+  e = launch_combine(s, sc, T, y, st, nullptr, 0, nullptr, nullptr, hc);
   if (e == cudaSuccess) e = mark(4);
   return e;
 }

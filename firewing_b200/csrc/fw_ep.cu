@@ -1,7 +1,7 @@
 // fw_ep.cu -- the collectives of expert parallelism, over NCCL.
 //
-// With expert parallelism, rank r of N holds experts [r*E/N, (r+1)*E/N) of
-// every layer and brings its own T tokens to each forward.  A layer then
+// With expert parallelism, rank r of N holds the experts e with e % N == r
+// of every layer and brings its own T tokens to each forward.  A layer then
 // moves data twice (the block's only exchange steps):
 //   dispatch: every rank's token rows, top-k ids and route weights are
 //             gathered on every rank (three all-gathers in one NCCL group);

@@ -129,6 +129,33 @@ struct Luts {
   const uint16_t* sigmoid = nullptr;
 };
 
+// ---- hyper-connection caller (fw_hc.cu) -------------------------------------
+struct HcWeights {
+  const uint16_t* norm = nullptr;      // [4H] hc_norm
+  const uint16_t* mix_down = nullptr;  // [LR][4H] input_mix_weight_down
+  const uint16_t* mix_up = nullptr;    // [4H][LR] input_mix_weight_up
+  const uint16_t* inject = nullptr;    // [4][4H] block_inject_weight
+  int lowrank = 0;                     // LR (multiple of 32)
+};
+struct HcScratch {
+  uint16_t* normed = nullptr;  // [T][4H]
+  uint16_t* down = nullptr;    // [T][LR]
+  uint16_t* up = nullptr;      // [T][4H]
+  uint16_t* inject = nullptr;  // [T][4]
+  uint16_t* mixed = nullptr;   // [T][H] the block input
+  uint16_t* inj_w = nullptr;   // [T][4] injection weights
+};
+// The injection after the block, done in the combine's epilogue:
+// out[t][g*H + c] = bf16(post[t][g*H + c] + bf16(y[t][c] * inj_w[t][g])).
+struct HcPost {
+  const uint16_t* post = nullptr;   // [T][4H] attention output (the residual streams)
+  const uint16_t* inj_w = nullptr;  // [T][4]
+  uint16_t* out = nullptr;          // [T][4H] layer output
+};
+// Everything before the block: post [T][4H] -> hs.mixed [T][H], hs.inj_w.
+cudaError_t launch_hc_pre(const HcWeights& w, const HcScratch& hs, const Luts& luts, const uint16_t* post, int H,
+                          int T, cudaStream_t st);
+
 // Pipeline stages of one block forward (for per-stage timing).
 enum Stage : int { kStageRouter = 0, kStageRoute, kStageExperts, kStageCombine, kStages };
 
@@ -137,7 +164,7 @@ enum Stage : int { kStageRouter = 0, kStageRoute, kStageExperts, kStageCombine, 
 cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts,
                          const Scratch& sc, const uint16_t* x, int T, uint16_t* y,
                          int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
-                         cudaEvent_t* stage_events = nullptr);
+                         cudaEvent_t* stage_events = nullptr, const HcPost* hc = nullptr);
 
 // The persistent expert kernel (gate_up + SwiGLU and down + scale for every
 // active expert and the shared expert); dynamic shared memory it needs.
@@ -184,7 +211,7 @@ bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratch
 cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
                            const PrefillScratchMaps& sm, const Luts& luts, const Scratch& sc, const uint16_t* x,
                            int T, uint16_t* y, int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
-                           cudaEvent_t* stage_events = nullptr);
+                           cudaEvent_t* stage_events = nullptr, const HcPost* hc = nullptr);
 // Prefill stages, composed by launch_prefill (one GPU) and by the
 // expert-parallel prefill forward (fw_api.cu):
 //   front: router + route of T tokens (pair counts when count_pairs);
@@ -218,9 +245,10 @@ cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& 
 // ep_idx / ep_world / ep_rows: expert parallelism (rows per source GPU,
 // see CombineArgs); null / 0 / null on one GPU.
 // row_of: explicit row of every (t, k) in ep_rows (expert-parallel prefill).
+// hc: the hyper-connection injection, fused into the epilogue (or null).
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
                            const int32_t* ep_idx = nullptr, int ep_world = 0, const uint16_t* ep_rows = nullptr,
-                           const int32_t* row_of = nullptr);
+                           const int32_t* row_of = nullptr, const HcPost* hc = nullptr);
 // Expert parallelism: schedule of this rank's experts (e % ep_world ==
 // ep_rank) over the gathered selections idx_all [T][K], shared expert over
 // sh_T tokens.

@@ -94,11 +94,14 @@ int setup_device(int dev, DeviceState** out) {
     if ((e = cudaGetSymbolAddress(&p, g_sigmoid_table)) != cudaSuccess)
       return cuda_fail("sigmoid table address", e);
     st.sigmoid = static_cast<uint16_t*>(p);
-    if ((e = cudaMemcpy(st.silu, g_host_silu, sizeof g_host_silu, cudaMemcpyHostToDevice)) != cudaSuccess)
+    if ((e = cudaMemcpyAsync(st.silu, g_host_silu, sizeof g_host_silu, cudaMemcpyHostToDevice,
+                             cudaStreamLegacy)) != cudaSuccess)
       return cuda_fail("silu table upload", e);
-    if ((e = cudaMemcpy(st.sigmoid, g_host_sigmoid, sizeof g_host_sigmoid, cudaMemcpyHostToDevice)) !=
-        cudaSuccess)
+    if ((e = cudaMemcpyAsync(st.sigmoid, g_host_sigmoid, sizeof g_host_sigmoid, cudaMemcpyHostToDevice,
+                             cudaStreamLegacy)) != cudaSuccess)
       return cuda_fail("sigmoid table upload", e);
+    // landed before any stream reads them (pageable copies may return early)
+    if ((e = cudaStreamSynchronize(cudaStreamLegacy)) != cudaSuccess) return cuda_fail("table upload", e);
     st.ready = true;
   }
   *out = &st;

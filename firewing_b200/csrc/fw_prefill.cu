@@ -1094,7 +1094,7 @@ cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int me
 cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
                            const PrefillScratchMaps& smaps, const Luts& luts, const Scratch& sc, const uint16_t* x,
                            int T, uint16_t* y, int32_t* topk_idx, uint16_t* topk_score, cudaStream_t st,
-                           cudaEvent_t* ev) {
+                           cudaEvent_t* ev, const HcPost* hc) {
   if (T <= 0) return cudaSuccess;
   cudaError_t e;
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
@@ -1107,7 +1107,7 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
       cudaSuccess)
     return e;
   if ((e = mark(3)) != cudaSuccess) return e;
-  if ((e = launch_combine(s, sc, T, y, st)) != cudaSuccess) return e;
+  if ((e = launch_combine(s, sc, T, y, st, nullptr, 0, nullptr, nullptr, hc)) != cudaSuccess) return e;
   return mark(4);
 }
 

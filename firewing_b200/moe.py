@@ -89,6 +89,9 @@ def library() -> ctypes.CDLL:
     L.fw_moe_sync.argtypes = [vp, vp]
     L.fw_moe_set_prefill_min_tokens.argtypes = [vp, ctypes.c_int32]
     L.fw_ep_unique_id.argtypes = [ctypes.c_char_p]
+    L.fw_moe_load_hc.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, vp, vp, vp, vp]
+    L.fw_moe_forward_hc.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp]
+    L.fw_moe_forward_hc_async.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp, vp]
     L.fw_moe_ep_init.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_char_p]
     L.fw_moe_memory.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_profile.argtypes = [vp, ctypes.c_int32]
@@ -104,7 +107,8 @@ def library() -> ctypes.CDLL:
     for name in ("fw_moe_create", "fw_moe_destroy", "fw_moe_load_layer", "fw_moe_synth_layer",
                  "fw_moe_forward", "fw_moe_forward_async", "fw_moe_sync", "fw_moe_memory",
                  "fw_moe_profile", "fw_moe_profile_read", "fw_moe_set_prefill_min_tokens",
-                 "fw_ep_unique_id", "fw_moe_ep_init",
+                 "fw_ep_unique_id", "fw_moe_ep_init", "fw_moe_load_hc", "fw_moe_forward_hc",
+                 "fw_moe_forward_hc_async",
                  "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
@@ -224,6 +228,25 @@ class MoeBlock:
         if len(unique_id) != 128:
             raise ValueError("unique_id must be 128 bytes")
         _check(library().fw_moe_ep_init(self._h, int(rank), int(world), bytes(unique_id)))
+
+    def load_hc(self, layer: int, lowrank: int, hc_norm, mix_down, mix_up, inject) -> None:
+        """Hyper-connection weights of one layer (host arrays or device tensors):
+        hc_norm [4H], mix_down [lowrank][4H], mix_up [4H][lowrank], inject [4][4H]."""
+        keep = [np.ascontiguousarray(a) if isinstance(a, np.ndarray) else a
+                for a in (hc_norm, mix_down, mix_up, inject)]
+        _check(library().fw_moe_load_hc(self._h, layer, lowrank, *[_ptr(a) for a in keep]))
+
+    def forward_hc(self, layer: int, post: np.ndarray):
+        """Attention output post [T][4H] (host) -> (layer output [T][4H],
+        top-k ids [T][K], scores [T][K]) through the hyper-connection caller
+        and the block."""
+        post = np.ascontiguousarray(post, dtype=np.uint16)
+        T = post.shape[0]
+        out = np.empty_like(post)
+        idx = np.empty((T, self.config.top_k), dtype=np.int32)
+        sc = np.empty((T, self.config.top_k), dtype=np.uint16)
+        _check(library().fw_moe_forward_hc(self._h, layer, _ptr(post), T, _ptr(out), _ptr(idx), _ptr(sc)))
+        return out, idx, sc
 
     def set_prefill_min_tokens(self, min_tokens: int) -> None:
         """Forwards of at least min_tokens tokens (and all above 256) take the

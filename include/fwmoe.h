@@ -111,6 +111,28 @@ int fw_moe_forward_async(fw_moe* handle, int32_t layer, const uint16_t* x, int32
                          uint16_t* y, int32_t* topk_idx, uint16_t* topk_scores,
                          void* stream);
 
+/* The hyper-connection caller on either side of the block
+ * (src/hyper_connection.rs:412-490, src/decoder_layer.rs:451-458, 587-607).
+ * fw_moe_load_hc copies one layer's weights (host or device pointers):
+ * hc_norm [4H], input_mix_weight_down [lowrank][4H], input_mix_weight_up
+ * [4H][lowrank], block_inject_weight [4][4H]; lowrank a multiple of 32.
+ * fw_moe_forward_hc maps the attention output post [T][4H] (four residual
+ * streams) to the layer output [T][4H]:
+ *   - grouped RMS norm, the low-rank input mix and the injection weights
+ *     give the block input mixed [T][H];
+ *   - the block runs on it;
+ *   - out[g*H + c] = bf16(post[g*H + c] + bf16(moe[c] * w[g])), fused into
+ *     the combine.
+ * Every rounding point is the reference's, so decode-width outputs are bit
+ * for bit the reference's.  Host buffers (forward_hc) or device buffers
+ * (forward_hc_async, stream-ordered); single GPU only. */
+int fw_moe_load_hc(fw_moe* handle, int32_t layer, int32_t lowrank, const uint16_t* hc_norm,
+                   const uint16_t* mix_down, const uint16_t* mix_up, const uint16_t* inject);
+int fw_moe_forward_hc(fw_moe* handle, int32_t layer, const uint16_t* post, int32_t tokens,
+                      uint16_t* out, int32_t* topk_idx, uint16_t* topk_scores);
+int fw_moe_forward_hc_async(fw_moe* handle, int32_t layer, const uint16_t* post, int32_t tokens,
+                            uint16_t* out, int32_t* topk_idx, uint16_t* topk_scores, void* stream);
+
 /* Forwards of at least `min_tokens` tokens (and every forward wider than
  * 256 tokens) run the prefill path: the expert FFNs as grouped bf16 GEMMs on
  * the tensor cores (f32 accumulation in the tensor core's own order, outputs
@@ -123,8 +145,11 @@ int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);
 
 /* Expert parallelism over the GPUs of one node (no reference counterpart:
  * the reference runs the block on one device).  Rank r of `world` holds the
- * routed experts [r*E/world, (r+1)*E/world) of every layer (router, shared
- * expert and bias replicated) and brings its own tokens to each forward.
+ * routed experts e with e % world == r of every layer, at bank index
+ * e / world (interleaved, so a skewed router's hot low ids spread over the
+ * ranks; router, shared expert and bias replicated), and brings its own
+ * tokens to each forward.  fw_moe_load_layer takes the full checkpoint banks
+ * and keeps this rank's experts.
  * Per layer:
  *   - router and route run on the rank's own tokens;
  *   - an all-gather brings every rank's token rows, top-k ids and route

@@ -74,6 +74,10 @@ def build() -> None:
 _lib = None
 
 
+class _HcLayer(ctypes.Structure):
+    _fields_ = [("norm", u16p), ("mix_down", u16p), ("mix_up", u16p), ("inject", u16p)]
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
@@ -112,6 +116,14 @@ def lib() -> ctypes.CDLL:
         L.fwo_synth_input.argtypes = [ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32, u16p]
         L.fwo_zipf_bias.argtypes = [ctypes.c_int32, f32p]
         L.fwo_make_hidden.argtypes = [ctypes.c_size_t, ctypes.POINTER(InputSpec), u16p]
+        L.fwo_inner_square_sum.restype = ctypes.c_float
+        L.fwo_inner_square_sum.argtypes = [f32p, ctypes.c_size_t]
+        L.fwo_grouped_rms.argtypes = [u16p, u16p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_float, u16p]
+        L.fwo_four_stream_mean.restype = ctypes.c_float
+        L.fwo_four_stream_mean.argtypes = [f32p]
+        L.fwo_hc_pre.argtypes = [u16p, ctypes.POINTER(_HcLayer), ctypes.c_size_t, ctypes.c_size_t, u16p, u16p,
+                                 u16p]
+        L.fwo_hc_post.argtypes = [u16p, u16p, u16p, ctypes.c_size_t, u16p]
         _lib = L
     return _lib
 
@@ -378,3 +390,65 @@ def reference_topk_shim():
         return list(out) if ok else None
 
     return call
+
+
+# ---- hyper-connection caller (src/hyper_connection.rs) -----------------------
+
+def inner_square_sum(values: np.ndarray) -> float:
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    return float(lib().fwo_inner_square_sum(_pf(v), v.size))
+
+
+def grouped_rms(x: np.ndarray, weight: np.ndarray, hidden: int, eps: float = 1.0e-6) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    out = np.empty_like(x)
+    lib().fwo_grouped_rms(_p16(x), _p16(np.ascontiguousarray(weight, dtype=np.uint16)), hidden,
+                          x.size // hidden, eps, _p16(out))
+    return out
+
+
+def four_stream_mean(values) -> float:
+    v = np.asarray(values, dtype=np.float32)
+    return float(lib().fwo_four_stream_mean(_pf(v)))
+
+
+class HcLayer:
+    """Seeded synthetic hyper-connection weights for one layer: hc_norm [4H],
+    input_mix_weight_down [LR][4H], input_mix_weight_up [4H][LR],
+    block_inject_weight [4][4H]."""
+
+    T_NORM, T_DOWN, T_UP, T_INJECT = 20, 21, 22, 23
+
+    def __init__(self, hidden: int, lowrank: int, seed: int, std: float = 0.02):
+        HH = 4 * hidden
+        self.hidden, self.lowrank = hidden, lowrank
+        self.norm = synth_bf16(seed, self.T_NORM, 0, HH, std)
+        self.mix_down = synth_bf16(seed, self.T_DOWN, 0, lowrank * HH, std)
+        self.mix_up = synth_bf16(seed, self.T_UP, 0, HH * lowrank, std)
+        self.inject = synth_bf16(seed, self.T_INJECT, 0, 4 * HH, std)
+
+    def c(self):
+        return _HcLayer(_p16(self.norm), _p16(self.mix_down), _p16(self.mix_up), _p16(self.inject))
+
+
+def hc_pre(layer: HcLayer, post: np.ndarray):
+    """post [T][4H] -> (mixed [T][H], injection weights [T][4])."""
+    post = np.ascontiguousarray(post, dtype=np.uint16)
+    T, H = post.shape[0], layer.hidden
+    mixed = np.empty((T, H), dtype=np.uint16)
+    inj = np.empty((T, 4), dtype=np.uint16)
+    c = layer.c()
+    for t in range(T):
+        lib().fwo_hc_pre(_p16(post[t]), ctypes.byref(c), H, layer.lowrank, _p16(mixed[t]), _p16(inj[t]), None)
+    return mixed, inj
+
+
+def hc_post(post: np.ndarray, moe: np.ndarray, inj: np.ndarray) -> np.ndarray:
+    post = np.ascontiguousarray(post, dtype=np.uint16)
+    moe = np.ascontiguousarray(moe, dtype=np.uint16)
+    inj = np.ascontiguousarray(inj, dtype=np.uint16)
+    T, H = moe.shape
+    out = np.empty_like(post)
+    for t in range(T):
+        lib().fwo_hc_post(_p16(post[t]), _p16(moe[t]), _p16(inj[t]), H, _p16(out[t]))
+    return out

@@ -461,3 +461,145 @@ int fwo_make_hidden(size_t size, const fwo_input_spec* spec, uint16_t* out) {
     }
     return 0;
 }
+
+/* ---- hyper-connection caller -------------------------------------------- */
+
+/* src/hyper_connection.rs:211-283: four lanes x four interleaved registers
+ * x four cascade levels of f32 accumulators, each square rounded before its
+ * add (no fused multiply-add). */
+float fwo_inner_square_sum(const float* values, size_t n) {
+    enum { LANES = 4, INTERLEAVE = 4, LEVELS = 4 };
+    const size_t vector_count = n / LANES;
+    const size_t cascade_size = vector_count / INTERLEAVE;
+    size_t ceil_log2 = 0;
+    if (cascade_size > 1) {
+        size_t v = cascade_size - 1;
+        while (v) { ++ceil_log2; v >>= 1; }
+    }
+    const size_t level_power = (ceil_log2 / LEVELS) > 4 ? (ceil_log2 / LEVELS) : 4;
+    const size_t level_step = (size_t)1 << level_power;
+    const size_t level_mask = level_step - 1;
+    float acc[LEVELS][INTERLEAVE][LANES];
+    memset(acc, 0, sizeof acc);
+    size_t index = 0;
+    while (index + level_step <= cascade_size) {
+        for (size_t s = 0; s < level_step; ++s) {
+            for (int r = 0; r < INTERLEAVE; ++r) {
+                const size_t base = (index * INTERLEAVE + r) * LANES;
+                for (int l = 0; l < LANES; ++l) {
+                    const float sq = values[base + l] * values[base + l];
+                    acc[0][r][l] = acc[0][r][l] + sq;
+                }
+            }
+            ++index;
+        }
+        for (int level = 1; level < LEVELS; ++level) {
+            for (int r = 0; r < INTERLEAVE; ++r)
+                for (int l = 0; l < LANES; ++l) {
+                    acc[level][r][l] = acc[level][r][l] + acc[level - 1][r][l];
+                    acc[level - 1][r][l] = 0.0f;
+                }
+            if (index & (level_mask << (level * level_power))) break;
+        }
+    }
+    while (index < cascade_size) {
+        for (int r = 0; r < INTERLEAVE; ++r) {
+            const size_t base = (index * INTERLEAVE + r) * LANES;
+            for (int l = 0; l < LANES; ++l) {
+                const float sq = values[base + l] * values[base + l];
+                acc[0][r][l] = acc[0][r][l] + sq;
+            }
+        }
+        ++index;
+    }
+    for (int level = 1; level < LEVELS; ++level)
+        for (int r = 0; r < INTERLEAVE; ++r)
+            for (int l = 0; l < LANES; ++l) acc[0][r][l] = acc[0][r][l] + acc[level][r][l];
+    for (size_t vec = cascade_size * INTERLEAVE; vec < vector_count; ++vec)
+        for (int l = 0; l < LANES; ++l) {
+            const float v = values[vec * LANES + l];
+            const float sq = v * v;
+            acc[0][0][l] = acc[0][0][l] + sq;
+        }
+    for (int r = 1; r < INTERLEAVE; ++r)
+        for (int l = 0; l < LANES; ++l) acc[0][0][l] = acc[0][0][l] + acc[0][r][l];
+    float result = 0.0f;
+    for (size_t i = vector_count * LANES; i < n; ++i) {
+        const float sq = values[i] * values[i];
+        result = result + sq;
+    }
+    for (int l = 0; l < LANES; ++l) result = result + acc[0][0][l];
+    return result;
+}
+
+/* src/hyper_connection.rs:285-303 */
+void fwo_grouped_rms(const uint16_t* input, const uint16_t* weight, size_t hidden, size_t groups, float eps,
+                     uint16_t* out) {
+    float* f = (float*)malloc(hidden * sizeof(float));
+    for (size_t g = 0; g < groups; ++g) {
+        const uint16_t* in = input + g * hidden;
+        for (size_t i = 0; i < hidden; ++i) f[i] = fwo_from_bf16(in[i]);
+        const float mean = fwo_inner_square_sum(f, hidden) / (float)hidden;
+        const float inverse = 1.0f / sqrtf(mean + eps);
+        for (size_t i = 0; i < hidden; ++i) {
+            const float scaled = f[i] * inverse;
+            const float gain = 1.0f + fwo_from_bf16(weight[g * hidden + i]);
+            out[g * hidden + i] = fwo_to_bf16(scaled * gain);
+        }
+    }
+    free(f);
+}
+
+/* src/hyper_connection.rs:305-307 */
+float fwo_four_stream_mean(const float values[4]) {
+    float sum = 0.0f;
+    for (int i = 0; i < 4; ++i) sum = sum + values[i];
+    return sum / 4.0f;
+}
+
+/* src/hyper_connection.rs:309-317 -- silu rounded to bf16. */
+static uint16_t silu_bf16(uint16_t v16) {
+    const float v = fwo_from_bf16(v16);
+    return fwo_to_bf16(v / (1.0f + expf(-v)));
+}
+
+/* src/hyper_connection.rs:412-490 */
+void fwo_hc_pre(const uint16_t* input, const fwo_hc_layer* layer, size_t hidden, size_t lowrank,
+                uint16_t* mixed, uint16_t* injection_weights, uint16_t* normed_out) {
+    const size_t HH = 4 * hidden;
+    uint16_t* normed = (uint16_t*)malloc(HH * 2);
+    uint16_t* down = (uint16_t*)malloc(lowrank * 2);
+    uint16_t* up = (uint16_t*)malloc(HH * 2);
+    fwo_grouped_rms(input, layer->norm, hidden, 4, 1.0e-6f, normed);
+    fwo_linear_bf16(layer->mix_down, normed, lowrank, HH, down);
+    for (size_t i = 0; i < lowrank; ++i) down[i] = silu_bf16(fwo_to_bf16(fwo_from_bf16(down[i]) / 4.0f));
+    fwo_linear_bf16(layer->mix_up, down, HH, lowrank, up);
+    for (size_t c = 0; c < hidden; ++c) {
+        float p[4];
+        for (int g = 0; g < 4; ++g) {
+            const size_t i = g * hidden + c;
+            p[g] = fwo_from_bf16(fwo_to_bf16(fwo_from_bf16(fwo_sigmoid_bf16(up[i])) * fwo_from_bf16(normed[i])));
+        }
+        mixed[c] = fwo_to_bf16(fwo_four_stream_mean(p));
+    }
+    uint16_t inj[4];
+    fwo_linear_bf16(layer->inject, normed, 4, HH, inj);
+    for (int g = 0; g < 4; ++g) {
+        const uint16_t scaled = fwo_to_bf16(fwo_from_bf16(inj[g]) / 4.0f);
+        injection_weights[g] = fwo_to_bf16(2.0f * fwo_from_bf16(fwo_sigmoid_bf16(scaled)));
+    }
+    if (normed_out) memcpy(normed_out, normed, HH * 2);
+    free(normed);
+    free(down);
+    free(up);
+}
+
+/* src/decoder_layer.rs:587-607 */
+void fwo_hc_post(const uint16_t* post, const uint16_t* moe, const uint16_t* injection_weights, size_t hidden,
+                 uint16_t* out) {
+    for (int g = 0; g < 4; ++g)
+        for (size_t c = 0; c < hidden; ++c) {
+            const uint16_t prod = fwo_to_bf16(fwo_from_bf16(moe[c]) * fwo_from_bf16(injection_weights[g]));
+            out[g * hidden + c] = fwo_add_bf16(post[g * hidden + c], prod);
+        }
+}

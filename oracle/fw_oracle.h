@@ -116,6 +116,33 @@ typedef struct {
 } fwo_input_spec;
 int fwo_make_hidden(size_t size, const fwo_input_spec* spec, uint16_t* out);
 
+/* ---- hyper-connection caller of the block (src/hyper_connection.rs,
+ *      src/decoder_layer.rs:451-458, 587-607) ---- */
+/* PyTorch's contiguous f32 inner square-sum cascade
+ * (src/hyper_connection.rs:211-283). */
+float fwo_inner_square_sum(const float* values, size_t n);
+/* grouped_rms (src/hyper_connection.rs:285-303): per group of `hidden`,
+ * bf16(v * (1/sqrt(sum/hidden + eps)) * (1 + w)). */
+void fwo_grouped_rms(const uint16_t* input, const uint16_t* weight, size_t hidden, size_t groups, float eps,
+                     uint16_t* out);
+/* four_stream_mean (src/hyper_connection.rs:305-307): sequential from 0.0. */
+float fwo_four_stream_mean(const float values[4]);
+/* run_hyper_connection (src/hyper_connection.rs:412-490) for one token:
+ * input [4H] -> mixed [H] (the block input) and injection weights [4];
+ * normed [4H] optional (NULL to skip). */
+typedef struct {
+    const uint16_t* norm;      /* [4H] hc_norm */
+    const uint16_t* mix_down;  /* [LR][4H] input_mix_weight_down */
+    const uint16_t* mix_up;    /* [4H][LR] input_mix_weight_up */
+    const uint16_t* inject;    /* [4][4H] block_inject_weight */
+} fwo_hc_layer;
+void fwo_hc_pre(const uint16_t* input, const fwo_hc_layer* layer, size_t hidden, size_t lowrank,
+                uint16_t* mixed, uint16_t* injection_weights, uint16_t* normed);
+/* The injection after the block (src/decoder_layer.rs:587-607):
+ * out[g*H + c] = add_bf16(post[g*H + c], bf16(moe[c] * w[g])). */
+void fwo_hc_post(const uint16_t* post, const uint16_t* moe, const uint16_t* injection_weights, size_t hidden,
+                 uint16_t* out);
+
 #ifdef __cplusplus
 }
 #endif
