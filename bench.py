@@ -509,9 +509,10 @@ def measure_prefill(args, rank, world, local_rank, peaks, stream, max_over_ranks
         "experts_frac_hbm": wbytes / ex_s / 1e9 / hbm_peak,
         "peak_source": "measured bf16_tflops / hbm_gbs" if peaks else "fallback",
         "hottest_expert_tokens": int(counts.max()), "distinct_experts": unique,
-        "gpu_launches_per_step": 7,
-        "kernels": "router (exact, CUDA cores), route, pair offsets, pair scatter, gate/up GEMM "
-                   "(tcgen05, SwiGLU epilogue), down GEMM (tcgen05, weight epilogue), combine",
+        "gpu_launches_per_step": 8,
+        "kernels": "router logits (tcgen05), exact repair of the selectable logits (CUDA cores), route, "
+                   "pair offsets, pair scatter, gate/up GEMM (tcgen05, SwiGLU epilogue), down GEMM "
+                   "(tcgen05, weight epilogue), combine",
     }
 
 

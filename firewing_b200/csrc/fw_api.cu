@@ -258,6 +258,23 @@ int check_handle(const fw_moe* h, int32_t layer) {
 // skewed router's hot low-id experts over the GPUs.
 int held_experts(const fw_moe* h) { return h->cfg.experts / h->ep_world; }
 
+// The prefill router's per-layer tables (row-norm bounds, partial-major
+// copy), stream-ordered after the router weights and the shared gate
+// vector; shapes without a prefill path need none.
+int router_tables(fw_moe* h, OwnedLayer& L) {
+  if (!fw::prefill_supported(h->shape)) return FW_OK;
+  const size_t E = h->cfg.experts, H = h->cfg.hidden;
+  float* norms = nullptr;
+  uint16_t* pm = nullptr;
+  FW_TRY(alloc(h, &norms, E, L.owned));
+  FW_TRY(alloc(h, &pm, (E + 1) * H, L.owned));
+  FW_CUDA(fw::launch_router_tables(L.w.router, L.w.sh_gate_w, static_cast<int>(E), static_cast<int>(H), norms, pm,
+                                   h->stream));
+  L.w.router_norm = norms;
+  L.w.router_pm = pm;
+  return FW_OK;
+}
+
 int free_layer(OwnedLayer& L) {
   for (void* p : L.owned) cudaFree(p);
   L.owned.clear();
@@ -319,7 +336,7 @@ int ep_prefill_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], cs) : cudaSuccess; };
   auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
   if ((e = mark(0)) != cudaSuccess) return cuda_failed("event");
-  if ((e = fw::launch_prefill_front(s, L.w, h->luts, h->sc, x, T_l, idx, score, false, cs)) != cudaSuccess)
+  if ((e = fw::launch_prefill_front(s, L.w, L.maps, h->luts, h->sc, x, T_l, idx, score, false, cs)) != cudaSuccess)
     return cuda_failed("router / route launch");
   if ((e = mark(1)) != cudaSuccess) return cuda_failed("event");
   const char* m = fw::ep_dispatch(h->ep, x, h->ep_x_all, static_cast<size_t>(T_l) * s.H, idx, h->ep_idx_all,
@@ -486,6 +503,9 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &s.pair_tk, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.xg, static_cast<size_t>(M) * K * H, o)) != FW_OK) break;
     s.pair_cap = static_cast<long long>(M) * K;
+    if (fw::prefill_supported(h->shape) &&
+        (rc = alloc(h, &s.router_approx, static_cast<size_t>(M) * E, o)) != FW_OK)
+      break;
     if ((rc = alloc(h, &h->x_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->y_dev, static_cast<size_t>(M) * H, o)) != FW_OK) break;
     if ((rc = alloc(h, &h->idx_dev, static_cast<size_t>(M) * K, o)) != FW_OK) break;
@@ -565,6 +585,10 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
       return fail(FW_ECUDA, "weight copy", cudaGetErrorString(e));
     }
     *it.dst = d;
+  }
+  if (int rc = router_tables(h, L); rc != FW_OK) {
+    free_layer(L);
+    return rc;
   }
   const int ecount = held_experts(h), world = h->ep_world, rank = h->ep_rank;
   // Expert banks (this handle's experts) and the shared expert go to the
@@ -677,6 +701,10 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
       return fail(FW_ECUDA, "synth launch", cudaGetErrorString(e));
     }
     *it.dst = d;
+  }
+  if (int rc = router_tables(h, L); rc != FW_OK) {
+    free_layer(L);
+    return rc;
   }
   const int ecount = held_experts(h);
   // Expert banks (this handle's experts) and the shared expert: generated

@@ -41,6 +41,13 @@ struct LayerWeights {
   const uint16_t* sh_down = nullptr;
   const uint16_t* sh_gate_w = nullptr;
   const float* bias = nullptr;
+  // [E] upper bounds of the router rows' 2-norms (prefill router, see
+  // launch_router_norms); null without a prefill path.
+  const float* router_norm = nullptr;
+  // [E+1][H] router rows and the shared gate vector in partial-major order
+  // (element (row, j, i) = row[j + 32 i]) for the prefill router's exact
+  // repair; null without a prefill path.
+  const uint16_t* router_pm = nullptr;
   // Experts held: e with e % ep_world == ep_rank, bank index e / ep_world
   // (expert parallelism interleaves the experts over the GPUs; one GPU
   // holds all of them at their own index).
@@ -107,6 +114,7 @@ struct Scratch {
   int32_t* pair_tk = nullptr;    // [T*K] grouped pairs: t*K + top-k position
   uint16_t* xg = nullptr;        // input rows in grouped pair order, K-blocked: [H/64][pair_cap][64]
   long long pair_cap = 0;        // pair rows of xg / act / pair_tk (max_T * K; more under expert parallelism)
+  float* router_approx = nullptr;  // [T][E] tensor-core router logits (prefill), before the exact repair
 };
 
 // Schedule layout inside Scratch::sched (int32 words), written by the route
@@ -192,6 +200,7 @@ struct PrefillWeightMaps {
   CUtensorMap down;        // routed down bank
   CUtensorMap sh_gate_up;  // shared expert gate/up
   CUtensorMap sh_down;     // shared expert down
+  CUtensorMap router;      // router [E][H] (reference layout), 128-row x 64-column boxes
 };
 // Tensor maps of the fixed scratch (activations between the two GEMMs).
 struct PrefillScratchMaps {
@@ -221,9 +230,14 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
 //          shared expert over sh_T tokens;
 //   gemms: gate/up and down GEMMs; weighted rows to out_rows at row t*K+k,
 //          or at send_pos[t*K+k] when send_pos is given.
-cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
-                                 const uint16_t* x, int T, int32_t* topk_idx, uint16_t* topk_score, bool count_pairs,
-                                 cudaStream_t st);
+cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
+                                 const Luts& luts, const Scratch& sc, const uint16_t* x, int T, int32_t* topk_idx,
+                                 uint16_t* topk_score, bool count_pairs, cudaStream_t st);
+// Per-layer tables of the prefill router (H a multiple of 256): upper
+// bounds of the router rows' 2-norms [E] and the partial-major copy of the
+// router rows plus the shared gate vector [E+1][H].
+cudaError_t launch_router_tables(const uint16_t* w, const uint16_t* extra_row, int E, int H, float* norms,
+                                 uint16_t* pm, cudaStream_t st);
 cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_t* idx, int n_pairs,
                                  const uint16_t* x_src, int ep_rank, int ep_world, int ecount, int sh_T,
                                  bool count_here, cudaStream_t st);

@@ -8,7 +8,8 @@
 // thousand for a hot expert) the block is a grouped GEMM and belongs on the
 // tensor cores:
 //
-//   router (exact, shared with decode) -> route (+ per-expert pair counts)
+//   router (tensor-core logits + exact repair of those that can be
+//           selected, k_router_tc / k_router_fix) -> route (+ pair counts)
 //   -> k_pf_offsets (one CTA: pair offsets, work-unit prefixes)
 //   -> k_pf_scatter (pairs grouped by expert; token rows copied into the
 //                    grouped input xg [pairs][H])
@@ -40,8 +41,9 @@
 // Numerics: every product is exact and accumulated in f32 by the tensor
 // core in its own order, so outputs differ from the reference's 32-partial
 // schedule by f32 rounding before each bf16 rounding point (within the
-// block tolerance, max-abs 2e-2 / rel-L2 1e-3).  The router stays exact, so
-// expert selection matches the reference bit for bit.
+// block tolerance, max-abs 2e-2 / rel-L2 1e-3).  Every logit that can be
+// selected is recomputed exactly, so expert selection matches the
+// reference's bit for bit.
 //
 // Every wait is bounded (2 s of globaltimer); on expiry the CTA records
 // kErrTimeout, stops issuing, lets its copies and MMAs drain (bounded), frees
@@ -500,210 +502,372 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kAccCols) : "memory");
 }
 
-// ---- exact router for prefill widths -------------------------------------------
+// ---- router for prefill widths ---------------------------------------------------
 //
-// logits[t][e] = bf16(dot(router[e], x[t])) with the reference's dot schedule
-// (src/expert.rs:514-552): 32 f32 partials, partial j summing columns
-// j, j+32, ... in order, then the tree +16, +8, +4, (0+1)+(2+3).  Row E is
-// the shared-expert gate vector (its logit goes to sh_logit).
-//
-// Persistent CTAs walk tiles of 32 tokens x 16 rows.  Warp 8 is the
-// producer: it streams column chunks of every tile (bf16, rows padded by 16
-// bytes) into a 2-stage ring with bulk copies, on across tile boundaries.
-// Warps 0-7 (16 half-warps) consume: half-warp h owns tokens 4*(h&7)..+3
-// and rows 8*(h>>3)..+7, its lane l the partials 2l and 2l+1 (one 32-bit
-// load per operand row per 32-column block, mixed-precision bf16 FMAs into
-// f32).  Full/empty mbarriers replace block-wide barriers, so each warp runs
-// at its own pace.
-constexpr int kRtTok = 32, kRtRows = 16, kRtMaxChunk = 512, kRtPad = 8, kRtComputeWarps = 8;
+// Expert selection has to be the reference's, and only the logits near a
+// token's top-k boundary decide it.  So the router runs in two kernels:
+//   k_router_tc   every (token, expert) logit on the tensor cores, f32
+//                 accumulation ([T][E] `approx`), 128 router rows x 256
+//                 tokens per CTA;
+//   k_router_fix  one warp per token: an interval holding the reference's
+//                 biased bf16 logit of each expert, from approx -+ delta with
+//                 delta = 2^-10 * |w_e|_2 * |x_t|_2.  Experts whose upper end
+//                 reaches the k-th largest lower end are the only ones that
+//                 can be selected; their logits are recomputed with the
+//                 reference's dot schedule (src/expert.rs:514-552).  The other
+//                 logits keep the rounded approximation, within one bf16 step
+//                 of the reference's, and enter only the softmax denominator.
+//                 The shared gate logit is always recomputed.
+// The bound: the reference's dot (32 partials of H/32 products, then a
+// 5-level tree) is within (H/32 + 5) * 2^-24 * S of the exact dot, where
+// S = sum |w_i x_i| <= |w|_2 |x|_2 (Cauchy-Schwarz); the tensor core adds
+// exact bf16 products into an f32 accumulator in H/16 steps, within
+// (H/16) * 17 * 2^-24 * S even if each step truncated all 17 aligned terms
+// to 24 bits.  At H = 4096 the two add up to 2^-11.8 * S, so 2^-10 leaves a
+// factor of three.  Rounding to bf16 and adding the bias are monotone, so
+// the interval's ends give the lowest and highest possible bf16 logit.  An
+// expert whose highest possible logit is below the k-th largest lowest one
+// is beaten strictly by k others: the top-k (with its tie rule, decided by
+// k_route on the repaired logits) only ever compares exact logits.
+constexpr int kRcN = 256;                     // tokens per CTA (MMA N)
+constexpr int kRcStages = 4;
+constexpr int kRcBBytes = kRcN * kBK * 2;     // 32 KB token tile
+constexpr int kFixWarps = 4;                  // tokens per k_router_fix CTA
+constexpr float kDotBound = 0x1p-10f;         // delta / (|w| |x|)
+constexpr float kNormSlack = 1.00390625f;     // 1 + 2^-8: f32 sum of <= 2^15 squares, rounded up
+constexpr float kNormFloor = 0x1p-60f;        // norms below this are raised to it
+constexpr float kFiniteMax = 0x1p120f;        // larger |approx| or delta: no interval, recompute
 
-struct PfRouterArgs {
-  const uint16_t* w;          // [E][H]
-  const uint16_t* extra_row;  // [H]
-  const float* bias;          // [E] or null
-  const uint16_t* x;          // [T][H]
-  uint16_t* logits;           // [T][E]
-  uint16_t* extra_out;        // [T]
-  int E, H, T;
-  int kc;                     // columns per chunk: 512, or 256 when H is not a multiple of 512
+struct __align__(8) RcTail {
+  uint64_t full[kRcStages];
+  uint64_t empty[kRcStages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+
+size_t router_tc_smem() { return 1024 + static_cast<size_t>(kRcStages) * (kABytes + kRcBBytes) + sizeof(RcTail); }
+
+struct RouterTcArgs {
+  int E, T, H;
+  int bn;          // token rows per tile: min(256, T rounded up to 16)
+  float* approx;   // [T][E]
   int* err;
 };
 
-// a0 += lo(w) * lo(x), a1 += hi(w) * hi(x): mixed-precision FMAs (bf16
-// operands, f32 accumulator, round to nearest even).  A bf16 x bf16 product
-// is exact in f32, so each rounds like the reference's multiply then add.
-__device__ __forceinline__ void fma2_bf16(uint32_t w, uint32_t x, float& a0, float& a1) {
-  asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
-      "mov.b32 {w0, w1}, %2;\n\t"
-      "mov.b32 {x0, x1}, %3;\n\t"
-      "fma.rn.f32.bf16 %0, w0, x0, %0;\n\t"
-      "fma.rn.f32.bf16 %1, w1, x1, %1;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "r"(w), "r"(x));
-}
-
-size_t router_pf_smem() { return 2 * static_cast<size_t>(kRtTok + kRtRows) * (kRtMaxChunk + kRtPad) * 2 + 64; }
-
-__global__ void __launch_bounds__(32 * (kRtComputeWarps + 1), 2) k_router_pf(PfRouterArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  constexpr int kRowsAll = kRtTok + kRtRows;
-  const int kRtChunk = a.kc, kRtPitch = a.kc + kRtPad;
-  uint16_t* stage[2];
-  stage[0] = reinterpret_cast<uint16_t*>(smem);
-  stage[1] = stage[0] + kRowsAll * kRtPitch;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage[1] + kRowsAll * kRtPitch);  // [2]
-  uint64_t* empty = full + 2;                                                     // [2]
-  const int row_tiles = (a.E + 1 + kRtRows - 1) / kRtRows;
-  const int tiles = row_tiles * ((a.T + kRtTok - 1) / kRtTok);
-  const int nchunks = a.H / kRtChunk;
-  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int nstream = my_tiles * nchunks;
-  const uint32_t cbytes = kRtChunk * 2;
+// Warp 0 lane 0 loads (TMA, 128-byte swizzle: router rows m0.. and token
+// rows n0.., 64 columns per stage), warp 1 lane 0 issues the MMAs
+// (M = 128 router rows, N = bn tokens, K = 16 per instruction) into one
+// TMEM accumulator; then warp w stores TMEM lanes 32w.. (router rows) as
+// f32 logits, 32 tokens per tcgen05.ld, each a coalesced 128-byte row run.
+__global__ void __launch_bounds__(128, 1)
+    k_router_tc(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                RouterTcArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  unsigned char* ring_a = smem;
+  unsigned char* ring_b = smem + kRcStages * kABytes;
+  RcTail* tail = reinterpret_cast<RcTail*>(ring_b + kRcStages * kRcBBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  auto tile_geom = [&](int i, int& row0, int& nrows, int& t0, int& nt) {
-    const int tile = blockIdx.x + i * gridDim.x;
-    const int tr = tile % row_tiles, tt = tile / row_tiles;
-    row0 = tr * kRtRows;
-    nrows = min(kRtRows, a.E + 1 - row0);
-    t0 = tt * kRtTok;
-    nt = min(kRtTok, a.T - t0);
-  };
+  const int mtiles = (a.E + kBM - 1) / kBM;
+  const int m0 = (blockIdx.x % mtiles) * kBM, n0 = (blockIdx.x / mtiles) * a.bn;
+  const int nkb = a.H / kBK;
+  const uint32_t stage_bytes = kABytes + a.bn * kBK * 2;
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&full[b], 1);
-      mbar_init(&empty[b], kRtComputeWarps);
+    for (int i = 0; i < kRcStages; ++i) {
+      mbar_init(&tail->full[i], 1);
+      mbar_init(&tail->empty[i], 1);
     }
+    mbar_init(&tail->acc_full, 1);
     fence_mbar_init();
   }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tail->tmem_base)),
+                 "r"(kRcN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
   __syncthreads();
-
-  if (warp == kRtComputeWarps) {
-    // ---------------- producer ----------------
-    const uint64_t policy = l2_evict_first_policy();
-    bool waited = false;
-    int g = 0;
-    for (; g < nstream; ++g) {
-      const int b = g & 1;
-      int row0, nrows, t0, nt;
-      tile_geom(g / nchunks, row0, nrows, t0, nt);
-      const int c = g % nchunks;
-      bool ok = true;
-      if (lane == 0) {
-        ok = mbar_wait_bounded(&empty[b], ((g >> 1) & 1) ^ 1u, 2000000000ull);
-        if (ok) mbar_arrive_expect_tx(&full[b], cbytes * (nrows + nt));
-        else set_error(a.err, kErrTimeout);
+  tc_fence_after();
+  const uint32_t tmem = tail->tmem_base;
+  // The token rows may be the previous kernel's output.
+  pdl_wait();
+  pdl_launch_dependents();
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    int issued = 0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int st = kb % kRcStages;
+      if (!mbar_wait_bounded(&tail->empty[st], ((kb / kRcStages) & 1) ^ 1u, kWaitNs)) {
+        ok = false;
+        break;
       }
-      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
-      if (lane < nrows) {
-        const int row = row0 + lane;
-        const uint16_t* src = (row < a.E ? a.w + static_cast<size_t>(row) * a.H : a.extra_row) + c * kRtChunk;
-        bulk_g2s(stage[b] + (kRtTok + lane) * kRtPitch, src, cbytes, &full[b], policy);
-      }
-      // Weights do not depend on the previous kernel; token rows do.
-      if (!waited) {
-        pdl_wait();
-        pdl_launch_dependents();
-        waited = true;
-      }
-      if (lane < nt)
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                smem_u32(stage[b] + lane * kRtPitch)),
-            "l"(a.x + static_cast<size_t>(t0 + lane) * a.H + c * kRtChunk), "r"(cbytes), "r"(smem_u32(&full[b]))
-            : "memory");
+      mbar_arrive_expect_tx(&tail->full[st], stage_bytes);
+      tma_load_2d(ring_a + st * kABytes, &map_w, kb * kBK, m0, &tail->full[st]);
+      tma_load_2d(ring_b + st * kRcBBytes, &map_x, kb * kBK, n0, &tail->full[st]);
+      ++issued;
     }
-    if (!waited) {
-      pdl_wait();
-      pdl_launch_dependents();
+    // Copies in flight land before the CTA can exit.
+    for (int j = issued > kRcStages ? issued - kRcStages : 0; j < issued; ++j)
+      if (!mbar_wait_bounded(&tail->full[j % kRcStages], (j / kRcStages) & 1, kWaitNs)) ok = false;
+  } else if (warp == 1 && lane == 0) {
+    const uint32_t idesc = idesc_bf16(kBM, a.bn);
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int st = kb % kRcStages;
+      if (!mbar_wait_bounded(&tail->full[st], (kb / kRcStages) & 1, kWaitNs)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = smem_u32(ring_a + st * kABytes), sb = smem_u32(ring_b + st * kRcBBytes);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k)
+        umma_bf16(tmem, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+      umma_commit(&tail->empty[st]);
     }
-    // Copies still in flight land before the CTA exits (bounded).
-    if (lane == 0)
-      for (int gg = g > 2 ? g - 2 : 0; gg < g; ++gg) mbar_wait_bounded(&full[gg & 1], (gg >> 1) & 1, 2000000000ull);
-    return;
+    // Arrives once every MMA issued above has completed (after a failure too).
+    umma_commit(&tail->acc_full);
   }
-
-  // ---------------- compute warps ----------------
-  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
-  const int tg = hw & 7, rg = hw >> 3;
-  int g = 0;  // chunk-stream position
-  for (int i = 0; i < my_tiles; ++i) {
-    int row0, nrows, t0, nt;
-    tile_geom(i, row0, nrows, t0, nt);
-    float acc[4][8][2];
+  if (!ok) set_error(a.err, kErrTimeout);
+  __syncwarp();
+  const bool got = mbar_wait_bounded(&tail->acc_full, 0, kWaitNs);
+  if (!__all_sync(0xffffffffu, got)) {
+    if (lane == 0) set_error(a.err, kErrTimeout);
+  } else {
+    tc_fence_after();
+    const int e = m0 + 32 * warp + lane;
+    for (int c0 = 0; c0 < a.bn && n0 + c0 < a.T; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + c0, v);
+      if (e < a.E) {
 #pragma unroll
-    for (int ti = 0; ti < 4; ++ti)
-#pragma unroll
-      for (int r = 0; r < 8; ++r) acc[ti][r][0] = acc[ti][r][1] = 0.0f;
-    for (int c = 0; c < nchunks; ++c, ++g) {
-      const int b = g & 1;
-      const bool ok = mbar_wait_bounded(&full[b], (g >> 1) & 1, 2000000000ull);
-      if (!__all_sync(0xffffffffu, ok)) {
-        if (lane == 0) set_error(a.err, kErrTimeout);
-        return;
-      }
-      const uint16_t* xs = stage[b] + (4 * tg) * kRtPitch + 2 * l;
-      const uint16_t* ws = stage[b] + (kRtTok + 8 * rg) * kRtPitch + 2 * l;
-#pragma unroll 2
-      for (int k = 0; k < kRtChunk; k += 32) {
-        uint32_t xv[4], wv[8];
-#pragma unroll
-        for (int ti = 0; ti < 4; ++ti) xv[ti] = *reinterpret_cast<const uint32_t*>(xs + ti * kRtPitch + k);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) wv[r] = *reinterpret_cast<const uint32_t*>(ws + r * kRtPitch + k);
-#pragma unroll
-        for (int ti = 0; ti < 4; ++ti)
-#pragma unroll
-          for (int r = 0; r < 8; ++r) fma2_bf16(wv[r], xv[ti], acc[ti][r][0], acc[ti][r][1]);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[b]);
-    }
-    // Reference tree over the half-warp: lane l holds partials 2l, 2l+1.
-    uint32_t out[4][4];  // per token: 8 bf16 logits packed
-#pragma unroll
-    for (int ti = 0; ti < 4; ++ti) {
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        float p0 = acc[ti][r][0], p1 = acc[ti][r][1];
-        p0 += __shfl_down_sync(0xffffffffu, p0, 8, 16);  // j += j + 16
-        p1 += __shfl_down_sync(0xffffffffu, p1, 8, 16);
-        p0 += __shfl_down_sync(0xffffffffu, p0, 4, 16);  // j += j + 8
-        p1 += __shfl_down_sync(0xffffffffu, p1, 4, 16);
-        p0 += __shfl_down_sync(0xffffffffu, p0, 2, 16);  // j += j + 4
-        p1 += __shfl_down_sync(0xffffffffu, p1, 2, 16);
-        const float s = p0 + p1;                         // lane 0: 0+1, lane 1: 2+3
-        const float dot = s + __shfl_down_sync(0xffffffffu, s, 1, 16);
-        const uint32_t v = f32_to_bf16(dot);
-        if (r & 1) out[ti][r >> 1] |= v << 16;
-        else out[ti][r >> 1] = v;
-      }
-    }
-    if (l == 0) {
-      const int rbase = row0 + 8 * rg;
-#pragma unroll
-      for (int ti = 0; ti < 4; ++ti) {
-        const int t = t0 + 4 * tg + ti;
-        if (4 * tg + ti >= nt) continue;
-        if (rbase + 8 <= a.E && a.bias == nullptr) {
-          *reinterpret_cast<uint4*>(a.logits + static_cast<size_t>(t) * a.E + rbase) =
-              make_uint4(out[ti][0], out[ti][1], out[ti][2], out[ti][3]);
-          continue;
-        }
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const int row = rbase + r;
-          uint16_t v = static_cast<uint16_t>((out[ti][r >> 1] >> (16 * (r & 1))) & 0xffffu);
-          if (row < a.E) {
-            // build-defined extension: f32 logit bias, re-rounded to bf16
-            if (a.bias != nullptr) v = f32_to_bf16(bf16_to_f32(v) + a.bias[row]);
-            a.logits[static_cast<size_t>(t) * a.E + row] = v;
-          } else if (row == a.E) {
-            a.extra_out[t] = v;
-          }
+        for (int j = 0; j < 32; ++j) {
+          const int t = n0 + c0 + j;
+          if (t < a.T) a.approx[static_cast<size_t>(t) * a.E + e] = __uint_as_float(v[j]);
         }
       }
     }
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kRcN) : "memory");
+}
+
+struct RouterFixArgs {
+  const uint16_t* wpm;        // [E+1][H] router rows and the shared gate vector, partial-major
+  const float* bias;          // [E] or null
+  const float* wnorm;         // [E] upper bounds of the router rows' 2-norms
+  const float* approx;        // [T][E]
+  const uint16_t* x;          // [T][H]
+  uint16_t* logits;           // [T][E]
+  uint16_t* extra_out;        // [T]
+  int E, H, T, K;
+};
+
+// Lane blocks of a staged row are padded to an odd number of 16-byte
+// chunks, so the 16-byte loads of eight consecutive lanes hit distinct banks.
+__host__ __device__ inline int fix_stride(int H) {
+  const int nch = H / 256;
+  return nch + 1 + (nch & 1);
+}
+size_t router_fix_smem(int H, int E) {
+  return static_cast<size_t>(kFixWarps) * (2 * 32 * 16 * static_cast<size_t>(fix_stride(H)) + 2 * E);
+}
+
+// bf16 logit with the build's optional f32 bias, re-rounded (as k_router).
+__device__ __forceinline__ uint16_t biased_logit(float v, const float* bias, int e) {
+  uint16_t b = f32_to_bf16(v);
+  if (bias != nullptr) b = f32_to_bf16(bf16_to_f32(b) + bias[e]);
+  return b;
+}
+
+// Upper bound of |v|_2 from an f32 sum of squares of at most 2^15 terms.
+__device__ __forceinline__ float norm_bound(float sum_sq) {
+  return fmaxf(__fsqrt_ru(__fmul_ru(sum_sq, kNormSlack)), kNormFloor);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// acc += lo(w) * lo(x), then acc += hi(w) * hi(x): mixed-precision FMAs
+// (bf16 operands, f32 accumulator); an exact bf16 product and one rounding
+// per add, as the reference's multiply then add.
+__device__ __forceinline__ float fma_seq2(uint32_t w, uint32_t x, float acc) {
+  asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+      "mov.b32 {w0, w1}, %1;\n\t"
+      "mov.b32 {x0, x1}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, w0, x0, %0;\n\t"
+      "fma.rn.f32.bf16 %0, w1, x1, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(w), "r"(x));
+  return acc;
+}
+
+// One warp per token (see the section comment).  Lane j holds the token's
+// columns j, j+32, ... (PX bf16 pairs at most: H <= 64 * PX) in registers,
+// and the interval keys of experts j, j+32, ... (NS slots: E <= 32 * NS).
+// Candidate rows come from the partial-major copy (lane j's columns
+// contiguous), staged with cp.async, the next row in flight while the
+// current dot runs.
+template <int PX, int NS>
+__global__ void __launch_bounds__(32 * kFixWarps) k_router_fix(RouterFixArgs a) {
+  extern __shared__ __align__(16) unsigned char fix_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = a.H >> 8;  // 16-byte chunks (8 columns) per lane
+  const int S = fix_stride(a.H);
+  uint4* wbase = reinterpret_cast<uint4*>(fix_smem) + static_cast<size_t>(warp) * 2 * 32 * S;
+  uint16_t* cand = reinterpret_cast<uint16_t*>(reinterpret_cast<uint4*>(fix_smem) + kFixWarps * 2 * 32 * S) +
+                   static_cast<size_t>(warp) * a.E;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x * kFixWarps + warp;
+  if (t >= a.T) return;
+
+  // Token columns j + 32i, paired (i, i+1), and an upper bound of |x|_2.
+  const uint16_t* xr = a.x + static_cast<size_t>(t) * a.H + lane;
+  const int pairs = a.H >> 6;
+  uint32_t xv[PX];
+  float ss = 0.0f;
+#pragma unroll
+  for (int p = 0; p < PX; ++p) {
+    xv[p] = 0u;
+    if (p < pairs) {
+      const uint32_t lo = xr[64 * p], hi = xr[64 * p + 32];
+      xv[p] = lo | (hi << 16);
+      const float fl = bf16_to_f32(lo), fh = bf16_to_f32(hi);
+      ss = __fmaf_rn(fl, fl, ss);
+      ss = __fmaf_rn(fh, fh, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float xn = norm_bound(ss);
+
+  // Interval keys (the total order of bf16 the route kernel ranks by) of
+  // every expert; the rounded approximation is written for each bounded one.
+  const float* ar = a.approx + static_cast<size_t>(t) * a.E;
+  uint16_t* lr = a.logits + static_cast<size_t>(t) * a.E;
+  const int ne = a.E >> 5;
+  uint32_t lohi[NS];  // (lowest key << 16) | highest key
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    lohi[i] = 0u;
+    if (i < ne) {
+      const int e = lane + 32 * i;
+      const float av = ar[e];
+      const float d = __fmul_ru(__fmul_ru(a.wnorm[e], xn), kDotBound);
+      uint32_t lo = 0u, hi = 0xffffu;  // unbounded: always a candidate
+      if (fabsf(av) <= kFiniteMax && d <= kFiniteMax) {
+        lo = total_key(biased_logit(__fsub_rd(av, d), a.bias, e));
+        hi = total_key(biased_logit(__fadd_ru(av, d), a.bias, e));
+        lr[e] = biased_logit(av, a.bias, e);
+      }
+      lohi[i] = (lo << 16) | hi;
+    }
+  }
+  // tau = the K-th largest lowest key (bitwise search over the 16-bit keys).
+  uint32_t tau = 0u;
+  for (int b = 15; b >= 0; --b) {
+    const uint32_t c = (tau | (1u << b)) << 16;
+    unsigned n = 0;
+#pragma unroll
+    for (int i = 0; i < NS; ++i) n += (i < ne && lohi[i] >= c) ? 1u : 0u;
+    if (static_cast<int>(__reduce_add_sync(0xffffffffu, n)) >= a.K) tau |= 1u << b;
+  }
+  int nc = 0;
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    const bool c = i < ne && (lohi[i] & 0xffffu) >= tau;
+    const uint32_t m = __ballot_sync(0xffffffffu, c);
+    if (c) cand[nc + __popc(m & ((1u << lane) - 1u))] = static_cast<uint16_t>(lane + 32 * i);
+    nc += __popc(m);
+  }
+  __syncwarp();  // candidate list and the approximations above before the exact writes
+
+  // Rows 0..nc-1: the candidates; row nc: the shared gate vector (row E).
+  // Global chunk g of a row (lane block g / nch, chunk g % nch) goes to
+  // padded position (g / nch) * S + g % nch.
+  int blk0 = lane / nch, rem0 = lane - blk0 * nch;
+  const int step_blk = 32 / nch, step_rem = 32 - step_blk * nch;
+  auto fetch = [&](int j, uint4* buf) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.wpm + static_cast<size_t>(j < nc ? cand[j] : a.E) * a.H);
+    int blk = blk0, rem = rem0;
+    for (int g = lane; g < 32 * nch; g += 32) {
+      cp_async16(buf + blk * S + rem, src + g);
+      blk += step_blk;
+      rem += step_rem;
+      if (rem >= nch) {
+        rem -= nch;
+        ++blk;
+      }
+    }
+    cp_async_commit();
+  };
+  fetch(0, wbase);
+  for (int j = 0; j <= nc; ++j) {
+    uint4* cur = wbase + (j & 1) * 32 * S;
+    if (j < nc) fetch(j + 1, wbase + ((j + 1) & 1) * 32 * S);
+    else cp_async_commit();  // an empty group keeps "all but the newest" meaning row j
+    cp_async_wait_prev();
+    __syncwarp();  // every lane's part of row j has landed
+    // The reference dot: lane j sums its columns in order, then the tree
+    // +16, +8, +4, (0+1)+(2+3) (src/expert.rs:514-552).
+    const uint4* wl = cur + lane * S;
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < PX / 4; ++q) {
+      if (q < nch) {
+        const uint4 w4 = wl[q];
+        acc = fma_seq2(w4.x, xv[4 * q], acc);
+        acc = fma_seq2(w4.y, xv[4 * q + 1], acc);
+        acc = fma_seq2(w4.z, xv[4 * q + 2], acc);
+        acc = fma_seq2(w4.w, xv[4 * q + 3], acc);
+      }
+    }
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 16));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    const float qs = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));  // lanes 0, 2: (0+1), (2+3)
+    const float dot = __fadd_rn(qs, __shfl_down_sync(0xffffffffu, qs, 2));
+    if (lane == 0) {
+      if (j < nc) lr[cand[j]] = biased_logit(dot, a.bias, cand[j]);
+      else a.extra_out[t] = f32_to_bf16(dot);
+    }
+    __syncwarp();  // row j read by every lane before its buffer is refilled
+  }
+}
+
+// Per layer, for the prefill router: an upper bound of each router row's
+// 2-norm (one warp per row), and the partial-major copy of the router rows
+// plus the shared gate vector: element (row, j, i) = row[j + 32 i].
+__global__ void k_router_tables(const uint16_t* w, const uint16_t* extra_row, int E, int H, float* norms,
+                                uint16_t* pm) {
+  const long long n = static_cast<long long>(E + 1) * H;
+  const int per = H / 32;
+  for (long long o = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; o < n;
+       o += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(o / H), r = static_cast<int>(o - static_cast<long long>(row) * H);
+    const int j = r / per, i = r - j * per;
+    pm[o] = (row < E ? w + static_cast<size_t>(row) * H : extra_row)[j + 32 * i];
+  }
+  const int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (e >= E) return;
+  const uint16_t* rw = w + static_cast<size_t>(e) * H;
+  float ss = 0.0f;
+  for (int c = lane; c < H; c += 32) {
+    const float v = bf16_to_f32(rw[c]);
+    ss = __fmaf_rn(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) norms[e] = norm_bound(ss);
 }
 
 // ---- grouping kernels -----------------------------------------------------------
@@ -977,14 +1141,15 @@ int sm_count() {
 }  // namespace
 
 bool prefill_supported(const Shape& s) {
-  return s.H % (kRtMaxChunk / 2) == 0 && s.H % kBM == 0 && (2 * s.I) % kBM == 0 && (2 * s.Is) % kBM == 0 && s.E <= 1024;
+  return s.H % 256 == 0 && (2 * s.I) % kBM == 0 && (2 * s.Is) % kBM == 0 && s.E <= 1024;
 }
 
 bool make_prefill_weight_maps(const Shape& s, const LayerWeights& w, PrefillWeightMaps* out) {
   if (!w.tiled || !prefill_supported(s)) return false;
   const long long E = w.expert_count;
   return weight_map(&out->gate_up, w.gate_up, s.H, E * 2 * s.I) && weight_map(&out->down, w.down, s.I, E * s.H) &&
-         weight_map(&out->sh_gate_up, w.sh_gate, s.H, 2LL * s.Is) && weight_map(&out->sh_down, w.sh_down, s.Is, s.H);
+         weight_map(&out->sh_gate_up, w.sh_gate, s.H, 2LL * s.Is) && weight_map(&out->sh_down, w.sh_down, s.Is, s.H) &&
+         rows_map(&out->router, w.router, s.H, s.E, kBM);
 }
 
 bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratchMaps* out) {
@@ -995,18 +1160,49 @@ bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratch
          rows_map(&out->act_sh, sc.act_sh, 64, (s.Is / 64) * M, 16);
 }
 
-cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
-                                 const uint16_t* x, int T, int32_t* topk_idx, uint16_t* topk_score, bool count_pairs,
-                                 cudaStream_t st) {
+cudaError_t launch_router_tables(const uint16_t* w, const uint16_t* extra_row, int E, int H, float* norms,
+                                 uint16_t* pm, cudaStream_t st) {
+  if (H % 256 != 0) return cudaErrorInvalidValue;
+  const long long n = static_cast<long long>(E + 1) * H;
+  const int blocks = static_cast<int>(std::max<long long>((E + 7) / 8, std::min<long long>((n + 255) / 256, 4096)));
+  k_router_tables<<<blocks, 256, 0, st>>>(w, extra_row, E, H, norms, pm);
+  return cudaGetLastError();
+}
+
+template <int PX>
+cudaError_t launch_router_fix_px(const RouterFixArgs& fa, cudaStream_t st) {
+  const dim3 grid((fa.T + kFixWarps - 1) / kFixWarps), block(32 * kFixWarps);
+  const size_t smem = router_fix_smem(fa.H, fa.E);
+  return fa.E <= 512 ? launch_pdl_ex(k_router_fix<PX, 16>, grid, block, smem, st, fa)
+                     : launch_pdl_ex(k_router_fix<PX, 32>, grid, block, smem, st, fa);
+}
+
+cudaError_t launch_router_fix(const RouterFixArgs& fa, cudaStream_t st) {
+  const int pairs = fa.H / 64;
+  if (pairs <= 16) return launch_router_fix_px<16>(fa, st);
+  if (pairs <= 32) return launch_router_fix_px<32>(fa, st);
+  if (pairs <= 48) return launch_router_fix_px<48>(fa, st);
+  return launch_router_fix_px<64>(fa, st);
+}
+
+cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
+                                 const Luts& luts, const Scratch& sc, const uint16_t* x, int T, int32_t* topk_idx,
+                                 uint16_t* topk_score, bool count_pairs, cudaStream_t st) {
+  if (w.router_norm == nullptr || w.router_pm == nullptr || sc.router_approx == nullptr) return cudaErrorInvalidValue;
   cudaError_t e;
   if (count_pairs && (e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * s.E, st)) != cudaSuccess) return e;
-  PfRouterArgs ra{w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T,
-                  s.H % kRtMaxChunk == 0 ? kRtMaxChunk : kRtMaxChunk / 2, sc.err};
-  const int rtiles = (s.E + 1 + kRtRows - 1) / kRtRows * ((T + kRtTok - 1) / kRtTok);
-  const dim3 rgrid(rtiles < 2 * sm_count() ? rtiles : 2 * sm_count());
-  if ((e = launch_pdl_ex(k_router_pf, rgrid, dim3(32 * (kRtComputeWarps + 1)), router_pf_smem(), st, ra)) !=
-      cudaSuccess)
+  // Tensor-core logits, then the exact repair of the ones that can be selected.
+  const int bn = T < kRcN ? (T + 15) & ~15 : kRcN;
+  CUtensorMap x_rows;
+  if (!rows_map(&x_rows, x, s.H, T, bn)) return cudaErrorInvalidValue;
+  const RouterTcArgs ta{s.E, T, s.H, bn, sc.router_approx, sc.err};
+  const int mtiles = (s.E + kBM - 1) / kBM;
+  if ((e = launch_pdl_ex(k_router_tc, dim3(mtiles * ((T + bn - 1) / bn)), dim3(128), router_tc_smem(), st, wm.router,
+                         x_rows, ta)) != cudaSuccess)
     return e;
+  const RouterFixArgs fa{w.router_pm, w.bias, w.router_norm, sc.router_approx, x, sc.logits, sc.sh_logit,
+                         s.E, s.H, T, s.K};
+  if ((e = launch_router_fix(fa, st)) != cudaSuccess) return e;
   return launch_route_block(s, luts, sc, T, topk_idx, topk_score, false, count_pairs ? sc.pair_count : nullptr, st);
 }
 
@@ -1099,7 +1295,7 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   cudaError_t e;
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
   if ((e = mark(0)) != cudaSuccess) return e;
-  if ((e = launch_prefill_front(s, w, luts, sc, x, T, topk_idx, topk_score, true, st)) != cudaSuccess) return e;
+  if ((e = launch_prefill_front(s, w, wm, luts, sc, x, T, topk_idx, topk_score, true, st)) != cudaSuccess) return e;
   if ((e = mark(1)) != cudaSuccess) return e;
   if ((e = launch_prefill_group(s, sc, topk_idx, T * s.K, x, 0, 1, s.E, T, false, st)) != cudaSuccess) return e;
   if ((e = mark(2)) != cudaSuccess) return e;
