@@ -203,10 +203,17 @@ struct PrefillWeightMaps {
   CUtensorMap router;      // router [E][H] (reference layout), 128-row x 64-column boxes
 };
 // Tensor maps of the fixed scratch (activations between the two GEMMs).
+// Token-tile maps of one operand: boxes of 16, 32, 64, 128 and 256 rows
+// (64 columns, 128-byte swizzle); a tile of n rows (a multiple of 16) is
+// loaded as the binary decomposition of n, at most five copies.
+constexpr int kTokenBoxes = 5;
+struct TokenMaps {
+  CUtensorMap box[kTokenBoxes];
+};
 struct PrefillScratchMaps {
-  CUtensorMap xg;      // [T*K][H] grouped input rows, 16-row boxes
-  CUtensorMap act;     // [T*K][I] grouped SwiGLU rows, 16-row boxes
-  CUtensorMap act_sh;  // [T][Is]
+  TokenMaps xg;      // [H/64][pair_cap][64] grouped input rows
+  TokenMaps act;     // [I/64][pair_cap][64] grouped SwiGLU rows
+  TokenMaps act_sh;  // [Is/64][T][64] shared expert SwiGLU rows
 };
 // Whether the prefill kernels support this shape (H a multiple of 256, 2I
 // and 2Is multiples of 128).

@@ -22,17 +22,21 @@
 //
 // The shared expert is one more slot whose token list is all T tokens.
 //
-// GEMM kernel (k_gemm): persistent, one CTA per SM, 10 warps.
+// GEMM kernel (k_gemm): persistent, one CTA per SM, 11 warps.
 //   warp 0  producer: TMA loads of the weight tile (4-D map over the tiled
 //           bank: 128 rows x 64 columns = 16 KB, already in the 128-byte
-//           swizzled K-major operand layout) and of the token tile (16-row
-//           boxes of contiguous rows, 128-byte swizzle) into a 4-stage ring.
-//   warp 1  MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> f32),
+//           swizzled K-major operand layout) into a 4-stage ring.
+//   warp 1  producer: TMA loads of the token tile (contiguous rows, 128-byte
+//           swizzle) into a 4-stage ring, as the binary decomposition of the
+//           tile's rows into boxes of 256, 128, 64, 32 and 16 rows (one copy
+//           for a whole chunk: the number of copies per stage, not their
+//           bytes, was the limit with 16-row boxes).
+//   warp 2  MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> f32),
 //           M = 128 weight rows, N = the unit's tokens rounded up to 16
 //           (<= 256), K = 64 per stage as 4 instructions; accumulators in
 //           TMEM, double-buffered (2 x 256 columns); tcgen05.commit frees
 //           ring stages and hands finished accumulators to the epilogue.
-//   warps 2-9 epilogue, two sets of four: tcgen05.ld of the accumulator
+//   warps 3-10 epilogue, two sets of four: tcgen05.ld of the accumulator
 //           (warp w reads TMEM lanes 32*(w%4)..+31; the sets take alternate
 //           32-column groups), bf16 rounding points of the reference, stores.
 // Work unit = (slot, 256-token chunk, 128-row tile); units are numbered
@@ -277,7 +281,7 @@ __device__ __forceinline__ void produce(const GemmArgs& a, const int* s_prefix, 
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap map_a_r, const __grid_constant__ CUtensorMap map_a_s,
-           const __grid_constant__ CUtensorMap map_b_r, const __grid_constant__ CUtensorMap map_b_s, GemmArgs a) {
+           const __grid_constant__ TokenMaps map_b_r, const __grid_constant__ TokenMaps map_b_s, GemmArgs a) {
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte alignment for the swizzled operand tiles.
   const uint32_t raw = smem_u32(smem_raw);
@@ -344,12 +348,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         [&](const Unit& w, int) { return static_cast<uint32_t>(w.bn * kBK * 2); },
         [&](const Unit& w, int kb, int st, uint64_t* bar) {
           unsigned char* sb = ring_b + st * kBBytes;
-          const CUtensorMap* mb = w.routed ? &map_b_r : &map_b_s;
+          const TokenMaps* mb = w.routed ? &map_b_r : &map_b_s;
           // K-blocked operands: block kb's rows n0.. are one contiguous run.
           const bool blocked = w.routed || a.b_blocked_s;
           const int c0 = blocked ? 0 : kb * kBK;
           const int r0 = (blocked ? kb * (w.routed ? a.rows_r : a.rows_s) : 0) + w.n0;
-          for (int j = lane * 16; j < w.bn; j += 512) tma_load_2d(sb + j * 128, mb, c0, r0 + j, bar);
+          // bn (a multiple of 16, <= 256) as boxes of 256, 128, ..., 16 rows
+          if (lane == 0) {
+            int j = 0;
+#pragma unroll
+            for (int b = kTokenBoxes - 1; b >= 0; --b)
+              if (w.bn & (16 << b)) {
+                tma_load_2d(sb + j * 128, &mb->box[b], c0, r0 + j, bar);
+                j += 16 << b;
+              }
+          }
         });
   } else if (warp == 2) {
     // ---------------- MMA issuer ----------------
@@ -1126,6 +1139,13 @@ bool rows_map(CUtensorMap* m, const uint16_t* base, int cols, long long rows, in
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The five token-tile boxes of a row-major [rows][cols] operand.
+bool token_maps(TokenMaps* m, const uint16_t* base, int cols, long long rows) {
+  for (int b = 0; b < kTokenBoxes; ++b)
+    if (!rows_map(&m->box[b], base, cols, rows, 16 << b)) return false;
+  return true;
+}
+
 int sm_count() {
   static std::once_flag once;
   static int n = 148;
@@ -1156,8 +1176,8 @@ bool make_prefill_scratch_maps(const Shape& s, const Scratch& sc, PrefillScratch
   if (!prefill_supported(s)) return false;
   // K-blocked [K/64][rows][64] operands as 64-column row-major views.
   const long long P = sc.pair_cap, M = sc.max_T;
-  return rows_map(&out->xg, sc.xg, 64, (s.H / 64) * P, 16) && rows_map(&out->act, sc.act, 64, (s.I / 64) * P, 16) &&
-         rows_map(&out->act_sh, sc.act_sh, 64, (s.Is / 64) * M, 16);
+  return token_maps(&out->xg, sc.xg, 64, (s.H / 64) * P) && token_maps(&out->act, sc.act, 64, (s.I / 64) * P) &&
+         token_maps(&out->act_sh, sc.act_sh, 64, (s.Is / 64) * M);
 }
 
 cudaError_t launch_router_tables(const uint16_t* w, const uint16_t* extra_row, int E, int H, float* norms,
@@ -1231,12 +1251,15 @@ cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, co
                                  const uint16_t* score, const int32_t* send_pos, uint16_t* out_rows,
                                  cudaStream_t st) {
   // Per-forward map of this rank's input rows (the shared expert's token tiles).
-  CUtensorMap x_rows;
-  if (!rows_map(&x_rows, x_own, s.H, T_own, 16)) return cudaErrorInvalidValue;
+  TokenMaps x_rows;
+  if (!token_maps(&x_rows, x_own, s.H, T_own)) return cudaErrorInvalidValue;
   cudaError_t e;
   const size_t smem = gemm_smem_bytes(ecount);
   const dim3 grid(sm_count()), block(kGemmThreads);
   GemmArgs g{};
+  auto launch = [&](const CUtensorMap& ma_r, const CUtensorMap& ma_s, const TokenMaps& mb_r, const TokenMaps& mb_s) {
+    return launch_pdl_ex(k_gemm, grid, block, smem, st, ma_r, ma_s, mb_r, mb_s, g);
+  };
   g.E = ecount;
   g.T = T_own;
   g.K = s.K;
@@ -1265,9 +1288,7 @@ cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, co
   g.groups_r = 2 * s.I / 8;
   g.b_blocked_s = 0;  // shared up: the row-major input
   g.prefix = sc.unit_prefix;
-  if ((e = launch_pdl_ex(k_gemm, grid, block, smem, st, wm.gate_up, wm.sh_gate_up, smaps.xg, x_rows, g)) !=
-      cudaSuccess)
-    return e;
+  if ((e = launch(wm.gate_up, wm.sh_gate_up, smaps.xg, x_rows)) != cudaSuccess) return e;
   // down + route weight / shared gate
   g.phase = 1;
   g.kb_r = s.I / kBK;
@@ -1277,7 +1298,7 @@ cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, co
   g.groups_r = s.H / 8;
   g.b_blocked_s = 1;  // shared down: K-blocked act_sh
   g.prefix = sc.unit_prefix + ecount + 2;
-  return launch_pdl_ex(k_gemm, grid, block, smem, st, wm.down, wm.sh_down, smaps.act, smaps.act_sh, g);
+  return launch(wm.down, wm.sh_down, smaps.act, smaps.act_sh);
 }
 
 cudaError_t launch_ep_positions(const int32_t* idx, int n, int group_len, int me, int world, bool recv,
