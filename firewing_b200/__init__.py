@@ -23,6 +23,7 @@ from .moe import (  # noqa: F401
     library_path,
     linear_bf16,
     route_bf16,
+    safetensors_tensor_info,
     swiglu_bf16,
     topk_bf16,
 )

@@ -531,6 +531,12 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
   return FW_OK;
 }
 
+int fw_moe_get_config(const fw_moe* h, fw_moe_config* out) {
+  if (h == nullptr || out == nullptr) return fail(FW_EINVAL, "null argument");
+  *out = h->cfg;
+  return FW_OK;
+}
+
 int fw_moe_destroy(fw_moe* h) {
   if (h == nullptr) return FW_OK;
   cudaSetDevice(h->device);

@@ -47,7 +47,6 @@ template <bool kTiled> struct RingCfg {
   static constexpr int kRing = 2;                                     // stages per warp ring
   static constexpr int kStageBytes = kTiled ? 8192 : 8 * (512 * 2 + 16);  // 8192 / 8320
 };
-constexpr int kMaxChunk = 512;                    // columns per stage
 constexpr int kMaxTGP = 8;                        // tokens per pass (upper bound)
 constexpr int kSmemMeta = 512;                    // mbarriers, abort flag, token table
 constexpr uint64_t kWaitNs = 2000000000ull;       // bounded waits: 2 s

@@ -93,6 +93,12 @@ def library() -> ctypes.CDLL:
     L.fw_moe_forward_hc.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp]
     L.fw_moe_forward_hc_async.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp, vp]
     L.fw_moe_ep_init.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_char_p]
+    L.fw_moe_load_layer_safetensors.argtypes = [vp, ctypes.c_int32, ctypes.c_char_p, ctypes.c_char_p]
+    L.fw_moe_load_hc_safetensors.argtypes = [vp, ctypes.c_int32, ctypes.c_char_p, ctypes.c_char_p]
+    L.fw_safetensors_tensor_info.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
+                                             ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int32),
+                                             ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
+    L.fw_moe_get_config.argtypes = [vp, ctypes.POINTER(_Config)]
     L.fw_moe_memory.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_profile.argtypes = [vp, ctypes.c_int32]
     L.fw_moe_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
@@ -108,7 +114,8 @@ def library() -> ctypes.CDLL:
                  "fw_moe_forward", "fw_moe_forward_async", "fw_moe_sync", "fw_moe_memory",
                  "fw_moe_profile", "fw_moe_profile_read", "fw_moe_set_prefill_min_tokens",
                  "fw_ep_unique_id", "fw_moe_ep_init", "fw_moe_load_hc", "fw_moe_forward_hc",
-                 "fw_moe_forward_hc_async",
+                 "fw_moe_forward_hc_async", "fw_moe_load_layer_safetensors", "fw_moe_load_hc_safetensors",
+                 "fw_safetensors_tensor_info", "fw_moe_get_config",
                  "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
@@ -236,6 +243,18 @@ class MoeBlock:
                 for a in (hc_norm, mix_down, mix_up, inject)]
         _check(library().fw_moe_load_hc(self._h, layer, lowrank, *[_ptr(a) for a in keep]))
 
+    def load_layer_safetensors(self, layer: int, checkpoint: str, prefix: str) -> None:
+        """The block's BF16 tensors under `prefix` (e.g.
+        "model.language_model.layers.0.mlp") from a safetensors checkpoint: a
+        directory with model.safetensors.index.json, or one file."""
+        _check(library().fw_moe_load_layer_safetensors(self._h, layer, os.fsencode(checkpoint),
+                                                        prefix.encode()))
+
+    def load_hc_safetensors(self, layer: int, checkpoint: str, prefix: str) -> None:
+        """Hyper-connection tensors under `prefix` (e.g.
+        "model.language_model.layers.0.mlp_hyper_connection")."""
+        _check(library().fw_moe_load_hc_safetensors(self._h, layer, os.fsencode(checkpoint), prefix.encode()))
+
     def forward_hc(self, layer: int, post: np.ndarray):
         """Attention output post [T][4H] (host) -> (layer output [T][4H],
         top-k ids [T][K], scores [T][K]) through the hyper-connection caller
@@ -266,6 +285,21 @@ class MoeBlock:
         v = ctypes.c_uint64()
         _check(library().fw_moe_memory(self._h, ctypes.byref(v)))
         return int(v.value)
+
+
+def safetensors_tensor_info(file: str, tensor: str) -> dict:
+    """Validate a safetensors file as the checkpoint loader does and report
+    one tensor: {"dtype", "shape", "offset", "bytes"} (offset within the
+    payload).  Raises FwError on any validation failure."""
+    L = library()
+    dtype = ctypes.create_string_buffer(16)
+    shape = (ctypes.c_int64 * 8)()
+    rank = ctypes.c_int32()
+    offset, nbytes = ctypes.c_uint64(), ctypes.c_uint64()
+    _check(L.fw_safetensors_tensor_info(os.fsencode(file), tensor.encode(), dtype, shape, ctypes.byref(rank),
+                                        ctypes.byref(offset), ctypes.byref(nbytes)))
+    return {"dtype": dtype.value.decode(), "shape": [int(shape[i]) for i in range(rank.value)],
+            "offset": int(offset.value), "bytes": int(nbytes.value)}
 
 
 def ep_owner(expert: int, world: int) -> int:

@@ -70,6 +70,8 @@ const char* fw_last_error(void);
  * does (src/metal_moe.rs:95-223, 385-392, 399-421). */
 int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out);
 int fw_moe_destroy(fw_moe* handle);
+/* The configuration the handle was created with. */
+int fw_moe_get_config(const fw_moe* handle, fw_moe_config* out);
 
 /* Copy one layer's weights (host or device pointers) into memory the handle
  * owns.  Layouts: router [E][H] (model.layers.N.mlp.gate.weight);
@@ -172,6 +174,33 @@ int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);
  *     count, in the same order.  FW_ENCCL on collective errors. */
 int fw_ep_unique_id(uint8_t id[128]);
 int fw_moe_ep_init(fw_moe* handle, int32_t rank, int32_t world, const uint8_t id[128]);
+
+/* Weights from a safetensors checkpoint (no reference counterpart as a C
+ * call: the reference reads the same tensors with read_expert_slice /
+ * read_tensor_2d, src/expert.rs:362-512, and its mapped checkpoint catalog,
+ * src/checkpoint_catalog.rs:146-443).  `checkpoint` is a directory holding
+ * model.safetensors.index.json and its shards, or one .safetensors file;
+ * shards are memory-mapped and validated as the reference validates them
+ * (header length, dtypes, shapes, offsets, overlaps, index consistency).
+ *   fw_moe_load_layer_safetensors: the block's tensors under `prefix`
+ *     (e.g. "model.language_model.layers.0.mlp"): gate.weight [E][H],
+ *     experts.gate_up_proj [E][2I][H], experts.down_proj [E][H][I],
+ *     shared_expert.{gate,up}_proj.weight [Is][H],
+ *     shared_expert.down_proj.weight [H][Is], shared_expert_gate.weight
+ *     [1][H]; all BF16.  Under expert parallelism only this rank's experts
+ *     are copied to the device.
+ *   fw_moe_load_hc_safetensors: the hyper-connection tensors under `prefix`
+ *     (e.g. "model.language_model.layers.0.mlp_hyper_connection"):
+ *     hc_norm.weight [4H], input_mix_weight_down.weight [LR][4H],
+ *     input_mix_weight_up.weight [4H][LR], block_inject_weight.weight
+ *     [4][4H]; LR from the checkpoint.
+ *   fw_safetensors_tensor_info: handle-free; validates one file and reports a
+ *     tensor's dtype, shape (rank <= 8) and payload range.
+ * FW_EINVAL with a message naming the tensor on any mismatch. */
+int fw_moe_load_layer_safetensors(fw_moe* handle, int32_t layer, const char* checkpoint, const char* prefix);
+int fw_moe_load_hc_safetensors(fw_moe* handle, int32_t layer, const char* checkpoint, const char* prefix);
+int fw_safetensors_tensor_info(const char* file, const char* tensor, char dtype[16], int64_t shape[8],
+                               int32_t* rank, uint64_t* offset, uint64_t* bytes);
 
 /* Wait for `stream`, then report and clear device-side status. */
 int fw_moe_sync(fw_moe* handle, void* stream);
