@@ -180,6 +180,10 @@ struct fw_moe {
   bool prefill_ok = false;            // shape supported and scratch maps built
   fw::PrefillScratchMaps pf_maps{};
   int prefill_min_tokens = kDecodeMaxTokens + 1;  // forwards this wide or wider take the prefill path
+  // The last forward (fw_moe_last_union): 0 none, 1 decode (expert schedule),
+  // 2 prefill (grouped pair offsets over `last_experts` bank experts).
+  int last_path = 0, last_experts = 0;
+  cudaStream_t last_stream = nullptr;
   // Expert parallelism (fw_moe_ep_init): this rank's expert range, the NCCL
   // communicator and the exchange buffers (world * max_tokens tokens).
   fw::EpComm* ep = nullptr;
@@ -782,6 +786,15 @@ int fw_moe_synth_layer(fw_moe* h, int32_t layer, uint64_t seed, float std_dev, i
   return FW_OK;
 }
 
+namespace {
+// Remember which path the forward took, for fw_moe_last_union.
+void note_forward(fw_moe* h, bool prefill, cudaStream_t st) {
+  h->last_path = prefill ? 2 : 1;
+  h->last_experts = held_experts(h);
+  h->last_stream = st;
+}
+}  // namespace
+
 int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t tokens, uint16_t* y,
                          int32_t* topk_idx, uint16_t* topk_scores, void* stream) {
   FW_TRY(check_handle(h, layer));
@@ -799,10 +812,12 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
   if (h->ep != nullptr) {
     const bool ep_prefill = tokens > h->ep_decode_max || tokens >= h->prefill_min_tokens;
-    if (!ep_prefill) return ep_forward(h, L, x, tokens, y, idx, sc, cs, ev);
-    if (!L.prefill || h->ep_send_pos == nullptr)
+    if (ep_prefill && (!L.prefill || h->ep_send_pos == nullptr))
       return fail(FW_EINVAL, "this many tokens need the prefill path, which this handle's shape lacks");
-    return ep_prefill_forward(h, L, x, tokens, y, idx, sc, cs, ev);
+    const int rc = ep_prefill ? ep_prefill_forward(h, L, x, tokens, y, idx, sc, cs, ev)
+                              : ep_forward(h, L, x, tokens, y, idx, sc, cs, ev);
+    if (rc == FW_OK) note_forward(h, ep_prefill, cs);
+    return rc;
   }
   const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
   if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
@@ -810,6 +825,28 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
       prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev)
               : fw::launch_block(h->shape, L.w, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev);
   if (e != cudaSuccess) return fail(FW_ECUDA, std::string("launch: ") + cudaGetErrorString(e));
+  note_forward(h, prefill, cs);
+  return FW_OK;
+}
+
+int fw_moe_last_union(fw_moe* h, int32_t* distinct_experts, uint64_t* weight_bytes) {
+  if (h == nullptr || distinct_experts == nullptr || weight_bytes == nullptr)
+    return fail(FW_EINVAL, "null argument");
+  if (h->last_path == 0) return fail(FW_EINVAL, "no forward has run on this handle");
+  FW_CUDA(cudaSetDevice(h->device));
+  FW_CUDA(cudaStreamSynchronize(h->last_stream));
+  int n = 0;
+  if (h->last_path == 1) {
+    FW_CUDA(cudaMemcpy(&n, h->sc.sched, sizeof(int), cudaMemcpyDeviceToHost));  // n_active
+  } else {
+    std::vector<int> off(static_cast<size_t>(h->last_experts) + 1);
+    FW_CUDA(cudaMemcpy(off.data(), h->sc.pair_offset, off.size() * sizeof(int), cudaMemcpyDeviceToHost));
+    for (int e = 0; e < h->last_experts; ++e) n += off[e + 1] > off[e] ? 1 : 0;
+  }
+  const uint64_t H = h->cfg.hidden, I = h->cfg.intermediate, Is = h->cfg.shared_intermediate;
+  const uint64_t E = h->cfg.experts;
+  *distinct_experts = n;
+  *weight_bytes = 2 * (E * H + H + 3 * H * Is + static_cast<uint64_t>(n) * 3 * H * I);
   return FW_OK;
 }
 
@@ -934,6 +971,7 @@ int fw_moe_forward_hc_async(fw_moe* h, int32_t layer, const uint16_t* post, int3
               : fw::launch_block(h->shape, L.w, h->luts, h->sc, h->hs.mixed, tokens, h->hc_moe, idx, sc, cs, ev,
                                  &hp);
   if (e != cudaSuccess) return fail(FW_ECUDA, std::string("launch: ") + cudaGetErrorString(e));
+  note_forward(h, prefill, cs);
   return FW_OK;
 }
 

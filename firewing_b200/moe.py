@@ -99,6 +99,7 @@ def library() -> ctypes.CDLL:
                                              ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int32),
                                              ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_get_config.argtypes = [vp, ctypes.POINTER(_Config)]
+    L.fw_moe_last_union.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_memory.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_profile.argtypes = [vp, ctypes.c_int32]
     L.fw_moe_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
@@ -115,7 +116,7 @@ def library() -> ctypes.CDLL:
                  "fw_moe_profile", "fw_moe_profile_read", "fw_moe_set_prefill_min_tokens",
                  "fw_ep_unique_id", "fw_moe_ep_init", "fw_moe_load_hc", "fw_moe_forward_hc",
                  "fw_moe_forward_hc_async", "fw_moe_load_layer_safetensors", "fw_moe_load_hc_safetensors",
-                 "fw_safetensors_tensor_info", "fw_moe_get_config",
+                 "fw_safetensors_tensor_info", "fw_moe_get_config", "fw_moe_last_union",
                  "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
@@ -242,6 +243,13 @@ class MoeBlock:
         keep = [np.ascontiguousarray(a) if isinstance(a, np.ndarray) else a
                 for a in (hc_norm, mix_down, mix_up, inject)]
         _check(library().fw_moe_load_hc(self._h, layer, lowrank, *[_ptr(a) for a in keep]))
+
+    def last_union(self) -> dict:
+        """Expert union of the last forward: {"distinct_experts": U (routed
+        experts streamed on this GPU), "weight_bytes": bytes read}."""
+        n, b = ctypes.c_int32(), ctypes.c_uint64()
+        _check(library().fw_moe_last_union(self._h, ctypes.byref(n), ctypes.byref(b)))
+        return {"distinct_experts": int(n.value), "weight_bytes": int(b.value)}
 
     def load_layer_safetensors(self, layer: int, checkpoint: str, prefix: str) -> None:
         """The block's BF16 tensors under `prefix` (e.g.

@@ -202,6 +202,16 @@ int fw_moe_load_hc_safetensors(fw_moe* handle, int32_t layer, const char* checkp
 int fw_safetensors_tensor_info(const char* file, const char* tensor, char dtype[16], int64_t shape[8],
                                int32_t* rank, uint64_t* offset, uint64_t* bytes);
 
+/* The expert union of the last forward on the handle (synchronises its
+ * stream): the distinct routed experts it streamed on this GPU (U), and the
+ * weight bytes it read: router, shared gate, shared expert and those U
+ * experts once each, however many of the forward's tokens selected them.
+ * With speculative decoding, a verify forward over the proposal positions
+ * reads U experts for T tokens; the caller divides its accepted tokens (A)
+ * by U as the reference's A / U accounting does (docs/ARCHITECTURE.md:93-96,
+ * src/mtp_transaction.rs:182-212).  FW_EINVAL before the first forward. */
+int fw_moe_last_union(fw_moe* handle, int32_t* distinct_experts, uint64_t* weight_bytes);
+
 /* Wait for `stream`, then report and clear device-side status. */
 int fw_moe_sync(fw_moe* handle, void* stream);
 

@@ -10,7 +10,8 @@ each token's owner in the receive layout of ep_combine_row; the owner's
 ascending-expert-id sum plus its shared expert.
 """
 import os
-import socket
+import tempfile
+from datetime import timedelta
 
 import numpy as np
 import pytest
@@ -26,10 +27,10 @@ import firewing_b200 as fw  # noqa: E402
 SHAPE = dict(hidden=256, intermediate=128, shared_intermediate=192, experts=64, top_k=4)
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous() -> str:
+    """A file-based rendezvous (no port to collide with another process)."""
+    d = tempfile.mkdtemp(prefix="fw_ep_")
+    return "file://" + os.path.join(d, "store")
 
 
 def _bf16_add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
@@ -48,10 +49,8 @@ def _gather(arr: np.ndarray, world: int) -> np.ndarray:
     return torch.cat(out).numpy().astype(arr.dtype)
 
 
-def _rank_main(rank: int, world: int, port: int, seed: int, t_local: int, zipf: bool, q) -> None:
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _rank_main(rank: int, world: int, store: str, seed: int, t_local: int, zipf: bool, q) -> None:
+    dist.init_process_group("gloo", init_method=store, rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
         shape = O.BlockShape(**SHAPE)
         H, I, Is, E, K = (SHAPE[k] for k in ("hidden", "intermediate", "shared_intermediate", "experts",
@@ -112,8 +111,8 @@ def test_ep_decomposition_matches_single_device_oracle(zipf):
     world, t_local = 2, 6
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, 31, t_local, zipf, q)) for r in range(world)]
+    store = _rendezvous()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, store, 31, t_local, zipf, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -5,7 +5,8 @@ where scores match; the same selection everywhere).  Skipped with fewer than
 two GPUs.
 """
 import os
-import socket
+import tempfile
+from datetime import timedelta
 
 import numpy as np
 import pytest
@@ -21,23 +22,23 @@ SMALL = dict(hidden=256, intermediate=128, shared_intermediate=192, experts=64, 
 CFG0 = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10)
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous() -> str:
+    """A file-based rendezvous (no port to collide with another process)."""
+    d = tempfile.mkdtemp(prefix="fw_ep_")
+    return "file://" + os.path.join(d, "store")
 
 
-def _rank_main(rank, world, port, shape, t_local, layers, zipf, q, min_tokens=None):
+def _rank_main(rank, world, store, shape, t_local, layers, zipf, q, min_tokens=None):
     import torch.distributed as dist
 
     import firewing_b200 as fw
 
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     # No NVLink multicast objects in a test that may stop a rank early.
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a rank that fails ends the other's collectives within a minute
+    dist.init_process_group("gloo", init_method=store, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
     try:
         uid = [fw.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
@@ -88,13 +89,13 @@ def _run(shape, t_local, layers, zipf, min_tokens=None):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, shape, t_local, layers, zipf, q, min_tokens))
+    store = _rendezvous()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, store, shape, t_local, layers, zipf, q, min_tokens))
              for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=600)
+        p.join(timeout=300)
     for p in procs:
         if p.is_alive():
             p.kill()
