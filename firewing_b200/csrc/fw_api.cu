@@ -207,6 +207,11 @@ struct fw_moe {
   uint16_t* hc_out_dev = nullptr;    // [M][4H]
 };
 
+namespace fw {
+HandlePlace handle_place(const fw_moe* h) { return HandlePlace{h->device, h->ep_rank, h->ep_world}; }
+}  // namespace fw
+
+
 namespace {
 
 template <typename T>
@@ -676,6 +681,33 @@ int fw_moe_load_layer(fw_moe* h, int32_t layer, const uint16_t* router, const ui
   L.w.expert_count = ecount;
   L.prefill = h->prefill_ok && fw::make_prefill_weight_maps(h->shape, L.w, &L.maps);
   L.loaded = true;
+  return FW_OK;
+}
+
+int fw_moe_load_expert(fw_moe* h, int32_t layer, int32_t expert, const uint16_t* gate_up, const uint16_t* down) {
+  FW_TRY(check_handle(h, layer));
+  if (expert < 0 || expert >= h->cfg.experts) return fail(FW_EINVAL, "expert out of range");
+  if (gate_up == nullptr || down == nullptr) return fail(FW_EINVAL, "gate_up / down is null");
+  if (expert % h->ep_world != h->ep_rank) return fail(FW_EINVAL, "expert is held by another rank");
+  FW_CUDA(cudaSetDevice(h->device));
+  OwnedLayer& L = h->layers[layer];
+  const size_t H = h->cfg.hidden, I = h->cfg.intermediate;
+  const long long bank = expert / h->ep_world;  // bank index of the expert on this GPU
+  const fw::TiledSpec gu{0, static_cast<int>(H), static_cast<int>(I), static_cast<long long>(2 * I * H),
+                         static_cast<long long>(2 * I * H)};
+  const fw::TiledSpec dn{1, static_cast<int>(I), 0, static_cast<long long>(H * I), static_cast<long long>(H * I)};
+  uint16_t* tmp = nullptr;
+  cudaError_t e = cudaMalloc(&tmp, 3 * H * I * 2);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, gate_up, 2 * I * H * 2, cudaMemcpyDefault, h->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(tmp + 2 * I * H, down, H * I * 2, cudaMemcpyDefault, h->stream);
+  // the banks are this handle's own buffers
+  if (e == cudaSuccess) e = fw::launch_relayout(gu, bank, 1, tmp, nullptr, const_cast<uint16_t*>(L.w.gate_up), h->stream);
+  if (e == cudaSuccess)
+    e = fw::launch_relayout(dn, bank, 1, tmp + 2 * I * H, nullptr, const_cast<uint16_t*>(L.w.down), h->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+  if (tmp) cudaFree(tmp);
+  if (e != cudaSuccess)
+    return fail(e == cudaErrorMemoryAllocation ? FW_ENOMEM : FW_ECUDA, "expert load", cudaGetErrorString(e));
   return FW_OK;
 }
 

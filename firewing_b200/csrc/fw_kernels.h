@@ -6,6 +6,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+struct fw_moe;  // the C ABI handle (include/fwmoe.h)
+
 namespace fw {
 
 // Device-side status codes written to the per-handle error word (first
@@ -301,6 +303,12 @@ const char* ep_exchange_rows(EpComm* c, const uint16_t* send, const int* rows_se
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.
 int record_error(int code, const char* msg);
+// Where a handle lives: its device and, under expert parallelism, its rank
+// and world (rank 0 of 1 otherwise).
+struct HandlePlace {
+  int device, rank, world;
+};
+HandlePlace handle_place(const fw_moe* h);
 
 // Seeded synthetic weights written straight into the tiled layout: element
 // d takes the generator value of its reference index under stream

@@ -100,6 +100,11 @@ def library() -> ctypes.CDLL:
                                              ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_get_config.argtypes = [vp, ctypes.POINTER(_Config)]
     L.fw_moe_last_union.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_uint64)]
+    L.fw_moe_load_expert.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, vp, vp]
+    L.fw_moe_load_expert_container.argtypes = [vp, ctypes.c_int32, ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32,
+                                               ctypes.POINTER(ctypes.c_int32)]
+    L.fw_codec_container_check.argtypes = [ctypes.c_char_p, ctypes.c_int32, ctypes.c_uint64, ctypes.c_int32,
+                                           ctypes.POINTER(ctypes.c_int32)]
     L.fw_moe_memory.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_profile.argtypes = [vp, ctypes.c_int32]
     L.fw_moe_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
@@ -116,7 +121,8 @@ def library() -> ctypes.CDLL:
                  "fw_moe_profile", "fw_moe_profile_read", "fw_moe_set_prefill_min_tokens",
                  "fw_ep_unique_id", "fw_moe_ep_init", "fw_moe_load_hc", "fw_moe_forward_hc",
                  "fw_moe_forward_hc_async", "fw_moe_load_layer_safetensors", "fw_moe_load_hc_safetensors",
-                 "fw_safetensors_tensor_info", "fw_moe_get_config", "fw_moe_last_union",
+                 "fw_safetensors_tensor_info", "fw_moe_get_config", "fw_moe_last_union", "fw_moe_load_expert",
+                 "fw_moe_load_expert_container", "fw_codec_container_check",
                  "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
@@ -251,6 +257,20 @@ class MoeBlock:
         _check(library().fw_moe_last_union(self._h, ctypes.byref(n), ctypes.byref(b)))
         return {"distinct_experts": int(n.value), "weight_bytes": int(b.value)}
 
+    def load_expert(self, layer: int, expert: int, gate_up, down) -> None:
+        """Replace one routed expert of a loaded layer: gate_up [2I][H] and
+        down [H][I] (reference layout), host arrays or device tensors."""
+        keep = [np.ascontiguousarray(a) if isinstance(a, np.ndarray) else a for a in (gate_up, down)]
+        _check(library().fw_moe_load_expert(self._h, layer, expert, _ptr(keep[0]), _ptr(keep[1])))
+
+    def load_expert_container(self, layer: int, manifest: str, container_layer: int, verify: bool = True) -> int:
+        """Experts of `container_layer` from a compressed container (zstd
+        frames of byte-shuffled BF16) into `layer`; returns how many."""
+        n = ctypes.c_int32()
+        _check(library().fw_moe_load_expert_container(self._h, layer, os.fsencode(manifest), container_layer,
+                                                      1 if verify else 0, ctypes.byref(n)))
+        return int(n.value)
+
     def load_layer_safetensors(self, layer: int, checkpoint: str, prefix: str) -> None:
         """The block's BF16 tensors under `prefix` (e.g.
         "model.language_model.layers.0.mlp") from a safetensors checkpoint: a
@@ -308,6 +328,16 @@ def safetensors_tensor_info(file: str, tensor: str) -> dict:
                                         ctypes.byref(offset), ctypes.byref(nbytes)))
     return {"dtype": dtype.value.decode(), "shape": [int(shape[i]) for i in range(rank.value)],
             "offset": int(offset.value), "bytes": int(nbytes.value)}
+
+
+def codec_container_check(manifest: str, layer: int, source_bytes_per_expert: int, verify: bool = True) -> int:
+    """Validate a compressed expert container's manifest and decode (and with
+    `verify`, hash-check) the records of `layer` (all when < 0) without a
+    GPU; returns the number of records.  Raises FwError on any mismatch."""
+    n = ctypes.c_int32()
+    _check(library().fw_codec_container_check(os.fsencode(manifest), layer, source_bytes_per_expert,
+                                              1 if verify else 0, ctypes.byref(n)))
+    return int(n.value)
 
 
 def ep_owner(expert: int, world: int) -> int:

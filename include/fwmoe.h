@@ -202,6 +202,36 @@ int fw_moe_load_hc_safetensors(fw_moe* handle, int32_t layer, const char* checkp
 int fw_safetensors_tensor_info(const char* file, const char* tensor, char dtype[16], int64_t shape[8],
                                int32_t* rank, uint64_t* offset, uint64_t* bytes);
 
+/* Replace one routed expert of a loaded layer: gate_up [2I][H] and down
+ * [H][I] in the reference layout, host or device pointers (the reference
+ * streams experts one at a time into its resident buffers,
+ * src/metal_moe.rs:162-207; src/compressed_overlap.rs).  Synchronous; not
+ * concurrent with a forward of the same layer.  Under expert parallelism
+ * only experts this rank holds (FW_EINVAL otherwise). */
+int fw_moe_load_expert(fw_moe* handle, int32_t layer, int32_t expert, const uint16_t* gate_up,
+                       const uint16_t* down);
+
+/* Compressed expert containers, the reference's streamed-expert format
+ * (tools/build_sequential_shuffle_container.py, read by
+ * src/compressed_overlap.rs): one independent zstd frame per (layer, expert)
+ * at a page-aligned offset of `container_file`, listed by a JSON manifest
+ * (records {layer, expert, offset, compressed_bytes, physical_bytes,
+ * frame_sha256, source_sha256}); a frame decompresses to the expert's
+ * gate_up then down bytes, shuffled (even bytes, then odd bytes).
+ *   fw_moe_load_expert_container: every record of `container_layer` into
+ *     layer `layer` of the handle (experts held by this rank); the host
+ *     decompresses (libzstd, loaded at run time, several frames at once),
+ *     the GPU un-shuffles and re-lays the expert out.  verify != 0 checks
+ *     both SHA-256 digests.  *loaded = experts replaced.
+ *   fw_codec_container_check: handle-free; validates the manifest and
+ *     decodes (and with verify, hashes) the records of `layer` (all when
+ *     layer < 0) for experts of source_bytes_per_expert bytes.
+ * FW_EINVAL on any format, size or hash mismatch. */
+int fw_moe_load_expert_container(fw_moe* handle, int32_t layer, const char* manifest, int32_t container_layer,
+                                 int32_t verify, int32_t* loaded);
+int fw_codec_container_check(const char* manifest, int32_t layer, uint64_t source_bytes_per_expert,
+                             int32_t verify, int32_t* records);
+
 /* The expert union of the last forward on the handle (synchronises its
  * stream): the distinct routed experts it streamed on this GPU (U), and the
  * weight bytes it read: router, shared gate, shared expert and those U
