@@ -27,7 +27,7 @@ def test_container_and_single_expert_loads_match_oracle(tmp_path):
     bshape = O.BlockShape(**SMALL)
     x = O.synth_input(7, 8, SMALL["hidden"])
     ref_layer = O.SynthLayer(bshape, 21)
-    _, idx0, _ = O.router(bshape, ref_layer, x)
+    idx0, _, _ = O.router(bshape, ref_layer, x)
     chosen = sorted(set(int(v) for v in idx0.ravel()))[:6] + [63]
     for e in chosen:
         ref_layer.gate_up[e], ref_layer.down[e] = replacement(e)
