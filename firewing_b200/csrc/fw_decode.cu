@@ -421,7 +421,7 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
 }
 
 __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   const int E = a.E, K = a.K;
   const int t = blockIdx.x;
   const int e = threadIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
 // Expert parallelism: the schedule of this GPU's experts over every rank's
 // tokens (a.idx holds the gathered selections), built by one CTA.
 __global__ void __launch_bounds__(1024) k_schedule(RouteArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   pdl_wait();
   pdl_launch_dependents();
   build_schedule(a, smem);
