@@ -14,6 +14,7 @@ from .moe import (  # noqa: F401
     FwError,
     MoeBlock,
     MoeConfig,
+    add_bf16,
     codec_container_check,
     ep_combine_row,
     ep_held_experts,

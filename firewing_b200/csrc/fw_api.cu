@@ -1078,6 +1078,14 @@ int fw_swiglu_bf16(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t
   return FW_OK;
 }
 
+int fw_add_bf16(const uint16_t* a, const uint16_t* b, int64_t n, uint16_t* out, void* stream) {
+  if (!a || !b || !out || n < 0) return fail(FW_EINVAL, "bad argument");
+  if (n == 0) return FW_OK;
+  const cudaError_t e = fw::launch_add_bf16(a, b, n, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(FW_ECUDA, std::string("add: ") + cudaGetErrorString(e));
+  return FW_OK;
+}
+
 int fw_route_bf16(const uint16_t* logits, int32_t tokens, int32_t experts, int32_t top_k,
                   int32_t* indices, uint16_t* scores, void* stream) {
   if (!logits || !indices || !scores) return fail(FW_EINVAL, "null argument");

@@ -25,6 +25,21 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float v) {
   if ((b & 0x7fffffffu) > 0x7f800000u) return 0x7fc0u;
   return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
 }
+// a + b per bf16 half (low and high), rounded once to bf16 with round to
+// nearest even, NaN results as 0x7fc0: bit-identical to
+// f32_to_bf16(bf16_to_f32(a) + bf16_to_f32(b)) per half (the reference's
+// add_bf16, src/expert.rs:578).  For two bf16 operands the f32 sum is exact
+// unless their exponents differ by 16 or more; the smaller operand is then
+// below 2^-15 of the larger, under half a bf16 step, and both roundings give
+// the larger operand.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  uint32_t lo = r & 0xffffu, hi = r >> 16;
+  lo = (lo & 0x7fffu) > 0x7f80u ? 0x7fc0u : lo;
+  hi = (hi & 0x7fffu) > 0x7f80u ? 0x7fc0u : hi;
+  return lo | (hi << 16);
+}
 // Two packed bf16 values (little-endian: element 0 in the low half).
 __device__ __forceinline__ float lo_bf16(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }

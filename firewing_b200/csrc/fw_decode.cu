@@ -559,15 +559,15 @@ struct CombineArgs {
   HcPost hc;  // hyper-connection injection (hc.out null: none)
 };
 
-__global__ void k_combine(CombineArgs a) {
+__global__ void __launch_bounds__(512, 2) k_combine(CombineArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   const int t = blockIdx.x;
   const int c = threadIdx.x * 8;
   if (c >= a.H) return;
-  uint32_t acc[8];
+  uint32_t acc[4];  // 8 bf16 sums, two per word
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0;  // bf16(0.0)
+  for (int i = 0; i < 4; ++i) acc[i] = 0;  // bf16(0.0) pairs
   const int32_t* ss = a.sorted_slot + static_cast<size_t>(t) * a.K;
   // Issue the slot loads, then all row loads of a group, before any add, so
   // the dependent loads cost two memory latencies per 8 experts.
@@ -591,24 +591,16 @@ __global__ void k_combine(CombineArgs a) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (n0 + i < a.K) {
-        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc[2 * j] = f32_to_bf16(bf16_to_f32(acc[2 * j]) + lo_bf16(w[j]));
-          acc[2 * j + 1] = f32_to_bf16(bf16_to_f32(acc[2 * j + 1]) + hi_bf16(w[j]));
-        }
+        acc[0] = add_bf16x2(acc[0], v[i].x);
+        acc[1] = add_bf16x2(acc[1], v[i].y);
+        acc[2] = add_bf16x2(acc[2], v[i].z);
+        acc[3] = add_bf16x2(acc[3], v[i].w);
       }
     }
   }
   const uint4 sv = *reinterpret_cast<const uint4*>(a.gated_sh + static_cast<size_t>(t) * a.H + c);
-  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t l = f32_to_bf16(bf16_to_f32(acc[2 * i]) + lo_bf16(sw[i]));
-    const uint32_t h = f32_to_bf16(bf16_to_f32(acc[2 * i + 1]) + hi_bf16(sw[i]));
-    o[i] = l | (h << 16);
-  }
+  const uint32_t o[4] = {add_bf16x2(acc[0], sv.x), add_bf16x2(acc[1], sv.y), add_bf16x2(acc[2], sv.z),
+                         add_bf16x2(acc[3], sv.w)};
   *reinterpret_cast<uint4*>(a.y + static_cast<size_t>(t) * a.H + c) = make_uint4(o[0], o[1], o[2], o[3]);
   if (a.hc.out == nullptr) return;
   // Hyper-connection injection (src/decoder_layer.rs:587-607):
@@ -633,6 +625,23 @@ __global__ void k_combine(CombineArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// out = add_bf16(a, b) elementwise (src/expert.rs:578); n even elements
+// go two per step, an odd tail alone.
+__global__ void k_add_bf16(const uint16_t* a, const uint16_t* b, long long n, uint16_t* out) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; 2 * i < n; i += stride) {
+    if (2 * i + 1 < n) {
+      const uint32_t x = static_cast<uint32_t>(a[2 * i]) | (static_cast<uint32_t>(a[2 * i + 1]) << 16);
+      const uint32_t y = static_cast<uint32_t>(b[2 * i]) | (static_cast<uint32_t>(b[2 * i + 1]) << 16);
+      const uint32_t r = add_bf16x2(x, y);
+      out[2 * i] = static_cast<uint16_t>(r & 0xffffu);
+      out[2 * i + 1] = static_cast<uint16_t>(r >> 16);
+    } else {
+      out[2 * i] = static_cast<uint16_t>(add_bf16x2(a[2 * i], b[2 * i]) & 0xffffu);
+    }
+  }
+}
+
 __global__ void k_swiglu(const uint16_t* gate, const uint16_t* up, long long n,
                          const uint16_t* lut, uint16_t* out) {
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
@@ -737,6 +746,14 @@ cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* i
   RouteArgs a{logits, T, E, K, idx, score, err, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
               0, 0, 0, 0, nullptr, nullptr, 0, 1, T};
   return launch_route_kernel(a, st);
+}
+
+cudaError_t launch_add_bf16(const uint16_t* a, const uint16_t* b, long long n, uint16_t* out, cudaStream_t st) {
+  const long long pairs = (n + 1) / 2;
+  const long long blocks = (pairs + 255) / 256;
+  const int grid = static_cast<int>(blocks < 4096 ? (blocks > 0 ? blocks : 1) : 4096);
+  k_add_bf16<<<grid, 256, 0, st>>>(a, b, n, out);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, long long n,

@@ -192,6 +192,8 @@ cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int co
                           uint16_t* y, cudaStream_t st);
 cudaError_t launch_route(const uint16_t* logits, int T, int E, int K, int32_t* idx,
                          uint16_t* score, int* err, cudaStream_t st);
+// out = add_bf16(a, b) elementwise, n elements (src/expert.rs:578).
+cudaError_t launch_add_bf16(const uint16_t* a, const uint16_t* b, long long n, uint16_t* out, cudaStream_t st);
 cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, long long n,
                           const uint16_t* silu_lut, uint16_t* out, cudaStream_t st);
 

@@ -110,6 +110,7 @@ def library() -> ctypes.CDLL:
     L.fw_moe_profile_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.c_int32]
     L.fw_linear_bf16.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp]
     L.fw_swiglu_bf16.argtypes = [vp, vp, ctypes.c_int64, vp, vp]
+    L.fw_add_bf16.argtypes = [vp, vp, ctypes.c_int64, vp, vp]
     L.fw_route_bf16.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp, vp]
     L.fw_moe_forward_noalloc.argtypes = [ctypes.POINTER(_Config), ctypes.POINTER(_Weights), vp,
                                          ctypes.c_int32, vp, vp, vp, vp]
@@ -123,7 +124,7 @@ def library() -> ctypes.CDLL:
                  "fw_moe_forward_hc_async", "fw_moe_load_layer_safetensors", "fw_moe_load_hc_safetensors",
                  "fw_safetensors_tensor_info", "fw_moe_get_config", "fw_moe_last_union", "fw_moe_load_expert",
                  "fw_moe_load_expert_container", "fw_codec_container_check",
-                 "fw_linear_bf16", "fw_swiglu_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
+                 "fw_linear_bf16", "fw_swiglu_bf16", "fw_add_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
@@ -381,6 +382,11 @@ def forward_noalloc(config: MoeConfig, weights: dict, x, tokens: int, y, topk_id
 
 def linear_bf16(w, x, rows: int, cols: int, tokens: int, y, stream=None) -> None:
     _check(library().fw_linear_bf16(_ptr(w), _ptr(x), rows, cols, tokens, _ptr(y), _stream(stream)))
+
+
+def add_bf16(a, b, n: int, out, stream=None) -> None:
+    """out = add_bf16(a, b) for n bf16 elements (device tensors)."""
+    _check(library().fw_add_bf16(_ptr(a), _ptr(b), n, _ptr(out), _stream(stream)))
 
 
 def swiglu_bf16(gate, up, n: int, out, stream=None) -> None:

@@ -302,6 +302,9 @@ int fw_linear_bf16(const uint16_t* w, const uint16_t* x, int32_t rows, int32_t c
  * src/metal_moe.rs:385-392. */
 int fw_swiglu_bf16(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out,
                    void* stream);
+/* out[i] = add_bf16(a[i], b[i]) (src/expert.rs:578): bf16 round to nearest
+ * even of the f32 sum, NaN as 0x7fc0; device pointers, stream-ordered. */
+int fw_add_bf16(const uint16_t* a, const uint16_t* b, int64_t n, uint16_t* out, void* stream);
 
 /* In-layer route for `tokens` logit rows [T][experts]: top-k (logit
  * descending, ties by ascending index, src/router.rs:241-247), f32 softmax,
