@@ -165,6 +165,30 @@ __device__ __forceinline__ bool epi_any(int set, bool v) {
   return r != 0;
 }
 
+
+// ---- packed bf16 epilogue arithmetic --------------------------------------------
+// bf16 bits with NaN as 0x7fc0 (the canonical pattern of f32_to_bf16).
+__device__ __forceinline__ uint32_t nanfix_bf16x2(uint32_t r) {
+  uint32_t lo = r & 0xffffu, hi = r >> 16;
+  lo = (lo & 0x7fffu) > 0x7f80u ? 0x7fc0u : lo;
+  hi = (hi & 0x7fffu) > 0x7f80u ? 0x7fc0u : hi;
+  return lo | (hi << 16);
+}
+// {bf16(lo), bf16(hi)} round to nearest even, one instruction for the pair.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return nanfix_bf16x2(r);
+}
+// a * b per bf16 half, one rounding (a bf16 x bf16 product is exact in f32
+// outside the f32 subnormal range, so this equals f32_to_bf16 of the f32
+// product there).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return nanfix_bf16x2(r);
+}
+
 // ---- work units ---------------------------------------------------------------
 
 struct GemmArgs {
@@ -454,30 +478,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // (row & 7) < 4 own a gate row and take the matching up value
           // from lane + 4.  swiglu_bf16 (src/expert.rs:562-571) on the bf16
           // outputs of linear_bf16: bf16(bf16(silu(g)) * u).
-          uint32_t gb[32];
-          float ub[32];
+          uint32_t gb[16], ub[16];  // bf16 pairs: columns j, j+1
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float g = __uint_as_float(v[j]);
-            const float up = __shfl_down_sync(0xffffffffu, g, 4);
-            gb[j] = f32_to_bf16(g);
-            ub[j] = bf16_to_f32(f32_to_bf16(up));
+          for (int j = 0; j < 32; j += 2) {
+            const float g0 = __uint_as_float(v[j]), g1 = __uint_as_float(v[j + 1]);
+            const float u0 = __shfl_down_sync(0xffffffffu, g0, 4), u1 = __shfl_down_sync(0xffffffffu, g1, 4);
+            gb[j / 2] = cvt_bf16x2(g0, g1);
+            ub[j / 2] = cvt_bf16x2(u0, u1);
           }
           if ((lane & 7) < 4) {
-            uint16_t sl[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) sl[j] = a.silu[gb[j]];
             const int il = 16 * q + 4 * (lane >> 3) + (lane & 3);  // intermediate within the tile
 #pragma unroll
-            for (int j = 0; j < 32; ++j) stage[j * 64 + il] = f32_to_bf16(bf16_to_f32(sl[j]) * ub[j]);
+            for (int j = 0; j < 32; j += 2) {
+              const uint32_t s2 = static_cast<uint32_t>(a.silu[gb[j / 2] & 0xffffu]) |
+                                  (static_cast<uint32_t>(a.silu[gb[j / 2] >> 16]) << 16);
+              const uint32_t p2 = mul_bf16x2(s2, ub[j / 2]);
+              stage[j * 64 + il] = static_cast<uint16_t>(p2 & 0xffffu);
+              stage[(j + 1) * 64 + il] = static_cast<uint16_t>(p2 >> 16);
+            }
           }
         } else {
           // routed: bf16(bf16(down) * route weight) (src/expert.rs:748-751);
           // shared: bf16(sigmoid * bf16(down)) (src/expert.rs:1144-1147)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float dv = bf16_to_f32(f32_to_bf16(__uint_as_float(v[j])));
-            stage[j * 128 + row] = f32_to_bf16(dv * s_col_scale[c0 + j]);
+          for (int j = 0; j < 32; j += 2) {
+            const uint32_t d2 = cvt_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+            const uint32_t s2 = __float_as_uint(s_col_scale[c0 + j]) >> 16 |
+                                (__float_as_uint(s_col_scale[c0 + j + 1]) & 0xffff0000u);
+            const uint32_t p2 = mul_bf16x2(d2, s2);
+            stage[j * 128 + row] = static_cast<uint16_t>(p2 & 0xffffu);
+            stage[(j + 1) * 128 + row] = static_cast<uint16_t>(p2 >> 16);
           }
         }
         epi_sync(set);
