@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Sparse-MoE block benchmark (tokens/s + roofline) on B200.
 
-Default workload = BASELINE config 1: a 24-layer stack of the config-0 block
+Default workload = benchmark config 1: a 24-layer stack of the config-0 block
 (H=2048, 512 experts, top-10, I = Is = 512, bf16 weights ~N(0,0.02) from
 seeds 1..24, inputs bf16 N(0,1) RMS-normalised), decode at T=64 tokens per
 layer (T=4 is reported alongside).  A step = every layer of the stack over
@@ -33,18 +33,18 @@ WORKLOADS = {
                  layers=24, tokens=64, zipf=False,
                  name="cfg1: 24-layer stack of the config-0 block, decode"),
 }
-# Reported alongside at N > 1 (not the headline): BASELINE config 3, expert
+# Reported alongside at N > 1 (not the headline): benchmark config 3, expert
 # parallelism over the N GPUs.
 EP = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10,
           tokens=256, layers=24, layers_8=48,
           name="cfg3: {layers}-layer stack of the config-0 block, EP over {world} GPUs ({per} experts "
                "per GPU), decode T=256 per layer, uniform routing")
-# Reported alongside (not the headline): BASELINE config 4, the larger block
+# Reported alongside (not the headline): benchmark config 4, the larger block
 # at prefill width, 12 layers; one GPU at N = 1, expert-parallel at N > 1.
 CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512, top_k=10,
             tokens=8192, layers=12, zipf=True,
             name="cfg4: 12-layer stack, H=3072, I=Is=768, Zipf-biased router, prefill T=8192 per GPU")
-# Reported alongside (not the headline): BASELINE config 2, one block at
+# Reported alongside (not the headline): benchmark config 2, one block at
 # prefill width with the Zipf-biased router, on the tensor-core path.
 PREFILL = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10,
                tokens=8192, zipf=True, seed=1,
@@ -449,7 +449,7 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
 
 
 def measure_prefill(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier):
-    """BASELINE config 2 on the tensor-core prefill path: one block, T=8192
+    """benchmark config 2 on the tensor-core prefill path: one block, T=8192
     tokens, Zipf-biased router.  CUDA events around `steps` forwards with
     device-resident inputs; a per-stage pass afterwards."""
     import torch
@@ -517,7 +517,7 @@ def measure_prefill(args, rank, world, local_rank, peaks, stream, max_over_ranks
 
 
 def measure_cfg4(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist):
-    """12 layers of the larger block at prefill width,
+    """benchmark config 4: 12 layers of the larger block at prefill width,
     8192 tokens per GPU per layer, Zipf-biased router.  One GPU at N = 1;
     expert parallelism over the N GPUs otherwise (rank r holds the experts
     e with e % N == r).  Whole-job token-layers/s and its per-GPU share,
@@ -576,7 +576,7 @@ def measure_cfg4(args, rank, world, local_rank, peaks, stream, max_over_ranks, b
 
 
 def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, barrier, dist):
-    """BASELINE config 3 on `world` GPUs with expert parallelism: decode of
+    """benchmark config 3 on `world` GPUs with expert parallelism: decode of
     256 tokens per layer in total (256/world per rank), uniform routing, a
     48-layer stack at 8 GPUs (64 experts per GPU), 24 layers at 2 or 4.
     Rank r holds the experts e with e % world == r of every layer; each

@@ -1,6 +1,6 @@
 """GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
 
-Bar: selected expert indices identical except where
+Bar (the target's stated tolerance): selected expert indices identical except where
 router logits tie; block output within max-abs 2e-2 and relative-L2 1e-3.
 The CUDA path keeps the reference's reduction order, so outputs are expected
 bit-identical; the only licensed difference is a renormalised score one bf16
@@ -179,7 +179,7 @@ CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512,
 
 @pytest.mark.parametrize("T", [1, 4, 33])
 def test_block_config4_shape_zipf(T):
-    # BASELINE config 4's block (H=3072, I=Is=768) on the decode path.
+    # Benchmark config 4's block (H=3072, I=Is=768) on the decode path.
     _, _, _, got, ref = run_pair(CFG4, 3, T, zipf=True)
     assert_block_close(got[0], ref[0], got[1], ref[1], got[2], ref[2], ref[3]["logits"])
 
