@@ -267,11 +267,12 @@ int check_handle(const fw_moe* h, int32_t layer) {
 // skewed router's hot low-id experts over the GPUs.
 int held_experts(const fw_moe* h) { return h->cfg.experts / h->ep_world; }
 
-// The prefill router's per-layer tables (row-norm bounds, partial-major
-// copy), stream-ordered after the router weights and the shared gate
-// vector; shapes without a prefill path need none.
+// The router's per-layer tables (row-norm bounds for the prefill router,
+// the partial-major copy both routers read), stream-ordered after the router
+// weights and the shared gate vector; hidden sizes that are not a multiple
+// of 256 use the other decode router and have no prefill path.
 int router_tables(fw_moe* h, OwnedLayer& L) {
-  if (!fw::prefill_supported(h->shape)) return FW_OK;
+  if (h->cfg.hidden % 256 != 0) return FW_OK;  // the decode router's 16-byte chunks and the prefill path need it
   const size_t E = h->cfg.experts, H = h->cfg.hidden;
   float* norms = nullptr;
   uint16_t* pm = nullptr;

@@ -40,6 +40,20 @@ __device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
   hi = (hi & 0x7fffu) > 0x7f80u ? 0x7fc0u : hi;
   return lo | (hi << 16);
 }
+// acc += lo(w) * lo(x), then acc += hi(w) * hi(x): mixed-precision FMAs
+// (bf16 operands, f32 accumulator); an exact bf16 product and one rounding
+// per add, as the reference's multiply then add.
+__device__ __forceinline__ float fma_seq2(uint32_t w, uint32_t x, float acc) {
+  asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+      "mov.b32 {w0, w1}, %1;\n\t"
+      "mov.b32 {x0, x1}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, w0, x0, %0;\n\t"
+      "fma.rn.f32.bf16 %0, w1, x1, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(w), "r"(x));
+  return acc;
+}
+
 // Two packed bf16 values (little-endian: element 0 in the low half).
 __device__ __forceinline__ float lo_bf16(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }

@@ -739,19 +739,6 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-// acc += lo(w) * lo(x), then acc += hi(w) * hi(x): mixed-precision FMAs
-// (bf16 operands, f32 accumulator); an exact bf16 product and one rounding
-// per add, as the reference's multiply then add.
-__device__ __forceinline__ float fma_seq2(uint32_t w, uint32_t x, float acc) {
-  asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
-      "mov.b32 {w0, w1}, %1;\n\t"
-      "mov.b32 {x0, x1}, %2;\n\t"
-      "fma.rn.f32.bf16 %0, w0, x0, %0;\n\t"
-      "fma.rn.f32.bf16 %0, w1, x1, %0;\n\t}"
-      : "+f"(acc)
-      : "r"(w), "r"(x));
-  return acc;
-}
 
 // One warp per token (see the section comment).  Lane j holds the token's
 // columns j, j+32, ... (PX bf16 pairs at most: H <= 64 * PX) in registers,

@@ -184,6 +184,17 @@ def test_block_config4_shape_zipf(T):
     assert_block_close(got[0], ref[0], got[1], ref[1], got[2], ref[2], ref[3]["logits"])
 
 
+# A hidden size that is not a multiple of 256: the decode router without the
+# partial-major copy (and no prefill path).
+ODD_H = dict(hidden=192, intermediate=128, shared_intermediate=128, experts=64, top_k=4)
+
+
+@pytest.mark.parametrize("T", [1, 6])
+def test_block_hidden_not_multiple_of_256(T):
+    _, _, _, got, ref = run_pair(ODD_H, 6, T, zipf=True)
+    assert_block_close(got[0], ref[0], got[1], ref[1], got[2], ref[2], ref[3]["logits"])
+
+
 def test_block_all_ties_input():
     # x = 0 -> every logit 0: selection 0..K-1, equal scores (tie rule).
     x = np.zeros((2, SMALL["hidden"]), dtype=np.uint16)
