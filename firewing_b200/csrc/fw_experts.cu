@@ -576,7 +576,432 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
   }
 }
 
+// ---- small widths: one producer warp, a CTA-wide ring ----------------------
+//
+// At a few tokens the FMA work per stage is small and the kernel above is
+// bound by its structure: 8 per-warp rings of 2 stages hold whole 4-stage up
+// units, so at ~9.5 up units per CTA half the warps idle while the others
+// stream a second unit, and every pass boundary is a CTA barrier.  This
+// variant (tiled layout, T <= kSmallMaxT) keeps the same schedule, cost
+// space and CTA ranges but splits loading from arithmetic:
+//   - warp 7 (one lane) walks the CTA's stage sequence -- its up units, then
+//     its down units -- and streams every stage into a CTA-wide ring of R
+//     stages (about 200 KB at T = 1) with one bulk copy each, gated by the
+//     ring's empty barriers, so the bytes in flight do not depend on how the
+//     units fall on warps;
+//   - warps 0..6 take the CTA's units round-robin, each unit's stages in
+//     order, with no CTA barriers: the up activations are all T token rows,
+//     staged once; the down activations (SwiGLU of the slot's gate/up rows)
+//     go to a per-warp buffer after a per-warp bounded wait on up_done.
+// A unit's FMA chain, reduction and epilogue are those of the kernel above.
+// Deadlock freedom: all up stages precede all down stages in the producer's
+// order, and R exceeds a unit's stage count, so every up unit of every CTA
+// completes without waiting on a down unit; down units wait only on up
+// units.  Every wait is bounded and also ends when another warp aborted.
+
+constexpr int kSmallMaxT = 4;      // widths served by the small-width kernel (measured: T = 8 is faster on the kernel above)
+constexpr int kSmallSlot = 8192;   // ring slot: one tiled stage (8 rows x <= 512 columns)
+constexpr int kSmallMaxR = 32;     // ring slots at most
+// "Full" barriers are indexed by stage mod kSmallFull, independently of the
+// ring slot (stage mod R).  Stages are issued in steps of 8, in order across
+// steps; F = the first stage of the current step (all below it issued).  A
+// consumer waits on stage g only after its previous unit is consumed, so
+// g < F + 8 + 7 units x 8 stages; every stage below F - R is consumed.  With
+// kSmallFull >= R + 64 the barrier's previous use (stage g - kSmallFull) has
+// landed whenever g is waited on, and its next use (g + kSmallFull) cannot
+// be issued before g is consumed, so the parity names the right phase.
+constexpr int kSmallFull = 128;
+constexpr int kIssueLanes = 8;     // producer lanes issuing one stage each per step
+constexpr unsigned kIssueMask = 0xffu;
+constexpr int kSmallWarps = 7;     // consumer warps; warp 7 is the producer (8 warps keep 255 registers)
+constexpr int kSmallThreads = (kSmallWarps + 1) * 32;
+
+struct SmallLayout {
+  size_t bars, meta, tables, pairs, toks, xs, wact, total;
+  int nx, ntmax, kdmax;
+};
+
+__host__ __device__ inline size_t align128(size_t v) { return (v + 127) & ~static_cast<size_t>(127); }
+
+// Shared-memory plan of a CTA with R ring slots: ring, full/empty barriers,
+// abort flag, schedule tables, pair tables, per-warp token tables, the token
+// rows (x, then the shared expert's rows when they are a separate buffer),
+// per-warp down activations.
+__host__ __device__ inline SmallLayout small_layout(int H, int I, int Is, int E, int K, int T, int sh_T,
+                                                    bool sh_separate, int tgp, int R) {
+  SmallLayout L{};
+  L.nx = T + (sh_separate ? sh_T : 0);
+  L.ntmax = T < tgp ? (T > 0 ? T : 1) : tgp;
+  L.kdmax = I > Is ? I : Is;
+  L.bars = static_cast<size_t>(R) * kSmallSlot;
+  L.meta = L.bars + align128(static_cast<size_t>(kSmallFull + R) * 8);
+  L.tables = L.meta + 128;
+  L.pairs = L.tables + align128(static_cast<size_t>(4) * (E + 2) * 4);
+  L.toks = L.pairs + align128(static_cast<size_t>(2 * T * K + sh_T) * 4);
+  L.xs = L.toks + align128(static_cast<size_t>(3) * kSmallWarps * kMaxTGP * 4);
+  L.wact = L.xs + align128(static_cast<size_t>(L.nx) * H * 2);
+  L.total = L.wact + align128(static_cast<size_t>(kSmallWarps) * L.ntmax * L.kdmax * 2);
+  return L;
+}
+
+// Ring slots for a small-width launch: the most that fit, at least twice a
+// unit's stage count (and 12); 0 when the width is not served.
+inline int small_ring_slots(const Shape& s, int T, int sh_T, bool sh_separate, int tgp, size_t smem_max) {
+  if (T < 1 || T > kSmallMaxT) return 0;
+  const int nch = max(s.H / chunk_cols(s.H), max(s.I / chunk_cols(s.I), s.Is / chunk_cols(s.Is)));
+  const int r_min = max(12, 2 * nch + 2);
+  if (nch > 8) return 0;  // the full-barrier bound assumes units of at most 8 stages
+  for (int R = kSmallMaxR; R >= r_min; --R)
+    if (small_layout(s.H, s.I, s.Is, s.E, s.K, T, sh_T, sh_separate, tgp, R).total <= smem_max) return R;
+  return 0;
+}
+
+// Bounded wait on a ring barrier that also ends when another warp aborted.
+__device__ __forceinline__ bool ring_wait(uint64_t* bar, uint32_t parity, volatile int* s_abort, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*s_abort) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      set_error(err, kErrTimeout);
+      *s_abort = 1;
+      return false;
+    }
+  }
+}
+
+// Accumulate one tiled stage against NT token rows given by pointer (the
+// stage's column chunk starts at col0 of each row).
+template <int NT>
+__device__ __forceinline__ void stage_fma_rows(const unsigned char* buf, int cols, const uint16_t* const (&xr)[NT],
+                                               int col0, int r, int q, float (&acc)[kMaxTGP][8]) {
+  const unsigned char* wrow = buf + r * 128;
+  const int nb = cols >> 5;
+#pragma unroll 4
+  for (int b = 0; b < nb; ++b) {
+    const int off = (b >> 1) * 1024 + (((4 * (b & 1) + q) ^ r) << 4);
+    const uint4 w = *reinterpret_cast<const uint4*>(wrow + off);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      fma8_bf16(w, *reinterpret_cast<const uint4*>(xr[t] + col0 + b * 32 + q * 8), acc[t]);
+  }
+}
+
+// One unit (all of its stages, starting at ring stage g) for NT padded tokens.
+template <int NT>
+__device__ __forceinline__ bool small_unit(const Ctx& c, const Pass& p, int item, int nt, const uint16_t* const (&rows)[kMaxTGP],
+                                           unsigned char* ring, uint64_t* full, uint64_t* empty, int R, int g,
+                                           int lane, volatile int* s_abort, const int* tok_row,
+                                           const float* tok_scale) {
+  const int r = lane & 7, q = lane >> 3;
+  const int nch = n_chunks(c, p.phase, p.s), cols = chunk_width(c, p.phase, p.s);
+  const uint16_t* xr[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) xr[t] = rows[t];
+  float acc[kMaxTGP][8];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[t][i] = 0.0f;
+  for (int ch = 0; ch < nch; ++ch, ++g) {
+    const int slot = g % R;
+    const bool ok = ring_wait(&full[g % kSmallFull], (g / kSmallFull) & 1, s_abort, c.a->err);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    stage_fma_rows<NT>(ring + static_cast<size_t>(slot) * kSmallSlot, cols, xr, ch * cols, r, q, acc);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  epilogue<NT>(c, p, item, nt, acc, lane, tok_row, tok_scale);
+  return true;
+}
+
+// Publish n stored up units of slot s: the warp's stores, then a release
+// (fence + add) by lane 0.
+__device__ __forceinline__ void flush_up(int* up_done, int s, int n, int lane) {
+  __syncwarp();
+  if (lane == 0 && n > 0) {
+    __threadfence();
+    atomicAdd(&up_done[s], n);
+  }
+}
+
+__global__ void __launch_bounds__(kSmallThreads, 1) k_experts_small(const __grid_constant__ ExpertsArgs a, int R) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const bool sh_sep = a.sh_x != a.x;
+  const SmallLayout L = small_layout(a.H, a.I, a.Is, a.E, a.K, a.T, a.sh_T, sh_sep, a.tgp, R);
+  unsigned char* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);  // [kSmallFull]
+  uint64_t* empty = full + kSmallFull;                           // [R]
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L.meta);
+  int32_t* tables = reinterpret_cast<int32_t*>(smem + L.tables);
+  int32_t* s_pairs = reinterpret_cast<int32_t*>(smem + L.pairs);
+  float* s_pscore = reinterpret_cast<float*>(s_pairs + a.T * a.K);
+  float* s_shsig = s_pscore + a.T * a.K;
+  int* toks = reinterpret_cast<int*>(smem + L.toks);
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem + L.xs);
+  uint16_t* wact = reinterpret_cast<uint16_t*>(smem + L.wact);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    *s_abort = 0;
+    for (int i = 0; i < kSmallFull; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < R; ++i) mbar_init(&empty[i], 1);
+  }
+  fence_mbar_init();
+
+  pdl_wait();  // the schedule comes from the route kernel
+  pdl_launch_dependents();
+
+  Ctx c;
+  c.a = &a;
+  c.n_active = a.sched[0];
+  {
+    const int n = c.n_active;
+    const int32_t* g_act = a.sched + 1;
+    const int32_t* g_off = a.sched + 1 + a.E;
+    const int32_t* g_pairs = a.sched + 2 + 2 * a.E;
+    const int32_t* g_up = g_pairs + a.T * a.K;
+    const int32_t* g_dn = g_up + (a.E + 2);
+    int32_t* s_up = tables;
+    int32_t* s_dn = tables + (a.E + 2);
+    int32_t* s_off = tables + 2 * (a.E + 2);
+    int32_t* s_act = s_off + (a.E + 2);
+    for (int i = threadIdx.x; i < n + 2; i += kSmallThreads) {
+      s_up[i] = g_up[i];
+      s_dn[i] = g_dn[i];
+      if (i <= n) s_off[i] = g_off[i];
+      if (i < n) s_act[i] = g_act[i];
+    }
+    for (int i = threadIdx.x; i < a.T * a.K; i += kSmallThreads) {
+      s_pairs[i] = g_pairs[i];
+      s_pscore[i] = bf16_to_f32(a.pair_score[i]);
+    }
+    for (int i = threadIdx.x; i < a.sh_T; i += kSmallThreads) s_shsig[i] = bf16_to_f32(a.sh_sig[i]);
+    // every token row the up units read: x, then the shared expert's rows
+    // when they are a separate buffer
+    const int per_row = a.H >> 3;
+    for (int i = threadIdx.x; i < L.nx * per_row; i += kSmallThreads) {
+      const int t = i / per_row, c8 = (i - t * per_row) * 8;
+      const uint16_t* src = t < a.T ? a.x + static_cast<size_t>(t) * a.H : a.sh_x + static_cast<size_t>(t - a.T) * a.H;
+      *reinterpret_cast<uint4*>(xs + static_cast<size_t>(t) * a.H + c8) = *reinterpret_cast<const uint4*>(src + c8);
+    }
+    c.up_pref = s_up;
+    c.dn_pref = s_dn;
+    c.offs = s_off;
+    c.act_ids = s_act;
+  }
+  c.qpr = a.I / 4;
+  c.qps = a.Is / 4;
+  c.ops = a.H / 8;
+  c.cu = chunk_cols(a.H);
+  c.cdr = chunk_cols(a.I);
+  c.cds = chunk_cols(a.Is);
+  __syncthreads();  // tables, rows and barrier init visible to all warps
+  {
+    const long long G = gridDim.x, b = blockIdx.x;
+    const long long U = c.up_pref[c.n_active + 1], D = c.dn_pref[c.n_active + 1];
+    c.lo[0] = static_cast<int>(U * b / G);
+    c.hi[0] = static_cast<int>(U * (b + 1) / G);
+    c.lo[1] = static_cast<int>(D * b / G);
+    c.hi[1] = static_cast<int>(D * (b + 1) / G);
+  }
+
+  // Producer: lanes 0..7 issue 8 consecutive stages per step (one copy
+  // each), so one step's instruction stream serves 8 stages.  Lane j's slot
+  // was last used by stage g - R, issued in an earlier step (R > 8).
+  int issued = 0;           // stages issued in complete steps (uniform over the issuing lanes)
+  unsigned tail_mask = 0u;  // after an abort: lanes of the last step that issued
+  if (warp == kSmallWarps) {
+    if (lane < kIssueLanes) {
+      const uint64_t policy = l2_evict_first_policy();
+      bool stop = false;
+      for (int phase = 0; phase < 2 && !stop; ++phase) {
+        Pass p;
+        bool ok = first_pass(c, phase, p);
+        while (ok && !stop) {
+          Cursor k;
+          k.p = p;
+          cursor_slot(k, c);
+          const int n = (p.qb - p.qa) * k.nchunks;  // stages of this pass
+          const uint32_t bytes = 8u * k.cols * 2;
+          for (int o0 = 0; o0 < n; o0 += kIssueLanes) {
+            const int o = o0 + lane, gs = issued + lane;
+            bool good = true, sent = false;
+            if (o < n) {
+              const int slot = gs % R;
+              if (gs >= R) good = ring_wait(&empty[slot], ((gs / R) - 1) & 1, s_abort, a.err);
+              if (good) {
+                fence_proxy_async_smem();
+                uint64_t* fb = &full[gs % kSmallFull];
+                mbar_arrive_expect_tx(fb, bytes);
+                const int item = p.qa + o / k.nchunks, ch = o % k.nchunks;
+                const size_t tile = static_cast<size_t>(item) * k.nchunks + ch;
+                bulk_g2s(ring + static_cast<size_t>(slot) * kSmallSlot, k.row0 + tile * 8 * k.cols, bytes, fb,
+                         policy);
+                sent = true;
+              }
+            }
+            if (__any_sync(kIssueMask, !good)) {
+              tail_mask = __ballot_sync(kIssueMask, sent);
+              stop = true;
+              break;
+            }
+            issued += min(kIssueLanes, n - o0);
+          }
+          ok = next_pass(c, p);
+        }
+      }
+    }
+  } else {
+    int* tok_row = toks + warp * kMaxTGP;
+    float* tok_scale = reinterpret_cast<float*>(toks + (kSmallWarps + warp) * kMaxTGP);
+    int* tok_x = toks + (2 * kSmallWarps + warp) * kMaxTGP;
+    uint16_t* my_act = wact + static_cast<size_t>(warp) * L.ntmax * L.kdmax;
+    int g = 0, u = 0;
+    int cur_phase = -1, cur_s = -1, cur_tg = -1;
+    int nt = 0, nt_pad = 1, kd = 0;
+    const uint16_t* rows[kMaxTGP];
+    int pend_s = -1, pend_n = 0;  // up units stored but not yet counted in up_done
+    bool aborted = false;
+    for (int phase = 0; phase < 2 && !aborted; ++phase) {
+      Pass p;
+      bool ok = first_pass(c, phase, p);
+      while (ok && !aborted) {
+        const int nch = n_chunks(c, phase, p.s);
+        for (int item = p.qa; item < p.qb; ++item, ++u, g += nch) {
+          if (u % kSmallWarps != warp) continue;
+          if (phase != cur_phase || p.s != cur_s || p.tg != cur_tg) {
+            // this warp enters a new pass: its token table and activations
+            const bool routed = p.s < c.n_active;
+            const int t0 = p.tg * a.tgp;
+            nt = min(a.tgp, slot_tokens(c, p.s) - t0);
+            nt_pad = pad_tokens(nt);
+            kd = phase == 0 ? a.H : (routed ? a.I : a.Is);
+            __syncwarp();  // the previous pass's readers of the table and buffer are done
+            if (lane < nt) {
+              if (routed) {
+                const int pr = s_pairs[c.offs[p.s] + t0 + lane];
+                tok_row[lane] = pr;
+                tok_scale[lane] = s_pscore[pr];
+                tok_x[lane] = pr / a.K;
+              } else {
+                tok_row[lane] = t0 + lane;
+                tok_scale[lane] = s_shsig[t0 + lane];
+                tok_x[lane] = (sh_sep ? a.T : 0) + t0 + lane;
+              }
+            }
+            if (phase == 1) {
+              // all of the slot's up units are stored (bounded wait)
+              const int target = ((slot_tokens(c, p.s) + a.tgp - 1) / a.tgp) * units_per_pass(c, 0, p.s);
+              int good = 1;
+              if (lane == 0 && ld_acquire_gpu(&a.up_done[p.s]) < target) {
+                const uint64_t w0 = global_ns();
+                while (ld_acquire_gpu(&a.up_done[p.s]) < target) {
+                  if (*s_abort) {
+                    good = 0;
+                    break;
+                  }
+                  if (global_ns() - w0 > kWaitNs) {
+                    set_error(a.err, kErrTimeout);
+                    *s_abort = 1;
+                    good = 0;
+                    break;
+                  }
+                  __nanosleep(64);
+                }
+              }
+              if (!__shfl_sync(0xffffffffu, good, 0)) {
+                aborted = true;
+                break;
+              }
+              (void)ld_acquire_gpu(&a.up_done[p.s]);  // every lane: acquire before reading the rows
+              // SwiGLU (src/expert.rs:562-571) of the stored gate/up rows,
+              // bf16(bf16(silu(g)) * u), silu from the table
+              const int per_row = kd >> 3;
+              for (int i = lane; i < nt * per_row; i += 32) {
+                const int t = i / per_row, c8 = (i - t * per_row) * 8;
+                const uint16_t* row = routed ? a.act + static_cast<size_t>(s_pairs[c.offs[p.s] + t0 + t]) * 2 * a.I
+                                             : a.act_sh + static_cast<size_t>(t0 + t) * 2 * a.Is;
+                const uint4 gv = ld_cg_u4(row + c8);
+                const uint4 uv = ld_cg_u4(row + kd + c8);
+                const uint32_t gg[4] = {gv.x, gv.y, gv.z, gv.w}, uu[4] = {uv.x, uv.y, uv.z, uv.w};
+                uint32_t o[4];
+#pragma unroll
+                for (int e2 = 0; e2 < 4; ++e2) {
+                  const uint32_t sl0 = a.silu_lut[gg[e2] & 0xffffu], sl1 = a.silu_lut[gg[e2] >> 16];
+                  const uint32_t lo = f32_to_bf16(bf16_to_f32(sl0) * lo_bf16(uu[e2]));
+                  const uint32_t hi = f32_to_bf16(bf16_to_f32(sl1) * hi_bf16(uu[e2]));
+                  o[e2] = lo | (hi << 16);
+                }
+                *reinterpret_cast<uint4*>(my_act + static_cast<size_t>(t) * kd + c8) = make_uint4(o[0], o[1], o[2], o[3]);
+              }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int t = 0; t < kMaxTGP; ++t) {
+              const int tt = t < nt ? t : 0;  // padded tokens read token 0's row (results unused)
+              rows[t] = phase == 0 ? xs + static_cast<size_t>(tok_x[tt]) * a.H : my_act + static_cast<size_t>(tt) * kd;
+            }
+            cur_phase = phase;
+            cur_s = p.s;
+            cur_tg = p.tg;
+          }
+          bool good;
+          if (nt_pad == 1)
+            good = small_unit<1>(c, p, item, nt, rows, ring, full, empty, R, g, lane, s_abort, tok_row,
+                                 tok_scale);
+          else if (nt_pad == 2)
+            good = small_unit<2>(c, p, item, nt, rows, ring, full, empty, R, g, lane, s_abort, tok_row,
+                                 tok_scale);
+          else if (nt_pad == 4)
+            good = small_unit<4>(c, p, item, nt, rows, ring, full, empty, R, g, lane, s_abort, tok_row,
+                                 tok_scale);
+          else
+            good = small_unit<8>(c, p, item, nt, rows, ring, full, empty, R, g, lane, s_abort, tok_row,
+                                 tok_scale);
+          if (!good) {
+            aborted = true;
+            break;
+          }
+          if (phase == 0) {
+            // this unit's gate/up rows are stored: count it for the slot
+            // (published when the warp moves to another slot)
+            if (p.s != pend_s) {
+              flush_up(a.up_done, pend_s, pend_n, lane);
+              pend_s = p.s;
+              pend_n = 0;
+            }
+            ++pend_n;
+          }
+        }
+        if (aborted) break;
+        ok = next_pass(c, p);
+      }
+      if (phase == 0) {
+        // before any down unit can wait on these counts
+        flush_up(a.up_done, pend_s, pend_n, lane);
+        pend_s = -1;
+        pend_n = 0;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == kSmallWarps && lane == 0) {
+    // Copies still in flight (after an abort): let them land before the
+    // CTA's shared memory is released (bounded).  Stages below issued - R
+    // were consumed (their slots were reused); the last step's lanes that
+    // issued are in tail_mask.
+    for (int i = issued > R ? issued - R : 0; i < issued + kIssueLanes; ++i) {
+      if (i >= issued && !((tail_mask >> (i - issued)) & 1u)) continue;
+      if (!mbar_wait_bounded(&full[i % kSmallFull], (i / kSmallFull) & 1, kDrainNs)) break;
+    }
+  }
+}
+
 int g_num_sms = 0;
+int g_smem_optin = 0;
 
 }  // namespace
 
@@ -607,28 +1032,41 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
   }
-  const size_t smem = experts_smem_bytes(s, w.tiled);
-  auto kern = w.tiled ? k_experts<true> : k_experts<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, experts_tokens_per_pass(s), x, w.gate_up, w.down, w.sh_gate,
+  const int tgp = experts_tokens_per_pass(s);
+  ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, tgp, x, w.gate_up, w.down, w.sh_gate,
                 w.sh_up, w.sh_down, w.ep_world, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
                 sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err, sh_x, sh_T};
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(g_num_sms);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g_num_sms);
+  cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  const int R = w.tiled ? small_ring_slots(s, T, sh_T, sh_x != x, tgp, static_cast<size_t>(g_smem_optin)) : 0;
+  if (R > 0) {
+    const size_t smem = small_layout(s.H, s.I, s.Is, s.E, s.K, T, sh_T, sh_x != x, tgp, R).total;
+    cudaError_t e = cudaFuncSetAttribute(k_experts_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cfg.blockDim = dim3(kSmallThreads);
+    cfg.dynamicSmemBytes = smem;
+    return cudaLaunchKernelEx(&cfg, k_experts_small, a, R);
+  }
+  const size_t smem = experts_smem_bytes(s, w.tiled);
+  auto kern = w.tiled ? k_experts<true> : k_experts<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
