@@ -1051,9 +1051,12 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const int R = w.tiled ? small_ring_slots(s, T, sh_T, sh_x != x, tgp, static_cast<size_t>(g_smem_optin)) : 0;
+  // Small widths on one GPU.  Under expert parallelism (the shared expert's
+  // rows in their own buffer) the kernel above keeps the path: the small
+  // kernel's separate-rows case has not run on two GPUs.
+  const int R = w.tiled && sh_x == x ? small_ring_slots(s, T, sh_T, false, tgp, static_cast<size_t>(g_smem_optin)) : 0;
   if (R > 0) {
-    const size_t smem = small_layout(s.H, s.I, s.Is, s.E, s.K, T, sh_T, sh_x != x, tgp, R).total;
+    const size_t smem = small_layout(s.H, s.I, s.Is, s.E, s.K, T, sh_T, false, tgp, R).total;
     cudaError_t e = cudaFuncSetAttribute(k_experts_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
