@@ -621,19 +621,22 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
     }
   }
   if (a.sched == nullptr) return;
-  // The last CTA to finish builds the schedule from every token's selection.
+  // The last CTA to finish builds the schedule from every token's selection
+  // (a single-token launch is its own last CTA: no ticket).
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (gridDim.x > 1) {
+    if (threadIdx.x == 0) {
+      __threadfence();
+      flag[0] = (atomicAdd(a.ticket, 1) == a.T - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    const bool last = flag[0] != 0;
+    __syncthreads();  // every thread has read the flag before the schedule reuses smem
+    if (!last) return;
     __threadfence();
-    flag[0] = (atomicAdd(a.ticket, 1) == a.T - 1) ? 1 : 0;
   }
-  __syncthreads();
-  const bool last = flag[0] != 0;
-  __syncthreads();  // every thread has read the flag before the schedule reuses smem
-  if (!last) return;
-  __threadfence();
   build_schedule(a, smem);
-  if (threadIdx.x == 0) *a.ticket = 0;  // ready for the next forward
+  if (gridDim.x > 1 && threadIdx.x == 0) *a.ticket = 0;  // ready for the next forward
 }
 
 // Expert parallelism: the schedule of this GPU's experts over every rank's
