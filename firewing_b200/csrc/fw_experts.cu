@@ -1001,9 +1001,6 @@ __global__ void __launch_bounds__(kSmallThreads, 1) k_experts_small(const __grid
   }
 }
 
-int g_num_sms = 0;
-int g_smem_optin = 0;
-
 }  // namespace
 
 // Both layouts use the same tokens per pass (the route kernel's cost
@@ -1029,15 +1026,8 @@ size_t experts_smem_bytes(const Shape& s, bool tiled) {
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
                            const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st,
                            const uint16_t* sh_x, int sh_T) {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    e = cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (e != cudaSuccess) return e;
-    e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-  }
+  DeviceAttrs dev;
+  if (const cudaError_t e = current_device_attrs(&dev); e != cudaSuccess) return e;
   const int tgp = experts_tokens_per_pass(s);
   ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, tgp, x, w.gate_up, w.down, w.sh_gate,
                 w.sh_up, w.sh_down, w.ep_world, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
@@ -1048,14 +1038,14 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(g_num_sms);
+  cfg.gridDim = dim3(dev.sms);
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   // Small widths on one GPU.  Under expert parallelism (the shared expert's
   // rows in their own buffer) the kernel above keeps the path: the small
   // kernel's separate-rows case has not run on two GPUs.
-  const int R = w.tiled && sh_x == x ? small_ring_slots(s, T, sh_T, false, tgp, static_cast<size_t>(g_smem_optin)) : 0;
+  const int R = w.tiled && sh_x == x ? small_ring_slots(s, T, sh_T, false, tgp, static_cast<size_t>(dev.smem_optin)) : 0;
   if (R > 0) {
     const size_t smem = small_layout(s.H, s.I, s.Is, s.E, s.K, T, sh_T, false, tgp, R).total;
     cudaError_t e = cudaFuncSetAttribute(k_experts_small, cudaFuncAttributeMaxDynamicSharedMemorySize,

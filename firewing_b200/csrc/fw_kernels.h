@@ -305,6 +305,14 @@ const char* ep_exchange_rows(EpComm* c, const uint16_t* send, const int* rows_se
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.
 int record_error(int code, const char* msg);
+
+// Attributes of the calling thread's current device, read once per device
+// (a process may drive handles on several devices from several threads).
+struct DeviceAttrs {
+  int sms = 0;         // multiprocessors
+  int smem_optin = 0;  // opt-in shared memory per block, bytes
+};
+cudaError_t current_device_attrs(DeviceAttrs* out);
 // Where a handle lives: its device and, under expert parallelism, its rank
 // and world (rank 0 of 1 otherwise).
 struct HandlePlace {

@@ -1,6 +1,7 @@
 // fw_layout.cu -- the tiled expert layout: synthetic generation into it and
 // re-layout from the reference layout (see TiledSpec in fw_kernels.h).
 #include <cstdint>
+#include <mutex>
 
 #include "fw_common.cuh"
 #include "fw_kernels.h"
@@ -84,6 +85,28 @@ cudaError_t launch_relayout(const TiledSpec& spec, long long m0, long long n, co
   k_relayout<<<148 * 8, 256, 0, st>>>(spec, m0 * spec.mat_elems, n * spec.mat_elems, m0 * spec.src_mat_elems,
                                       src0, src1, out);
   return cudaGetLastError();
+}
+
+cudaError_t current_device_attrs(DeviceAttrs* out) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static DeviceAttrs cache[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceAttrs& a = cache[dev];
+  if (a.sms == 0) {
+    DeviceAttrs v;
+    if ((e = cudaDeviceGetAttribute(&v.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&v.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+      return e;
+    if (v.sms <= 0) return cudaErrorInvalidDevice;
+    a = v;
+  }
+  *out = a;
+  return cudaSuccess;
 }
 
 }  // namespace fw

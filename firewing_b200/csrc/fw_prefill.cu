@@ -1163,16 +1163,10 @@ bool token_maps(TokenMaps* m, const uint16_t* base, int cols, long long rows) {
   return true;
 }
 
+// SMs of the current device (148 on B200), read once per device.
 int sm_count() {
-  static std::once_flag once;
-  static int n = 148;
-  std::call_once(once, [] {
-    int dev = 0, v = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess &&
-        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
-      n = v;
-  });
-  return n;
+  DeviceAttrs a;
+  return current_device_attrs(&a) == cudaSuccess ? a.sms : 148;
 }
 
 }  // namespace

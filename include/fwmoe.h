@@ -280,7 +280,10 @@ typedef struct fw_moe_weights {
  * compiled into the library, which every GPU that loads the library holds
  * until exit.  Only the shape fields of `config` are read.  Shapes whose
  * scratch exceeds 8 MiB are rejected with FW_EINVAL (config 0, H=2048 with
- * K=10, fits up to T=128).  The first call on a device sets up that device
+ * K=10, fits up to T=121).  The weights stay in the reference layout, so
+ * this path always runs the generic decode expert kernel: at T <= 4 it is
+ * slower than fw_moe_forward, whose handle re-lays the banks out for the
+ * small-width kernel.  The first call on a device sets up that device
  * (looks up the array's device address, uploads the SiLU/sigmoid tables):
  * make it before any stream capture.  Calls share the scratch array, so
  * calls that overlap on the GPU race; each call is synchronous on `stream`.

@@ -63,12 +63,14 @@ class InputSpec(ctypes.Structure):
     ]
 
 
-def build() -> None:
-    """Compile the oracle (and the reference's top-k shim when the reference
-    tree is mounted) with oracle/Makefile."""
+def build(reference: Optional[str] = None) -> None:
+    """Compile the oracle with oracle/Makefile, and the reference's top-k
+    shim from its source when the firewing source tree is given (argument,
+    or the FIREWING_REFERENCE environment variable)."""
     subprocess.run(["make", "-s", "-C", _HERE, "all"], check=True)
-    if os.path.isdir("/root/reference/native"):
-        subprocess.run(["make", "-s", "-C", _HERE, "ref"], check=True)
+    ref = reference or os.environ.get("FIREWING_REFERENCE")
+    if ref and os.path.isfile(os.path.join(ref, "native", "topk_shim.cpp")):
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={os.path.abspath(ref)}"], check=True)
 
 
 _lib = None

@@ -1,8 +1,9 @@
-"""Expert parallelism on two GPUs through the C ABI: each rank holds half the
-experts (fw_moe_ep_init), brings its own tokens, and must return exactly the
-single-GPU decode result for them (the oracle's block output, bit for bit
-where scores match; the same selection everywhere).  Skipped with fewer than
-two GPUs.
+"""Expert parallelism on 2, 4 and 8 GPUs through the C ABI: each rank holds
+1/world of the experts (fw_moe_ep_init), brings its own tokens, and must
+return the single-GPU result for them: on the decode path the oracle's block
+output, bit for bit where scores match, and the same selection everywhere;
+on the prefill path the same selection and the block tolerance.  A case is
+skipped when fewer GPUs than its world are visible.
 """
 import os
 import tempfile
@@ -83,10 +84,9 @@ def _rank_main(rank, world, store, shape, t_local, layers, zipf, q, min_tokens=N
         dist.destroy_process_group()
 
 
-def _run(shape, t_local, layers, zipf, min_tokens=None):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+def _run(shape, t_local, layers, zipf, min_tokens=None, world=2):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     store = _rendezvous()
@@ -124,5 +124,19 @@ CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512,
                                                           (CFG4, 160, 1, True)])
 def test_ep_two_gpus_prefill(shape, t_local, min_tokens, zipf):
     for r in _run(shape, t_local, 1, zipf, min_tokens):
+        assert r["idx"] and r["score_ulp"] <= 1 and r["repeat"], r
+        assert r["max_abs"] <= 2e-2 and r["rel_l2"] <= 1e-3, r
+
+
+# Config 0's block at 2, 4 and 8 GPUs on both paths.
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_config0_decode(world):
+    for r in _run(CFG0, 16, 2, False, world=world):
+        assert r["idx"] and r["score_ulp"] <= 1 and r["exact_tokens_equal"] and r["repeat"], r
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_config0_prefill(world):
+    for r in _run(CFG0, 64, 1, True, min_tokens=1, world=world):
         assert r["idx"] and r["score_ulp"] <= 1 and r["repeat"], r
         assert r["max_abs"] <= 2e-2 and r["rel_l2"] <= 1e-3, r

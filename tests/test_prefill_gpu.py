@@ -10,6 +10,9 @@ bar is the block tolerance the target states: identical selected
 experts, scores within one bf16 ulp, output within max-abs 2e-2 and
 relative-L2 1e-3.
 """
+import os
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
 import pytest
 
@@ -120,3 +123,58 @@ def test_prefill_repeatable_and_nan_rejected():
     assert e.value.code == fw.FW_ENAN
     after = blk.forward(0, x)  # the handle stays usable
     assert all(np.array_equal(u, v) for u, v in zip(got, after))
+
+
+# ---- the benchmark widths: T = 8192 (config 2, and config 4's per-GPU width) ----
+#
+# Every token's selection is checked against the oracle's router; the block
+# output is checked on a subset of rows, since each token's output depends
+# on that token alone: tokens routed to the hottest expert (about 6,000 at
+# this width: two dozen 256-token chunks, the subset spread over all of
+# them), random tokens and the last token.
+
+def oracle_router_all(bshape, layer, x, chunk=256):
+    def one(t0):
+        return O.router(bshape, layer, x[t0:t0 + chunk])
+    with ThreadPoolExecutor(os.cpu_count() or 1) as ex:
+        parts = list(ex.map(one, range(0, x.shape[0], chunk)))
+    return (np.concatenate([p[0] for p in parts]), np.concatenate([p[1] for p in parts]),
+            np.concatenate([p[2] for p in parts]))
+
+
+def full_width(shape, seed, T):
+    cfg = fw.MoeConfig(**shape, max_tokens=T, layers=1)
+    blk = fw.MoeBlock(cfg)
+    blk.synth_layer(0, seed, 0.02, True)
+    x = O.synth_input(seed + 1000, T, shape["hidden"])
+    y, idx, sc = blk.forward(0, x)
+    blk.close()
+    bshape = O.BlockShape(**shape)
+    layer = O.SynthLayer(bshape, seed, 0.02, True)
+    ridx, rsc, logits = oracle_router_all(bshape, layer, x)
+    for t in np.nonzero(np.any(idx != ridx, axis=1))[0]:
+        assert O.equivalent_topk_order(ridx[t], idx[t], logits[t]), f"token {t}"
+    assert np.array_equal(idx, ridx)
+    assert int(np.abs(sc.astype(np.int32) - rsc.astype(np.int32)).max()) <= 1
+    counts = np.bincount(idx.ravel(), minlength=shape["experts"])
+    hot = int(np.argmax(counts))
+    assert counts[hot] > 16 * 256, "the Zipf router gives the hottest expert many token chunks"
+    rng = np.random.default_rng(seed)
+    hot_rows = np.nonzero(np.any(idx == hot, axis=1))[0]
+    rows = np.unique(np.concatenate([rng.choice(hot_rows, 96, replace=False), rng.choice(T, 64, replace=False),
+                                     [T - 1]]))
+    layer.ensure(ridx[rows])
+    ry, ri, rs = O.block_resident(bshape, layer, np.ascontiguousarray(x[rows]), threads=os.cpu_count() or 1)
+    assert np.array_equal(ri, idx[rows])
+    max_abs, rel = errors(y[rows], ry)
+    print(f"T={T} hottest expert {hot}: {counts[hot]} tokens; rows checked {rows.size}: "
+          f"max_abs={max_abs:.3e} rel_l2={rel:.3e}")
+    assert max_abs <= MAX_ABS and rel <= REL_L2, (max_abs, rel)
+
+
+def test_prefill_config2_full_width():
+    full_width(CFG0, 1, 8192)
+
+
+def test_prefill_config4_full_width():
+    full_width(CFG4, 2, 8192)

@@ -62,8 +62,14 @@ def close(y: np.ndarray, r: np.ndarray) -> bool:
     return max_abs <= MAX_ABS and rel <= REL_L2
 
 
-@pytest.mark.parametrize("shape_i,zipf", [(0, False), (1, False), (1, True)])
-def test_noalloc_matches_handle_forward_twice(shape_i, zipf):
+# Token counts of the two calls.  At T <= 4 the handle path takes other
+# kernels than at wider T (for hidden a multiple of 256: the partial-major
+# router at T = 1, the small-width expert kernel on its re-laid-out banks),
+# while this entry point always runs the generic router and expert kernel on
+# reference-layout weights; both must still agree bit for bit.
+@pytest.mark.parametrize("shape_i,zipf,tokens", [(0, False, (32, 7)), (1, False, (32, 7)), (1, True, (32, 7)),
+                                                 (1, False, (1, 3)), (1, True, (3, 1))])
+def test_noalloc_matches_handle_forward_twice(shape_i, zipf, tokens):
     shape = SHAPES[shape_i]
     H, K = shape["hidden"], shape["top_k"]
     cfg = fw.MoeConfig(**shape, max_tokens=32, layers=1)
@@ -72,7 +78,7 @@ def test_noalloc_matches_handle_forward_twice(shape_i, zipf):
     blk.load_layer(0, w["router"], w["gate_up"], w["down"], w["shared_gate"], w["shared_up"],
                    w["shared_down"], w["shared_gate_w"], w.get("logit_bias"))
     stream = torch.cuda.current_stream()
-    for call, T in enumerate((32, 7)):
+    for call, T in enumerate(tokens):
         x = dev(O.synth_input(500 + call, T, H))
         y_ref = torch.empty((T, H), dtype=torch.int16, device="cuda")
         i_ref = torch.empty((T, K), dtype=torch.int32, device="cuda")
@@ -118,6 +124,30 @@ def test_noalloc_rejects_scratch_beyond_the_static_area():
         fw.forward_noalloc(cfg, w, dummy, 256, dummy)
     assert e.value.code == fw.FW_EINVAL
     assert "scratch" in e.value.message
+
+
+def test_noalloc_scratch_limit_at_config0():
+    # Config 0 (H=2048, I=Is=512, E=512, K=10): T=121 fits the 8 MiB area,
+    # T=122 does not.  Zero weights are enough to run the forward.
+    shape = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512, top_k=10)
+    H, I, E = shape["hidden"], shape["intermediate"], shape["experts"]
+    cfg = fw.MoeConfig(**shape, max_tokens=122, layers=1)
+    z = lambda n: torch.zeros(n, dtype=torch.int16, device="cuda")  # noqa: E731
+    w = {"router": z(E * H), "gate_up": z(E * 2 * I * H), "down": z(E * H * I), "shared_gate": z(I * H),
+         "shared_up": z(I * H), "shared_down": z(H * I), "shared_gate_w": z(H)}
+    x = dev(O.synth_input(77, 122, H))
+    y = torch.empty((122, H), dtype=torch.int16, device="cuda")
+    idx = torch.empty((122, shape["top_k"]), dtype=torch.int32, device="cuda")
+    fw.forward_noalloc(cfg, w, x, 121, y, idx)
+    torch.cuda.synchronize()
+    # all logits equal: the tie rule selects experts 0..K-1 in index order
+    assert np.array_equal(idx[:121].cpu().numpy(), np.tile(np.arange(10, dtype=np.int32), (121, 1)))
+    with pytest.raises(fw.FwError) as e:
+        fw.forward_noalloc(cfg, w, x, 122, y, idx)
+    assert e.value.code == fw.FW_EINVAL
+    assert "scratch" in e.value.message
+    del w
+    torch.cuda.empty_cache()
 
 
 def test_noalloc_reports_nan_logits():
