@@ -797,7 +797,7 @@ def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, bar
         "parallelism": f"ep{world} (experts {E // world} per GPU) + dp tokens",
         "stage_ms_per_layer_by_rank": stages,
         "parity_sample": parity,
-        "exchange": "NCCL all-gather (rows, ids, weights) + grouped send/recv of weighted rows",
+        "exchange": "NVLink peer memory: rows pulled once per destination GPU, weighted rows stored by the expert kernel into the owner's window, bounded flag waits",
     }
 
 

@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build")
-SOURCES = ["fw_api.cu", "fw_decode.cu", "fw_experts.cu", "fw_layout.cu", "fw_noalloc.cu", "fw_prefill.cu", "fw_ep.cu", "fw_hc.cu", "fw_checkpoint.cu", "fw_codec.cu"]
+SOURCES = ["fw_api.cu", "fw_decode.cu", "fw_experts.cu", "fw_layout.cu", "fw_noalloc.cu", "fw_prefill.cu", "fw_ep.cu", "fw_p2p.cu", "fw_hc.cu", "fw_checkpoint.cu", "fw_codec.cu"]
 HEADERS = ["fw_common.cuh", "fw_kernels.h", "fw_json.h"]
 SO = os.path.join(HERE, "libfwmoe.so")
 LIB = os.path.join(HERE, "libfwmoe.a")

@@ -119,6 +119,7 @@ int map_device_error(int code) {
     case fw::kErrTimeout: return fail(FW_ETIMEOUT, "a bounded device wait timed out");
     case fw::kErrBadIndex: return fail(FW_EINVAL, "expert index out of range on device");
     case fw::kErrCapacity: return fail(FW_EINVAL, "token/expert pairs exceeded scratch capacity");
+    case fw::kErrPeer: return fail(FW_ENCCL, "an expert-parallel peer reported a failure in this forward");
     default: return fail(FW_ECUDA, "unknown device status " + std::to_string(code));
   }
 }
@@ -199,6 +200,11 @@ struct fw_moe {
   int* ep_counts = nullptr;          // device [4][world]: send rows, send offsets, recv rows, recv offsets
   int* ep_counts_host = nullptr;     // pinned copy
   cudaEvent_t ep_counts_ev = nullptr;
+  // Expert parallelism over NVLink peer memory (the default transport).
+  int ep_transport = FW_EP_TRANSPORT_P2P;
+  fw::P2pComm* p2p = nullptr;
+  unsigned ep_seq = 0;               // forwards issued under expert parallelism (same on every rank)
+  int stall_next = 0;                // fw_moe_test_stall: the next forward's expert kernel stalls
   // hyper-connection caller (allocated by the first fw_moe_load_hc)
   fw::HcScratch hs{};
   int hs_lowrank = 0;                // LR the scratch holds
@@ -297,58 +303,75 @@ int free_layer(OwnedLayer& L) {
 
 namespace {
 
-// One layer under expert parallelism, stream-ordered (see fw_ep.cu): local
-// router and route, dispatch (all-gather), this rank's experts over every
-// rank's tokens plus the shared expert over its own, combine exchange, then
-// the ascending-id sum of its own tokens' rows.
-int ep_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
-               uint16_t* score, cudaStream_t cs, cudaEvent_t* ev) {
+// Stage events of a forward (kStages + 1 of them), or null.
+struct Marks {
+  cudaEvent_t* ev;
+  cudaStream_t st;
+  cudaError_t operator()(int i) const { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; }
+};
+
+// The expert kernel's stall count for this forward (fw_moe_test_stall).
+int take_stall(fw_moe* h) {
+  const int v = h->stall_next;
+  h->stall_next = 0;
+  return v;
+}
+
+// One layer under expert parallelism over NCCL, stream-ordered (see
+// fw_ep.cu): local router and route, dispatch (all-gather), this rank's
+// experts over every rank's tokens plus the shared expert over its own,
+// combine exchange, then the ascending-id sum of its own tokens' rows.
+int ep_forward_nccl(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
+                    uint16_t* score, cudaStream_t cs, cudaEvent_t* ev, const fw::HcPost* hc) {
   const fw::Shape& s = h->shape;
   const int N = h->ep_world, T = N * T_l;
   cudaError_t e = cudaSuccess;
-  auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], cs) : cudaSuccess; };
+  const Marks mark{ev, cs};
   auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
   if ((e = mark(0)) != cudaSuccess) return cuda_failed("event");
   if ((e = fw::launch_router(s, L.w, h->sc, x, T_l, cs)) != cudaSuccess) return cuda_failed("router launch");
   if ((e = mark(1)) != cudaSuccess) return cuda_failed("event");
   if ((e = fw::launch_route_block(s, h->luts, h->sc, T_l, idx, score, false, nullptr, cs)) != cudaSuccess)
     return cuda_failed("route launch");
+  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
   const char* m = fw::ep_dispatch(h->ep, x, h->ep_x_all, static_cast<size_t>(T_l) * s.H, idx, h->ep_idx_all,
                                   score, h->ep_score_all, static_cast<size_t>(T_l) * s.K, cs);
   if (m != nullptr) return fail(FW_ENCCL, m);
   if ((e = fw::launch_ep_schedule(s, h->sc, h->ep_idx_all, T, h->ep_rank, N, T_l, cs)) != cudaSuccess)
     return cuda_failed("schedule launch");
-  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
-  if ((e = fw::launch_experts(s, L.w, h->luts, h->sc, h->ep_x_all, T, h->ep_score_all, cs, x, T_l)) !=
-      cudaSuccess)
-    return cuda_failed("expert kernel launch");
   if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
+  fw::Scratch sc = h->sc;
+  sc.stall = take_stall(h);
+  if ((e = fw::launch_experts(s, L.w, h->luts, sc, h->ep_x_all, T, h->ep_score_all, cs, x, T_l)) != cudaSuccess)
+    return cuda_failed("expert kernel launch");
+  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
   m = fw::ep_combine_exchange(h->ep, h->sc.weighted, h->ep_recv, static_cast<size_t>(T_l) * s.K * s.H, cs);
   if (m != nullptr) return fail(FW_ENCCL, m);
-  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, idx, N, h->ep_recv)) != cudaSuccess)
+  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, idx, N, h->ep_recv, nullptr, hc)) != cudaSuccess)
     return cuda_failed("combine launch");
-  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
+  if ((e = mark(5)) != cudaSuccess) return cuda_failed("event");
   return FW_OK;
 }
 
-// One layer of the prefill path under expert parallelism: local router and
-// route, dispatch (all-gather), this rank's experts grouped over every rank's
-// pairs and run as the tensor-core GEMMs (plus the shared expert over its own
-// tokens), the weighted rows packed per destination in (token, k) order,
-// a row-sized exchange (counts read on the host while the GEMMs run), then
-// the owner's ascending-id sum.
-int ep_prefill_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
-                       uint16_t* score, cudaStream_t cs, cudaEvent_t* ev) {
+// One layer of the prefill path under expert parallelism over NCCL: local
+// router and route, dispatch (all-gather), this rank's experts grouped over
+// every rank's pairs and run as the tensor-core GEMMs (plus the shared
+// expert over its own tokens), the weighted rows packed per destination in
+// (token, k) order, a row-sized exchange (counts read on the host while the
+// GEMMs run), then the owner's ascending-id sum.
+int ep_prefill_forward_nccl(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
+                            uint16_t* score, cudaStream_t cs, cudaEvent_t* ev, const fw::HcPost* hc) {
   const fw::Shape& s = h->shape;
   const int N = h->ep_world, T = N * T_l;
   const int count = held_experts(h);
   cudaError_t e = cudaSuccess;
-  auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], cs) : cudaSuccess; };
+  const Marks mark{ev, cs};
   auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
   if ((e = mark(0)) != cudaSuccess) return cuda_failed("event");
-  if ((e = fw::launch_prefill_front(s, L.w, L.maps, h->luts, h->sc, x, T_l, idx, score, false, cs)) != cudaSuccess)
+  if ((e = fw::launch_prefill_front(s, L.w, L.maps, h->luts, h->sc, x, T_l, idx, score, false, cs,
+                                    ev != nullptr ? ev[1] : nullptr)) != cudaSuccess)
     return cuda_failed("router / route launch");
-  if ((e = mark(1)) != cudaSuccess) return cuda_failed("event");
+  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
   const char* m = fw::ep_dispatch(h->ep, x, h->ep_x_all, static_cast<size_t>(T_l) * s.H, idx, h->ep_idx_all,
                                   score, h->ep_score_all, static_cast<size_t>(T_l) * s.K, cs);
   if (m != nullptr) return fail(FW_ENCCL, m);
@@ -365,21 +388,113 @@ int ep_prefill_forward(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_
   if ((e = cudaMemcpyAsync(h->ep_counts_host, cnt, 4 * N * sizeof(int), cudaMemcpyDeviceToHost, cs)) != cudaSuccess ||
       (e = cudaEventRecord(h->ep_counts_ev, cs)) != cudaSuccess)
     return cuda_failed("exchange counts");
-  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
+  if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
   if ((e = fw::launch_prefill_gemms(s, L.maps, h->pf_maps, h->luts, h->sc, x, T_l, count, h->ep_score_all,
                                     h->ep_send_pos, h->sc.weighted, cs)) != cudaSuccess)
     return cuda_failed("GEMM launch");
-  if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
+  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
   // The GEMMs keep running while the host reads the exchange sizes.
   if ((e = cudaEventSynchronize(h->ep_counts_ev)) != cudaSuccess) return cuda_failed("exchange counts");
-  const int* hc = h->ep_counts_host;
-  m = fw::ep_exchange_rows(h->ep, h->sc.weighted, hc, hc + N, h->ep_recv, hc + 2 * N, hc + 3 * N,
+  const int* hc_ = h->ep_counts_host;
+  m = fw::ep_exchange_rows(h->ep, h->sc.weighted, hc_, hc_ + N, h->ep_recv, hc_ + 2 * N, hc_ + 3 * N,
                            static_cast<size_t>(s.H), cs);
   if (m != nullptr) return fail(FW_ENCCL, m);
-  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, nullptr, 0, h->ep_recv, h->ep_recv_pos)) != cudaSuccess)
+  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, nullptr, 0, h->ep_recv, h->ep_recv_pos, hc)) != cudaSuccess)
     return cuda_failed("combine launch");
-  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
+  if ((e = mark(5)) != cudaSuccess) return cuda_failed("event");
   return FW_OK;
+}
+
+// One layer under expert parallelism over NVLink peer memory (fw_p2p.cu),
+// decode widths: router and route of this rank's tokens; publish them in
+// its window; pull every rank's selections and the token rows this rank's
+// experts need (bounded wait on the peers' pub flags); schedule; the
+// decode expert kernel, whose epilogue stores each weighted row in its
+// owner's window and whose last CTA sets this rank's done flags; the
+// combine (bounded wait on every done flag) over this rank's window.
+int ep_forward_p2p(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
+                   uint16_t* score, cudaStream_t cs, cudaEvent_t* ev, const fw::HcPost* hc) {
+  const fw::Shape& s = h->shape;
+  const int N = h->ep_world, T = N * T_l;
+  const fw::EpPeers P = fw::p2p_peers(h->p2p, T_l, ++h->ep_seq, h->sc.wait_ns);
+  cudaError_t e = cudaSuccess;
+  const Marks mark{ev, cs};
+  auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
+  if ((e = mark(0)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_router(s, L.w, h->sc, x, T_l, cs)) != cudaSuccess) return cuda_failed("router launch");
+  if ((e = mark(1)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_route_block(s, h->luts, h->sc, T_l, idx, score, false, nullptr, cs)) != cudaSuccess ||
+      (e = fw::launch_ep_publish(P, x, idx, score, h->sc.err, cs)) != cudaSuccess)
+    return cuda_failed("route / publish launch");
+  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_ep_pull(P, s.E, h->ep_idx_all, h->ep_score_all, h->ep_x_all, h->sc.err, cs)) != cudaSuccess ||
+      (e = fw::launch_ep_schedule(s, h->sc, h->ep_idx_all, T, h->ep_rank, N, T_l, cs)) != cudaSuccess)
+    return cuda_failed("dispatch launch");
+  if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
+  fw::Scratch sc = h->sc;
+  sc.stall = take_stall(h);
+  if ((e = fw::launch_experts(s, L.w, h->luts, sc, h->ep_x_all, T, h->ep_score_all, cs, x, T_l, &P)) != cudaSuccess)
+    return cuda_failed("expert kernel launch");
+  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, nullptr, 0, fw::p2p_recv(h->p2p), nullptr, hc, &P)) !=
+      cudaSuccess)
+    return cuda_failed("combine launch");
+  if ((e = mark(5)) != cudaSuccess) return cuda_failed("event");
+  return FW_OK;
+}
+
+// The same over peer memory at prefill widths: router and route, publish;
+// every rank's selections and this rank's pair counts (bounded wait on the
+// pub flags); pair offsets; the grouped input, each needed token row read
+// once from its owner's window; the tensor-core GEMMs, whose down epilogue
+// stores each weighted row in its owner's window (the transfer overlaps the
+// GEMM) and whose last CTA sets the done flags; the combine.  No host
+// synchronisation.
+int ep_prefill_forward_p2p(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx,
+                           uint16_t* score, cudaStream_t cs, cudaEvent_t* ev, const fw::HcPost* hc) {
+  const fw::Shape& s = h->shape;
+  const int count = held_experts(h);
+  const fw::EpPeers P = fw::p2p_peers(h->p2p, T_l, ++h->ep_seq, h->sc.wait_ns);
+  cudaError_t e = cudaSuccess;
+  const Marks mark{ev, cs};
+  auto cuda_failed = [&](const char* what) { return fail(FW_ECUDA, what, cudaGetErrorString(e)); };
+  if ((e = mark(0)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_prefill_front(s, L.w, L.maps, h->luts, h->sc, x, T_l, idx, score, false, cs,
+                                    ev != nullptr ? ev[1] : nullptr)) != cudaSuccess ||
+      (e = fw::launch_ep_publish(P, x, idx, score, h->sc.err, cs)) != cudaSuccess)
+    return cuda_failed("router / route / publish launch");
+  if ((e = mark(2)) != cudaSuccess) return cuda_failed("event");
+  if ((e = cudaMemsetAsync(h->sc.pair_count, 0, sizeof(int) * count, cs)) != cudaSuccess ||
+      (e = fw::launch_ep_ids(P, s.E, h->ep_idx_all, h->ep_score_all, h->sc.pair_count, h->sc.err, cs)) !=
+          cudaSuccess ||
+      (e = fw::launch_prefill_offsets(s, h->sc, count, T_l, cs)) != cudaSuccess ||
+      (e = fw::launch_ep_scatter(P, h->ep_idx_all, h->sc.pair_offset, h->sc.pair_fill, h->sc.pair_tk, h->sc.xg,
+                                 h->sc.pair_cap, h->sc.err, cs)) != cudaSuccess)
+    return cuda_failed("dispatch launch");
+  if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_prefill_gemms(s, L.maps, h->pf_maps, h->luts, h->sc, x, T_l, count, h->ep_score_all, nullptr,
+                                    h->sc.weighted, cs, &P)) != cudaSuccess)
+    return cuda_failed("GEMM launch");
+  if ((e = mark(4)) != cudaSuccess) return cuda_failed("event");
+  if ((e = fw::launch_combine(s, h->sc, T_l, y, cs, nullptr, 0, fw::p2p_recv(h->p2p), nullptr, hc, &P)) !=
+      cudaSuccess)
+    return cuda_failed("combine launch");
+  if ((e = mark(5)) != cudaSuccess) return cuda_failed("event");
+  return FW_OK;
+}
+
+// Whole block under expert parallelism (either transport, either path).
+int ep_block(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx, uint16_t* score,
+             cudaStream_t cs, cudaEvent_t* ev, const fw::HcPost* hc, bool* prefill) {
+  *prefill = T_l > h->ep_decode_max || T_l >= h->prefill_min_tokens;
+  if (*prefill && !L.prefill) return fail(FW_EINVAL, "this many tokens need the prefill path, which this handle's shape lacks");
+  if (h->p2p != nullptr)
+    return *prefill ? ep_prefill_forward_p2p(h, L, x, T_l, y, idx, score, cs, ev, hc)
+                    : ep_forward_p2p(h, L, x, T_l, y, idx, score, cs, ev, hc);
+  if (*prefill && h->ep_send_pos == nullptr)
+    return fail(FW_EINVAL, "this many tokens need the prefill path, which this handle's shape lacks");
+  return *prefill ? ep_prefill_forward_nccl(h, L, x, T_l, y, idx, score, cs, ev, hc)
+                  : ep_forward_nccl(h, L, x, T_l, y, idx, score, cs, ev, hc);
 }
 
 // Replace a scratch buffer owned by the handle with one of `count` elements.
@@ -406,15 +521,25 @@ int fw_ep_unique_id(uint8_t id[128]) {
   return m == nullptr ? FW_OK : fail(FW_ENCCL, m);
 }
 
+int fw_moe_ep_set_transport(fw_moe* h, int32_t transport) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  if (transport != FW_EP_TRANSPORT_P2P && transport != FW_EP_TRANSPORT_NCCL)
+    return fail(FW_EINVAL, "unknown expert-parallel transport");
+  if (h->ep != nullptr || h->p2p != nullptr) return fail(FW_EINVAL, "expert parallelism is already initialised");
+  h->ep_transport = transport;
+  return FW_OK;
+}
+
 int fw_moe_ep_init(fw_moe* h, int32_t rank, int32_t world, const uint8_t id[128]) {
   if (h == nullptr || id == nullptr) return fail(FW_EINVAL, "handle / id is null");
-  if (h->ep != nullptr) return fail(FW_EINVAL, "expert parallelism is already initialised");
+  if (h->ep != nullptr || h->p2p != nullptr) return fail(FW_EINVAL, "expert parallelism is already initialised");
   if (world < 2 || world > 8 || rank < 0 || rank >= world)
     return fail(FW_EINVAL, "need 2 <= world <= 8 and 0 <= rank < world");
   if (h->cfg.experts % world != 0) return fail(FW_EINVAL, "experts must divide evenly over the ranks");
   for (const auto& L : h->layers)
     if (L.loaded) return fail(FW_EINVAL, "initialise expert parallelism before loading layers");
   FW_CUDA(cudaSetDevice(h->device));
+  const bool p2p = h->ep_transport == FW_EP_TRANSPORT_P2P;
   const size_t M = h->cfg.max_tokens, W = static_cast<size_t>(world);
   // Decode width under expert parallelism: the schedule spans every rank's
   // tokens and is built by one CTA (at most 1024 tokens in total).
@@ -424,36 +549,64 @@ int fw_moe_ep_init(fw_moe* h, int32_t rank, int32_t world, const uint8_t id[128]
   const bool prefill = h->prefill_ok;
   const size_t K = h->cfg.top_k, H = h->cfg.hidden, I = h->cfg.intermediate, E = h->cfg.experts;
   fw::Scratch& s = h->sc;
-  // Schedule, activations and the outgoing weighted rows cover every rank's
-  // tokens; the rest of the scratch stays per rank.
+  // Schedule and activations cover every rank's tokens; the rest of the
+  // scratch stays per rank.  Over NCCL the outgoing weighted rows do too;
+  // over peer memory they go straight to their owners' windows.
   const size_t Gd = W * Md, Gp = prefill ? W * M : 0;
   FW_TRY(regrow(h, &s.sched, fw::sched_words(static_cast<int>(E), static_cast<int>(Gd), static_cast<int>(K))));
   FW_TRY(regrow(h, &s.act, std::max(Gd * K * 2 * I, Gp * K * I)));
-  FW_TRY(regrow(h, &s.weighted, std::max(Gd * K * H, Gp * K * H)));
-  FW_TRY(alloc(h, &h->ep_x_all, W * M * H, h->scratch_owned));
+  if (!p2p) FW_TRY(regrow(h, &s.weighted, std::max(Gd * K * H, Gp * K * H)));
+  // Gathered rows: decode widths only over peer memory (prefill rows go
+  // straight from the owners' windows into the grouped input).
+  FW_TRY(alloc(h, &h->ep_x_all, (p2p ? Gd : W * M) * H, h->scratch_owned));
   FW_TRY(alloc(h, &h->ep_idx_all, W * M * K, h->scratch_owned));
   FW_TRY(alloc(h, &h->ep_score_all, W * M * K, h->scratch_owned));
-  FW_TRY(alloc(h, &h->ep_recv, std::max(Gd * K * H, prefill ? M * K * H : 0), h->scratch_owned));
+  if (!p2p) FW_TRY(alloc(h, &h->ep_recv, std::max(Gd * K * H, prefill ? M * K * H : 0), h->scratch_owned));
   if (prefill) {
     FW_TRY(regrow(h, &s.pair_tk, Gp * K));
     FW_TRY(regrow(h, &s.xg, Gp * K * H));
     s.pair_cap = static_cast<long long>(Gp * K);
-    FW_TRY(alloc(h, &h->ep_send_pos, Gp * K, h->scratch_owned));
-    FW_TRY(alloc(h, &h->ep_recv_pos, M * K, h->scratch_owned));
-    FW_TRY(alloc(h, &h->ep_counts, 4 * W, h->scratch_owned));
-    FW_CUDA(cudaMallocHost(&h->ep_counts_host, 4 * W * sizeof(int)));
-    FW_CUDA(cudaEventCreateWithFlags(&h->ep_counts_ev, cudaEventDisableTiming));
+    if (!p2p) {
+      FW_TRY(alloc(h, &h->ep_send_pos, Gp * K, h->scratch_owned));
+      FW_TRY(alloc(h, &h->ep_recv_pos, M * K, h->scratch_owned));
+      FW_TRY(alloc(h, &h->ep_counts, 4 * W, h->scratch_owned));
+      FW_CUDA(cudaMallocHost(&h->ep_counts_host, 4 * W * sizeof(int)));
+      FW_CUDA(cudaEventCreateWithFlags(&h->ep_counts_ev, cudaEventDisableTiming));
+    }
   }
   // act / xg moved: re-encode the scratch tensor maps
   if (h->prefill_ok && !fw::make_prefill_scratch_maps(h->shape, s, &h->pf_maps))
     return fail(FW_ECUDA, "prefill tensor maps could not be encoded");
-  fw::EpComm* c = nullptr;
-  const char* m = fw::ep_comm_init(rank, world, id, &c);
-  if (m != nullptr) return fail(FW_ENCCL, m);
-  h->ep = c;
+  if (p2p) {
+    fw::P2pComm* c = nullptr;
+    const char* m = fw::p2p_init(h->device, rank, world, id, static_cast<int>(M), static_cast<int>(H),
+                                 static_cast<int>(K), &c);
+    if (m != nullptr) return fail(FW_ENCCL, m);
+    h->p2p = c;
+    h->bytes += fw::p2p_window_bytes(c);
+  } else {
+    fw::EpComm* c = nullptr;
+    const char* m = fw::ep_comm_init(rank, world, id, &c);
+    if (m != nullptr) return fail(FW_ENCCL, m);
+    h->ep = c;
+  }
   h->ep_rank = rank;
   h->ep_world = world;
   h->ep_decode_max = static_cast<int>(Md);
+  return FW_OK;
+}
+
+int fw_moe_set_wait_limit(fw_moe* h, uint64_t nanoseconds) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  if (nanoseconds < 1000000ull || nanoseconds > 60000000000ull)
+    return fail(FW_EINVAL, "the wait limit must be between 1 ms and 60 s");
+  h->sc.wait_ns = nanoseconds;
+  return FW_OK;
+}
+
+int fw_moe_test_stall(fw_moe* h) {
+  if (h == nullptr) return fail(FW_EINVAL, "handle is null");
+  h->stall_next = 1 << 30;
   return FW_OK;
 }
 
@@ -552,6 +705,7 @@ int fw_moe_destroy(fw_moe* h) {
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
   fw::ep_comm_destroy(h->ep);
+  fw::p2p_destroy(h->p2p);
   if (h->ep_counts_host) cudaFreeHost(h->ep_counts_host);
   if (h->ep_counts_ev) cudaEventDestroy(h->ep_counts_ev);
   for (auto& L : h->layers) {
@@ -843,20 +997,19 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   uint16_t* sc = topk_scores ? topk_scores : h->score_dev;
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
   cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
-  if (h->ep != nullptr) {
-    const bool ep_prefill = tokens > h->ep_decode_max || tokens >= h->prefill_min_tokens;
-    if (ep_prefill && (!L.prefill || h->ep_send_pos == nullptr))
-      return fail(FW_EINVAL, "this many tokens need the prefill path, which this handle's shape lacks");
-    const int rc = ep_prefill ? ep_prefill_forward(h, L, x, tokens, y, idx, sc, cs, ev)
-                              : ep_forward(h, L, x, tokens, y, idx, sc, cs, ev);
+  if (h->ep != nullptr || h->p2p != nullptr) {
+    bool ep_prefill = false;
+    const int rc = ep_block(h, L, x, tokens, y, idx, sc, cs, ev, nullptr, &ep_prefill);
     if (rc == FW_OK) note_forward(h, ep_prefill, cs);
     return rc;
   }
   const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
   if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
+  fw::Scratch scr = h->sc;
+  scr.stall = take_stall(h);
   const cudaError_t e =
-      prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev)
-              : fw::launch_block(h->shape, L.w, h->luts, h->sc, x, tokens, y, idx, sc, cs, ev);
+      prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, scr, x, tokens, y, idx, sc, cs, ev)
+              : fw::launch_block(h->shape, L.w, h->luts, scr, x, tokens, y, idx, sc, cs, ev);
   if (e != cudaSuccess) return fail(FW_ECUDA, std::string("launch: ") + cudaGetErrorString(e));
   note_forward(h, prefill, cs);
   return FW_OK;
@@ -982,7 +1135,6 @@ int fw_moe_forward_hc_async(fw_moe* h, int32_t layer, const uint16_t* post, int3
   FW_TRY(check_handle(h, layer));
   const OwnedLayer& L = h->layers[layer];
   if (L.hc.lowrank == 0) return fail(FW_EINVAL, "layer has no hyper-connection weights (fw_moe_load_hc)");
-  if (h->ep != nullptr) return fail(FW_EINVAL, "the hyper-connection forward is single-GPU");
   if (tokens < 0 || tokens > h->cfg.max_tokens) return fail(FW_EINVAL, "tokens out of range");
   if (tokens == 0) return FW_OK;
   if (post == nullptr || out == nullptr) return fail(FW_EINVAL, "post / out is null");
@@ -996,9 +1148,17 @@ int fw_moe_forward_hc_async(fw_moe* h, int32_t layer, const uint16_t* post, int3
   int32_t* idx = topk_idx ? topk_idx : h->idx_dev;
   uint16_t* sc = topk_scores ? topk_scores : h->score_dev;
   const fw::HcPost hp{post, h->hs.inj_w, out};
+  cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
+  if (h->ep != nullptr || h->p2p != nullptr) {
+    // The hyper-connection stages are per token (this rank's); the block in
+    // between is expert-parallel and its combine applies the injection.
+    bool ep_prefill = false;
+    const int rc = ep_block(h, L, h->hs.mixed, tokens, h->hc_moe, idx, sc, cs, ev, &hp, &ep_prefill);
+    if (rc == FW_OK) note_forward(h, ep_prefill, cs);
+    return rc;
+  }
   const bool prefill = tokens > kDecodeMaxTokens || tokens >= h->prefill_min_tokens;
   if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
-  cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
   e = prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, h->sc, h->hs.mixed, tokens, h->hc_moe,
                                    idx, sc, cs, ev, &hp)
               : fw::launch_block(h->shape, L.w, h->luts, h->sc, h->hs.mixed, tokens, h->hc_moe, idx, sc, cs, ev,

@@ -262,3 +262,86 @@ __device__ __forceinline__ void fma8_bf16(const uint4 w, const uint4 x, float* a
 }
 
 }  // namespace fw
+
+namespace fw {
+
+// ---- expert parallelism over NVLink peer memory (see EpPeers) -------------------
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_volatile_int(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// Flag `kind` that rank `writer` sets in rank `owner`'s window.
+__device__ __forceinline__ unsigned* ep_flag(const EpPeers& p, int owner, int kind, int writer) {
+  return reinterpret_cast<unsigned*>(p.win[owner] + kind * 128) + writer;
+}
+
+// Where the weighted row of pair g*K + k goes: row t*K + k of the receive
+// area of the rank that owns token g (rank g / t_local, its token t), in
+// that rank's window.
+__device__ __forceinline__ uint16_t* ep_recv_row(const EpPeers& p, long long pair) {
+  const long long g = pair / p.K;
+  const long long k = pair - g * p.K;
+  const int owner = static_cast<int>(g / p.t_local);
+  const long long t = g - static_cast<long long>(owner) * p.t_local;
+  return reinterpret_cast<uint16_t*>(p.win[owner] + p.off_recv) + (t * p.K + k) * p.H;
+}
+
+// Called by one thread: wait (bounded by p.wait_ns) until every rank has set
+// its flag `kind` in this rank's window for forward p.seq.  Returns false
+// after recording kErrTimeout (a rank never set it), kErrPeer (a rank
+// reported a failure in this forward), or when this rank's status word
+// already holds an error (its forward failed earlier; nothing more waits).
+__device__ __forceinline__ bool ep_wait_flags(const EpPeers& p, int kind, int* err) {
+  const unsigned* f = reinterpret_cast<const unsigned*>(p.win[p.rank] + kind * 128);
+  uint64_t t0 = 0;
+  bool timing = false;
+  for (int w = 0; w < p.world; ++w) {
+    unsigned v;
+    while (((v = ld_acquire_sys_u32(f + w)) >> 1) < p.seq) {
+      if (ld_volatile_int(err) != 0) return false;
+      if (!timing) {
+        t0 = global_ns();
+        timing = true;
+      } else if (global_ns() - t0 > p.wait_ns) {
+        set_error(err, kErrTimeout);
+        return false;
+      }
+      __nanosleep(100);
+    }
+    if ((v >> 1) == p.seq && (v & 1u) != 0) {
+      set_error(err, kErrPeer);
+      return false;
+    }
+  }
+  return ld_volatile_int(err) == 0;
+}
+
+// Called by every thread of every CTA at the very end of a kernel whose
+// writes other ranks will read (rows in their windows, or this rank's
+// window they read from): the last CTA to finish sets flag `kind` to
+// 2*seq (+1 when this rank's status word holds an error) in every rank's
+// window.  Each CTA fences its writes at system scope before it counts
+// itself in; the last one fences again after seeing every count, so every
+// CTA's writes precede the flags a peer acquires.
+__device__ __forceinline__ void ep_signal(const EpPeers& p, int kind, int* ticket, const int* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned ctas = gridDim.x * gridDim.y * gridDim.z;
+    if (static_cast<unsigned>(atomicAdd(ticket, 1)) == ctas - 1) {
+      __threadfence_system();
+      const unsigned v = 2u * p.seq + (ld_volatile_int(err) != 0 ? 1u : 0u);
+      for (int w = 0; w < p.world; ++w) st_release_sys_u32(ep_flag(p, w, kind, p.rank), v);
+      atomicExch(ticket, 0);
+    }
+  }
+}
+
+}  // namespace fw

@@ -665,11 +665,29 @@ struct CombineArgs {
   const uint16_t* gated_sh;
   uint16_t* y;
   HcPost hc;  // hyper-connection injection (hc.out null: none)
+  // Expert parallelism over peer memory: the rows arrived in this rank's
+  // window (k_ep_wait_done ran first); skip when the forward failed.
+  const int* err;
 };
+
+// Expert parallelism over peer memory: one thread waits (bounded) until
+// every rank has set its done flag in this rank's window, i.e. every
+// weighted row of this rank's tokens has landed; the combine follows in
+// stream order.
+struct EpWaitArgs {
+  EpPeers p;
+  int* err;
+};
+__global__ void k_ep_wait_done(EpWaitArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) ep_wait_flags(a.p, kEpFlagDone, a.err);
+}
 
 __global__ void __launch_bounds__(512, 2) k_combine(CombineArgs a) {
   pdl_wait();
   pdl_launch_dependents();
+  if (a.err != nullptr && ld_volatile_int(a.err) != 0) return;
   const int t = blockIdx.x;
   const int c = threadIdx.x * 8;
   if (c >= a.H) return;
@@ -914,9 +932,14 @@ cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t*
 
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
                            const int32_t* ep_idx, int ep_world, const uint16_t* ep_rows, const int32_t* row_of,
-                           const HcPost* hc) {
+                           const HcPost* hc, const EpPeers* wait) {
   CombineArgs a{s.H, s.K, T, sc.sorted_slot, ep_idx, ep_world > 0 ? ep_world : 1, row_of,
-                ep_rows != nullptr ? ep_rows : sc.weighted, sc.gated_sh, y, hc != nullptr ? *hc : HcPost{}};
+                ep_rows != nullptr ? ep_rows : sc.weighted, sc.gated_sh, y, hc != nullptr ? *hc : HcPost{},
+                wait != nullptr ? sc.err : nullptr};
+  if (wait != nullptr) {
+    const cudaError_t e = launch_pdl(k_ep_wait_done, dim3(1), dim3(32), 0, st, EpWaitArgs{*wait, sc.err});
+    if (e != cudaSuccess) return e;
+  }
   return launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
 }
 
@@ -930,15 +953,15 @@ cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts
   // 1. router logits + shared-gate logit
   e = launch_router(s, w, sc, x, T, st);
   if (e != cudaSuccess || (e = mark(1)) != cudaSuccess) return e;
-  // 2. route + expert schedule
+  // 2. route + expert schedule (the dispatch stage is empty on one GPU)
   e = launch_route_block(s, luts, sc, T, topk_idx, topk_score, true, nullptr, st);
-  if (e != cudaSuccess || (e = mark(2)) != cudaSuccess) return e;
+  if (e != cudaSuccess || (e = mark(2)) != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
   // 3. experts: gate_up + SwiGLU, then down + scale (one persistent kernel)
   e = launch_experts(s, w, luts, sc, x, T, topk_score, st, x, T);
-  if (e != cudaSuccess || (e = mark(3)) != cudaSuccess) return e;
+  if (e != cudaSuccess || (e = mark(4)) != cudaSuccess) return e;
   // 4. combine
   e = launch_combine(s, sc, T, y, st, nullptr, 0, nullptr, nullptr, hc);
-  if (e == cudaSuccess) e = mark(4);
+  if (e == cudaSuccess) e = mark(5);
   return e;
 }
 

@@ -73,7 +73,20 @@ struct ExpertsArgs {
   int* err;
   const uint16_t* sh_x;        // [sh_T][H] the shared expert's token rows
   int sh_T;
+  // Bound of the waits on up_done (ns), and a count added to every up_done
+  // target (0; a test makes it unreachable to exercise the bounded wait).
+  unsigned long long wait_ns;
+  int stall;
+  // Expert parallelism over peer memory (ep.world > 0): routed rows go to
+  // their owner's window (ep_recv_row) instead of `weighted`, and the
+  // kernel's last CTA sets this rank's done flag in every window.
+  EpPeers ep;
 };
+
+// Destination of pair `pair`'s weighted row.
+__device__ __forceinline__ uint16_t* routed_row(const ExpertsArgs& a, long long pair) {
+  return a.ep.world > 0 ? ep_recv_row(a.ep, pair) : a.weighted + pair * a.H;
+}
 
 // Per-launch constants, identical in every thread of a CTA.
 struct Ctx {
@@ -325,8 +338,8 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const Pass& p, int item, 
         const float d = bf16_to_f32(f32_to_bf16(val[t]));
         // routed: bf16(down * route weight) (src/expert.rs:748-751);
         // shared: bf16(sigmoid * down) (src/expert.rs:1144-1147)
-        uint16_t* dst = routed ? a.weighted : a.gated_sh;
-        dst[static_cast<size_t>(tok_row[t]) * a.H + h] = f32_to_bf16(d * tok_scale[t]);
+        uint16_t* dst = routed ? routed_row(a, tok_row[t]) : a.gated_sh + static_cast<size_t>(tok_row[t]) * a.H;
+        dst[h] = f32_to_bf16(d * tok_scale[t]);
       }
     }
   }
@@ -388,6 +401,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
 
   pdl_wait();  // the schedule comes from the route kernel
   pdl_launch_dependents();
+  // Under expert parallelism a failed dispatch leaves the schedule stale:
+  // compute nothing, but still signal (with the failure) so peers stop waiting.
+  const bool skip = a.ep.world > 0 && ld_volatile_int(a.err) != 0;
 
   Ctx c;
   c.a = &a;
@@ -436,14 +452,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
   const uint64_t policy = l2_evict_first_policy();
   Cursor k;
   cursor_begin(k, c, warp);
-  for (int i = 0; i < kRing && k.live; ++i) {
+  for (int i = 0; i < kRing && k.live && !skip; ++i) {
     issue_stage<kTiled>(k, c, my_ring + i * kStageBytes, &my_bars[i], policy, lane);
     cursor_next(k, c, warp);
   }
   int consumed = 0;
   bool aborted = false;
 
-  for (int phase = 0; phase < 2 && !aborted; ++phase) {
+  for (int phase = 0; phase < 2 && !aborted && !skip; ++phase) {
     Pass p;
     bool ok = first_pass(c, phase, p);
     int cur_s = -1, cur_units = 0;
@@ -461,11 +477,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
       if (phase == 1 && p.s != cur_s) {
         // all of this slot's up units must be complete (bounded wait)
         if (threadIdx.x == 0) {
-          const int target = ((slot_tokens(c, p.s) + a.tgp - 1) / a.tgp) * units_per_pass(c, 0, p.s);
+          const int target =
+              ((slot_tokens(c, p.s) + a.tgp - 1) / a.tgp) * units_per_pass(c, 0, p.s) + a.stall;
           if (ld_acquire_gpu(&a.up_done[p.s]) < target) {
             const uint64_t t0 = global_ns();
             while (ld_acquire_gpu(&a.up_done[p.s]) < target) {
-              if (global_ns() - t0 > kWaitNs) {
+              if (global_ns() - t0 > a.wait_ns) {
                 set_error(a.err, kErrTimeout);
                 *s_abort = 1;
                 break;
@@ -574,6 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
       if (!mbar_wait_bounded(&my_bars[kk % kRing], (kk / kRing) & 1, kDrainNs)) break;
     }
   }
+  if (a.ep.world > 0) ep_signal(a.ep, kEpFlagDone, a.ep.ticket + 1, a.err);
 }
 
 // ---- small widths: one producer warp, a CTA-wide ring ----------------------
@@ -895,7 +913,8 @@ __global__ void __launch_bounds__(kSmallThreads, 1) k_experts_small(const __grid
             }
             if (phase == 1) {
               // all of the slot's up units are stored (bounded wait)
-              const int target = ((slot_tokens(c, p.s) + a.tgp - 1) / a.tgp) * units_per_pass(c, 0, p.s);
+              const int target =
+                  ((slot_tokens(c, p.s) + a.tgp - 1) / a.tgp) * units_per_pass(c, 0, p.s) + a.stall;
               int good = 1;
               if (lane == 0 && ld_acquire_gpu(&a.up_done[p.s]) < target) {
                 const uint64_t w0 = global_ns();
@@ -904,7 +923,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1) k_experts_small(const __grid
                     good = 0;
                     break;
                   }
-                  if (global_ns() - w0 > kWaitNs) {
+                  if (global_ns() - w0 > a.wait_ns) {
                     set_error(a.err, kErrTimeout);
                     *s_abort = 1;
                     good = 0;
@@ -1025,13 +1044,14 @@ size_t experts_smem_bytes(const Shape& s, bool tiled) {
 
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
                            const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st,
-                           const uint16_t* sh_x, int sh_T) {
+                           const uint16_t* sh_x, int sh_T, const EpPeers* ep) {
   DeviceAttrs dev;
   if (const cudaError_t e = current_device_attrs(&dev); e != cudaSuccess) return e;
   const int tgp = experts_tokens_per_pass(s);
   ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, tgp, x, w.gate_up, w.down, w.sh_gate,
                 w.sh_up, w.sh_down, w.ep_world, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
-                sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err, sh_x, sh_T};
+                sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err, sh_x, sh_T,
+                sc.wait_ns, sc.stall, ep != nullptr ? *ep : EpPeers{}};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;

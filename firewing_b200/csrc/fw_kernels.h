@@ -18,7 +18,36 @@ enum DeviceError : int {
   kErrTimeout = 2,     // a bounded wait on an mbarrier / flag gave up
   kErrBadIndex = 3,    // an expert id outside [0, E) reached a kernel
   kErrCapacity = 4,    // more (token, expert) pairs than the scratch holds
+  kErrPeer = 5,        // an expert-parallel peer reported a failure in this forward
 };
+
+// ---- expert parallelism over NVLink peer memory (fw_p2p.cu) -----------------
+constexpr int kEpMaxWorld = 8;
+// Every rank owns one exchange window (same layout on every rank), and every
+// window is mapped into every rank's address space:
+//   [0, 32)      uint32 pub[world]:  pub[w] = 2*seq (+1 on failure) once rank
+//                                    w's tokens of forward `seq` are in its window
+//   [128, 160)   uint32 done[world]: done[w] likewise once rank w has written
+//                                    every weighted row it computed for this
+//                                    rank's tokens of forward `seq`
+//   off_x        [M][H] bf16   this rank's token rows of the current forward
+//   off_idx      [M][K] int32  their top-k ids
+//   off_score    [M][K] bf16   their route weights
+//   off_recv     [M][K][H] bf16 weighted rows of this rank's tokens, row t*K+k
+//                               written by the rank that holds expert idx[t][k]
+// A flag is written with a release store at system scope and read with
+// acquire loads; every wait on one is bounded.
+struct EpPeers {
+  unsigned char* win[kEpMaxWorld] = {};  // window of rank r in this rank's address space
+  int rank = 0, world = 0;               // world == 0: expert parallelism over peer memory is off
+  int t_local = 0;                       // tokens per rank in this forward
+  int K = 0, H = 0;
+  long long off_x = 0, off_idx = 0, off_score = 0, off_recv = 0;
+  unsigned seq = 0;                      // forward sequence number (same on every rank)
+  unsigned long long wait_ns = 0;        // bound of every wait on a peer
+  int* ticket = nullptr;                 // [2] CTA completion counters of the signalling kernels (kept at 0)
+};
+constexpr int kEpFlagPub = 0, kEpFlagDone = 1;
 
 
 // Block shape.  All counts in elements.
@@ -117,6 +146,11 @@ struct Scratch {
   uint16_t* xg = nullptr;        // input rows in grouped pair order, K-blocked: [H/64][pair_cap][64]
   long long pair_cap = 0;        // pair rows of xg / act / pair_tk (max_T * K; more under expert parallelism)
   float* router_approx = nullptr;  // [T][E] tensor-core router logits (prefill), before the exact repair
+  // Bound of the expert kernels' waits on other CTAs and on peers (ns), and
+  // a count added to the expert kernel's up_done targets (0; a test sets it
+  // to make that bounded wait expire).
+  unsigned long long wait_ns = 2000000000ull;
+  int stall = 0;
 };
 
 // Schedule layout inside Scratch::sched (int32 words), written by the route
@@ -166,8 +200,13 @@ struct HcPost {
 cudaError_t launch_hc_pre(const HcWeights& w, const HcScratch& hs, const Luts& luts, const uint16_t* post, int H,
                           int T, cudaStream_t st);
 
-// Pipeline stages of one block forward (for per-stage timing).
-enum Stage : int { kStageRouter = 0, kStageRoute, kStageExperts, kStageCombine, kStages };
+// Pipeline stages of one block forward (for per-stage timing): router
+// logits; route (and, under expert parallelism, publishing this rank's
+// tokens); dispatch (grouping the pairs by expert, and bringing every rank's
+// selections and the needed token rows under expert parallelism); the expert
+// FFNs; the combine (under expert parallelism including the wait for the
+// peers' rows).
+enum Stage : int { kStageRouter = 0, kStageRoute, kStageDispatch, kStageExperts, kStageCombine, kStages };
 
 // Whole decode-path block for T tokens, stream-ordered.  When stage_events is
 // non-null, kStages + 1 events are recorded around the stages.
@@ -183,9 +222,11 @@ size_t experts_smem_bytes(const Shape& s, bool tiled);
 int experts_tokens_per_pass(const Shape& s);
 // x / T: the routed pairs' token rows (all ranks' tokens under expert
 // parallelism); sh_x / sh_T: the tokens of the shared expert (this rank's).
+// ep: expert parallelism over peer memory (routed rows to their owners'
+// windows, done flags at the end), or null.
 cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
                            const uint16_t* x, int T, const uint16_t* topk_score, cudaStream_t st,
-                           const uint16_t* sh_x, int sh_T);
+                           const uint16_t* sh_x, int sh_T, const EpPeers* ep = nullptr);
 
 // Primitives (the reference crate's functions over device buffers).
 cudaError_t launch_linear(const uint16_t* w, const uint16_t* x, int rows, int cols, int T,
@@ -241,21 +282,28 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
 //          shared expert over sh_T tokens;
 //   gemms: gate/up and down GEMMs; weighted rows to out_rows at row t*K+k,
 //          or at send_pos[t*K+k] when send_pos is given.
+// mid (or null): an event recorded between the router logits and the route.
 cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
                                  const Luts& luts, const Scratch& sc, const uint16_t* x, int T, int32_t* topk_idx,
-                                 uint16_t* topk_score, bool count_pairs, cudaStream_t st);
+                                 uint16_t* topk_score, bool count_pairs, cudaStream_t st, cudaEvent_t mid = nullptr);
 // Per-layer tables of the prefill router (H a multiple of 256): upper
 // bounds of the router rows' 2-norms [E] and the partial-major copy of the
 // router rows plus the shared gate vector [E+1][H].
 cudaError_t launch_router_tables(const uint16_t* w, const uint16_t* extra_row, int E, int H, float* norms,
                                  uint16_t* pm, cudaStream_t st);
+// Pair offsets and GEMM work-unit prefixes from the pair counts of ecount
+// bank experts (one CTA); counts and scatter cursors are zeroed for the next
+// forward.
+cudaError_t launch_prefill_offsets(const Shape& s, const Scratch& sc, int ecount, int sh_T, cudaStream_t st);
 cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_t* idx, int n_pairs,
                                  const uint16_t* x_src, int ep_rank, int ep_world, int ecount, int sh_T,
                                  bool count_here, cudaStream_t st);
+// ep: expert parallelism over peer memory (routed rows to their owners'
+// windows, done flags after the down GEMM), or null.
 cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, const PrefillScratchMaps& smaps,
                                  const Luts& luts, const Scratch& sc, const uint16_t* x_own, int T_own, int ecount,
                                  const uint16_t* score, const int32_t* send_pos, uint16_t* out_rows,
-                                 cudaStream_t st);
+                                 cudaStream_t st, const EpPeers* ep = nullptr);
 // Packed positions of weighted rows for the expert-parallel exchange (see
 // k_ep_positions): send side over the gathered ids (group = token owner),
 // receive side over this rank's ids (group = computing GPU).
@@ -271,9 +319,12 @@ cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& 
 // see CombineArgs); null / 0 / null on one GPU.
 // row_of: explicit row of every (t, k) in ep_rows (expert-parallel prefill).
 // hc: the hyper-connection injection, fused into the epilogue (or null).
+// wait: expert parallelism over peer memory: wait (bounded) for every
+// rank's done flag before reading the rows (or null).
 cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y, cudaStream_t st,
                            const int32_t* ep_idx = nullptr, int ep_world = 0, const uint16_t* ep_rows = nullptr,
-                           const int32_t* row_of = nullptr, const HcPost* hc = nullptr);
+                           const int32_t* row_of = nullptr, const HcPost* hc = nullptr,
+                           const EpPeers* wait = nullptr);
 // Expert parallelism: schedule of this rank's experts (e % ep_world ==
 // ep_rank) over the gathered selections idx_all [T][K], shared expert over
 // sh_T tokens.
@@ -301,6 +352,35 @@ const char* ep_async_error(EpComm* c);
 const char* ep_exchange_rows(EpComm* c, const uint16_t* send, const int* rows_send, const int* off_send,
                              uint16_t* recv, const int* rows_recv, const int* off_recv, size_t row_elems,
                              cudaStream_t st);
+
+// ---- expert parallelism over peer memory (fw_p2p.cu) ------------------------
+struct P2pComm;
+// Create this rank's exchange window (for forwards of up to max_tokens
+// tokens per rank) and map every rank's; collective over the world ranks'
+// processes (they find each other by the 128-byte id).  Null or a message.
+const char* p2p_init(int device, int rank, int world, const unsigned char id[128], int max_tokens, int H, int K,
+                     P2pComm** out);
+void p2p_destroy(P2pComm* c);
+size_t p2p_window_bytes(const P2pComm* c);
+EpPeers p2p_peers(const P2pComm* c, int t_local, unsigned seq, unsigned long long wait_ns);
+uint16_t* p2p_recv(const P2pComm* c);  // this rank's receive area, [max_tokens][K][H]
+// Copy this rank's tokens (rows, ids, route weights) into its window and set
+// its pub flags.
+cudaError_t launch_ep_publish(const EpPeers& p, const uint16_t* x, const int32_t* idx, const uint16_t* score, int* err,
+                              cudaStream_t st);
+// Decode widths: every rank's ids and weights into idx_all / score_all
+// [world*t_local][K], and the rows of tokens with one of this rank's
+// experts into x_all [world*t_local][H].
+cudaError_t launch_ep_pull(const EpPeers& p, int E, int32_t* idx_all, uint16_t* score_all, uint16_t* x_all, int* err,
+                           cudaStream_t st);
+// Prefill widths: every rank's ids and weights, and pair counts of this
+// rank's experts (count zeroed by the caller) ...
+cudaError_t launch_ep_ids(const EpPeers& p, int E, int32_t* idx_all, uint16_t* score_all, int* count, int* err,
+                          cudaStream_t st);
+// ... then, after the pair offsets, the grouped input rows, each token row
+// read once from its owner's window.
+cudaError_t launch_ep_scatter(const EpPeers& p, const int32_t* idx_all, const int* offset, int* fill, int32_t* pair_tk,
+                              uint16_t* xg, long long xg_rows, int* err, cudaStream_t st);
 
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.

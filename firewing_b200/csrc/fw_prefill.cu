@@ -216,6 +216,11 @@ struct GemmArgs {
   uint16_t* weighted;      // [T*K][H]
   uint16_t* gated_sh;      // [T][H]
   int* err;
+  // Expert parallelism over peer memory (ep.world > 0): nothing is computed
+  // when this rank's forward already failed; the down phase stores routed
+  // rows in their owner's window (ep_recv_row) and its last CTA sets this
+  // rank's done flag in every window.
+  EpPeers ep;
 };
 
 struct Unit {
@@ -316,8 +321,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(ring_b + kRingB * kBBytes + kEpiSets * kStageBytes);
   int* s_prefix = reinterpret_cast<int*>(tail + 1);     // [E+2]
   int* s_offset = s_prefix + a.E + 2;                   // [E+1]
-  int* s_col_row = s_offset + a.E + 1;                  // [kBN] epilogue: destination row per column
-  float* s_col_scale = reinterpret_cast<float*>(s_col_row + kBN);  // [kBN] epilogue: scale per column
+  // [kBN] epilogue: destination row per column (8-byte aligned)
+  uint16_t** s_col_dst = reinterpret_cast<uint16_t**>((reinterpret_cast<uintptr_t>(s_offset + a.E + 1) + 7) & ~uintptr_t(7));
+  float* s_col_scale = reinterpret_cast<float*>(s_col_dst + kBN);  // [kBN] epilogue: scale per column
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -353,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tail->tmem_base;
-  const int total = s_prefix[a.E + 1];
+  const int total = (a.ep.world > 0 && ld_volatile_int(a.err) != 0) ? 0 : s_prefix[a.E + 1];
 
   if (warp == 0) {
     // ---------------- weight-tile producer ----------------
@@ -455,10 +461,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (((j >> 5) & 1) != set) continue;
           if (w.routed) {
             const int tk = a.pair_tk[w.n0 + j];
-            s_col_row[j] = a.send_pos != nullptr ? a.send_pos[tk] : tk;
+            s_col_dst[j] = a.ep.world > 0 ? ep_recv_row(a.ep, tk)
+                                          : a.weighted + static_cast<size_t>(a.send_pos != nullptr ? a.send_pos[tk] : tk) * a.H;
             s_col_scale[j] = bf16_to_f32(a.score[tk]);
           } else {
-            s_col_row[j] = w.n0 + j;
+            s_col_dst[j] = a.gated_sh + static_cast<size_t>(w.n0 + j) * a.H;
             s_col_scale[j] = bf16_to_f32(a.sh_sig[w.n0 + j]);
           }
         }
@@ -523,11 +530,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 *reinterpret_cast<const uint4*>(stage + r * 64 + c * 8);
           }
         } else {
-          // [32 tokens][128 output rows]: 16 chunks of 16 bytes per token.
-          uint16_t* dst = w.routed ? a.weighted : a.gated_sh;
+          // [32 tokens][128 output rows]: 16 chunks of 16 bytes per token
+          // (under expert parallelism, routed rows go over NVLink).
           for (int ch = et; ch < rows_here * 16; ch += 128) {
             const int r = ch >> 4, c = ch & 15;
-            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(s_col_row[c0 + r]) * a.H + w.m * kBM + c * 8) =
+            *reinterpret_cast<uint4*>(s_col_dst[c0 + r] + w.m * kBM + c * 8) =
                 *reinterpret_cast<const uint4*>(stage + r * 128 + c * 8);
           }
         }
@@ -543,6 +550,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kAccCols) : "memory");
+  if (a.phase == 1 && a.ep.world > 0) ep_signal(a.ep, kEpFlagDone, a.ep.ticket + 1, a.err);
 }
 
 // ---- router for prefill widths ---------------------------------------------------
@@ -1021,7 +1029,6 @@ __global__ void k_ep_count(const int32_t* idx, int n, int rank, int world, int e
 // pos[i] = offset[g] + (flagged entries of group g before i), else -1;
 // count[g], offset[g] (exclusive over g).  Entries in index order keep each
 // group's rows in (token, k) order on both sides.  One CTA of 1024 threads.
-constexpr int kEpMaxWorld = 8;
 __global__ void __launch_bounds__(1024) k_ep_positions(const int32_t* idx, int n, int group_len, int me, int world,
                                                         int recv_mode, int32_t* pos, int* count,
                                                         int* offset) {
@@ -1109,8 +1116,8 @@ cudaError_t launch_pdl_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStr
 
 size_t gemm_smem_bytes(int E) {
   return 1024 + static_cast<size_t>(kRingA) * kABytes + static_cast<size_t>(kRingB) * kBBytes +
-         kEpiSets * kStageBytes + sizeof(GemmSmemTail) +
-         sizeof(int) * (2 * kBN + 2 * static_cast<size_t>(E) + 3);
+         kEpiSets * kStageBytes + sizeof(GemmSmemTail) + sizeof(int) * (2 * static_cast<size_t>(E) + 3) + 8 +
+         (sizeof(uint16_t*) + sizeof(float)) * kBN;
 }
 
 // ---- tensor maps (host) --------------------------------------------------------------
@@ -1218,7 +1225,7 @@ cudaError_t launch_router_fix(const RouterFixArgs& fa, cudaStream_t st) {
 
 cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const PrefillWeightMaps& wm,
                                  const Luts& luts, const Scratch& sc, const uint16_t* x, int T, int32_t* topk_idx,
-                                 uint16_t* topk_score, bool count_pairs, cudaStream_t st) {
+                                 uint16_t* topk_score, bool count_pairs, cudaStream_t st, cudaEvent_t mid) {
   if (w.router_norm == nullptr || w.router_pm == nullptr || sc.router_approx == nullptr) return cudaErrorInvalidValue;
   cudaError_t e;
   if (count_pairs && (e = cudaMemsetAsync(sc.pair_count, 0, sizeof(int) * s.E, st)) != cudaSuccess) return e;
@@ -1234,7 +1241,14 @@ cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Pr
   const RouterFixArgs fa{w.router_pm, w.bias, w.router_norm, sc.router_approx, x, sc.logits, sc.sh_logit,
                          s.E, s.H, T, s.K};
   if ((e = launch_router_fix(fa, st)) != cudaSuccess) return e;
+  if (mid != nullptr && (e = cudaEventRecord(mid, st)) != cudaSuccess) return e;
   return launch_route_block(s, luts, sc, T, topk_idx, topk_score, false, count_pairs ? sc.pair_count : nullptr, st);
+}
+
+cudaError_t launch_prefill_offsets(const Shape& s, const Scratch& sc, int ecount, int sh_T, cudaStream_t st) {
+  OffsetsArgs oa{ecount, sh_T, 2 * s.I / kBM, 2 * s.Is / kBM, s.H / kBM, sc.pair_count, sc.pair_fill, sc.pair_offset,
+                 sc.unit_prefix};
+  return launch_pdl_ex(k_pf_offsets, dim3(1), dim3((ecount + 31) / 32 * 32), 0, st, oa);
 }
 
 cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_t* idx, int n_pairs,
@@ -1249,9 +1263,7 @@ cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_
         cudaSuccess)
       return e;
   }
-  OffsetsArgs oa{ecount, sh_T, 2 * s.I / kBM, 2 * s.Is / kBM, s.H / kBM, sc.pair_count, sc.pair_fill, sc.pair_offset,
-                 sc.unit_prefix};
-  if ((e = launch_pdl_ex(k_pf_offsets, dim3(1), dim3((ecount + 31) / 32 * 32), 0, st, oa)) != cudaSuccess) return e;
+  if ((e = launch_prefill_offsets(s, sc, ecount, sh_T, st)) != cudaSuccess) return e;
   return launch_pdl_ex(k_pf_scatter, dim3((n_pairs + 7) / 8), dim3(256), 0, st, idx, n_pairs, s.K, s.E, s.H, ep_rank,
                        ep_world, static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x_src, sc.xg,
                        static_cast<long long>(sc.pair_cap), sc.err);
@@ -1260,7 +1272,7 @@ cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_
 cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, const PrefillScratchMaps& smaps,
                                  const Luts& luts, const Scratch& sc, const uint16_t* x_own, int T_own, int ecount,
                                  const uint16_t* score, const int32_t* send_pos, uint16_t* out_rows,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, const EpPeers* ep) {
   // Per-forward map of this rank's input rows (the shared expert's token tiles).
   TokenMaps x_rows;
   if (!token_maps(&x_rows, x_own, s.H, T_own)) return cudaErrorInvalidValue;
@@ -1288,6 +1300,7 @@ cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, co
   g.gated_sh = sc.gated_sh;
   g.err = sc.err;
   g.send_pos = send_pos;
+  if (ep != nullptr) g.ep = *ep;
   g.rows_r = sc.pair_cap;
   g.rows_s = sc.max_T;
   // gate/up + SwiGLU
@@ -1327,16 +1340,18 @@ cudaError_t launch_prefill(const Shape& s, const LayerWeights& w, const PrefillW
   cudaError_t e;
   auto mark = [&](int i) { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; };
   if ((e = mark(0)) != cudaSuccess) return e;
-  if ((e = launch_prefill_front(s, w, wm, luts, sc, x, T, topk_idx, topk_score, true, st)) != cudaSuccess) return e;
-  if ((e = mark(1)) != cudaSuccess) return e;
-  if ((e = launch_prefill_group(s, sc, topk_idx, T * s.K, x, 0, 1, s.E, T, false, st)) != cudaSuccess) return e;
+  if ((e = launch_prefill_front(s, w, wm, luts, sc, x, T, topk_idx, topk_score, true, st,
+                                ev != nullptr ? ev[1] : nullptr)) != cudaSuccess)
+    return e;
   if ((e = mark(2)) != cudaSuccess) return e;
+  if ((e = launch_prefill_group(s, sc, topk_idx, T * s.K, x, 0, 1, s.E, T, false, st)) != cudaSuccess) return e;
+  if ((e = mark(3)) != cudaSuccess) return e;
   if ((e = launch_prefill_gemms(s, wm, smaps, luts, sc, x, T, s.E, topk_score, nullptr, sc.weighted, st)) !=
       cudaSuccess)
     return e;
-  if ((e = mark(3)) != cudaSuccess) return e;
+  if ((e = mark(4)) != cudaSuccess) return e;
   if ((e = launch_combine(s, sc, T, y, st, nullptr, 0, nullptr, nullptr, hc)) != cudaSuccess) return e;
-  return mark(4);
+  return mark(5);
 }
 
 }  // namespace fw

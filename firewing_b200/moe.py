@@ -30,6 +30,10 @@ FW_ETIMEOUT = -4
 FW_ENOMEM = -5
 FW_ENAN = -6
 
+# expert-parallel transports (fw_moe_ep_set_transport)
+EP_TRANSPORT_P2P = 0
+EP_TRANSPORT_NCCL = 1
+
 _HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -93,6 +97,9 @@ def library() -> ctypes.CDLL:
     L.fw_moe_forward_hc.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp]
     L.fw_moe_forward_hc_async.argtypes = [vp, ctypes.c_int32, vp, ctypes.c_int32, vp, vp, vp, vp]
     L.fw_moe_ep_init.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_char_p]
+    L.fw_moe_ep_set_transport.argtypes = [vp, ctypes.c_int32]
+    L.fw_moe_set_wait_limit.argtypes = [vp, ctypes.c_uint64]
+    L.fw_moe_test_stall.argtypes = [vp]
     L.fw_moe_load_layer_safetensors.argtypes = [vp, ctypes.c_int32, ctypes.c_char_p, ctypes.c_char_p]
     L.fw_moe_load_hc_safetensors.argtypes = [vp, ctypes.c_int32, ctypes.c_char_p, ctypes.c_char_p]
     L.fw_safetensors_tensor_info.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
@@ -124,7 +131,8 @@ def library() -> ctypes.CDLL:
                  "fw_moe_forward_hc_async", "fw_moe_load_layer_safetensors", "fw_moe_load_hc_safetensors",
                  "fw_safetensors_tensor_info", "fw_moe_get_config", "fw_moe_last_union", "fw_moe_load_expert",
                  "fw_moe_load_expert_container", "fw_codec_container_check",
-                 "fw_linear_bf16", "fw_swiglu_bf16", "fw_add_bf16", "fw_route_bf16", "fw_moe_forward_noalloc"):
+                 "fw_linear_bf16", "fw_swiglu_bf16", "fw_add_bf16", "fw_route_bf16", "fw_moe_forward_noalloc",
+                 "fw_moe_ep_set_transport", "fw_moe_set_wait_limit", "fw_moe_test_stall"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
@@ -233,16 +241,26 @@ class MoeBlock:
     def sync(self, stream=None) -> None:
         _check(library().fw_moe_sync(self._h, _stream(stream)))
 
-    STAGES = ("router", "route", "experts", "combine")
+    STAGES = ("router", "route", "dispatch", "experts", "combine")
 
-    def ep_init(self, rank: int, world: int, unique_id: bytes) -> None:
-        """Expert parallelism: this handle holds experts [rank*E/world,
-        (rank+1)*E/world) and every forward becomes collective over the
+    def ep_init(self, rank: int, world: int, unique_id: bytes, transport: int = EP_TRANSPORT_P2P) -> None:
+        """Expert parallelism: this handle holds the experts e with
+        e % world == rank and every forward becomes collective over the
         `world` ranks that share `unique_id` (from ep_unique_id on one rank).
-        Call on every rank before loading layers."""
+        transport: EP_TRANSPORT_P2P (NVLink peer memory, the default) or
+        EP_TRANSPORT_NCCL.  Call on every rank before loading layers."""
         if len(unique_id) != 128:
             raise ValueError("unique_id must be 128 bytes")
+        _check(library().fw_moe_ep_set_transport(self._h, int(transport)))
         _check(library().fw_moe_ep_init(self._h, int(rank), int(world), bytes(unique_id)))
+
+    def set_wait_limit(self, seconds: float) -> None:
+        """Bound of the device-side waits on other CTAs and on peers."""
+        _check(library().fw_moe_set_wait_limit(self._h, int(seconds * 1e9)))
+
+    def test_stall(self) -> None:
+        """Test hook: the next forward's expert-kernel wait runs out (FW_ETIMEOUT)."""
+        _check(library().fw_moe_test_stall(self._h))
 
     def load_hc(self, layer: int, lowrank: int, hc_norm, mix_down, mix_up, inject) -> None:
         """Hyper-connection weights of one layer (host arrays or device tensors):

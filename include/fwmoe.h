@@ -127,7 +127,10 @@ int fw_moe_forward_async(fw_moe* handle, int32_t layer, const uint16_t* x, int32
  *     the combine.
  * Every rounding point is the reference's, so decode-width outputs are bit
  * for bit the reference's.  Host buffers (forward_hc) or device buffers
- * (forward_hc_async, stream-ordered); single GPU only. */
+ * (forward_hc_async, stream-ordered).  Under expert parallelism the
+ * hyper-connection stages run on each rank's own tokens and the block in
+ * between is expert-parallel; the call is then collective like
+ * fw_moe_forward. */
 int fw_moe_load_hc(fw_moe* handle, int32_t layer, int32_t lowrank, const uint16_t* hc_norm,
                    const uint16_t* mix_down, const uint16_t* mix_up, const uint16_t* inject);
 int fw_moe_forward_hc(fw_moe* handle, int32_t layer, const uint16_t* post, int32_t tokens,
@@ -154,24 +157,40 @@ int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);
  * and keeps this rank's experts.
  * Per layer:
  *   - router and route run on the rank's own tokens;
- *   - an all-gather brings every rank's token rows, top-k ids and route
- *     weights;
- *   - this rank's experts run over all gathered tokens;
- *   - each token's weighted rows return to its owner, which sums them in
- *     ascending expert id.
- * The decode path (widths up to min(256, 1024 / world) tokens per rank)
- * returns fixed-size blocks and is bit-identical to one GPU.  Wider forwards
- * take the prefill path's tensor-core GEMMs and a row-sized exchange;
- * their outputs are within the block tolerance and the call waits once on
- * the host for the exchange sizes.  NCCL (libnccl.so.2) is loaded at run
- * time.
+ *   - dispatch: this rank's experts get the token rows that selected them;
+ *   - this rank's experts run over those tokens (and the shared expert over
+ *     its own tokens);
+ *   - combine: each token's weighted rows return to its owner, which sums
+ *     them in ascending expert id.
+ * Two transports (fw_moe_ep_set_transport, before fw_moe_ep_init):
+ *   FW_EP_TRANSPORT_P2P (default): NVLink peer memory.  Every rank's
+ *     exchange window is mapped by every rank; dispatch pulls each needed
+ *     token row once per destination GPU, the expert kernels' epilogues
+ *     store the weighted rows straight into the owners' windows (the
+ *     transfer overlaps the expert GEMMs), and flags with bounded waits
+ *     order the steps; nothing waits on the host.  The ranks' processes find
+ *     each other through abstract Unix sockets named after `id`.
+ *   FW_EP_TRANSPORT_NCCL: all-gathers for the dispatch and grouped
+ *     send/recv for the combine over NCCL (libnccl.so.2, loaded at run
+ *     time); the prefill path waits once on the host for the exchange sizes.
+ * The decode path (widths up to min(256, 1024 / world) tokens per rank) is
+ * bit-identical to one GPU.  Wider forwards take the prefill path's
+ * tensor-core GEMMs; their outputs are within the block tolerance.
  *   fw_ep_unique_id: a communicator id; make it on one rank and hand the
  *     128 bytes to every rank (any host transport).
  *   fw_moe_ep_init: on every rank, collectively, after fw_moe_create and
  *     before any layer is loaded.  Needs 2 <= world <= 8 and
  *     experts % world == 0.  Afterwards every forward on the handle is
  *     collective: all ranks call it for the same layer with the same token
- *     count, in the same order.  FW_ENCCL on collective errors. */
+ *     count, in the same order.  FW_ENCCL on transport errors, and from the
+ *     next fw_moe_sync when a peer reported a failure; FW_ETIMEOUT when a
+ *     peer did not take part in a forward within the wait limit
+ *     (fw_moe_set_wait_limit).  A handle whose expert-parallel forward failed
+ *     stays failed (the ranks no longer agree on the forward count):
+ *     destroy it on every rank. */
+#define FW_EP_TRANSPORT_P2P 0
+#define FW_EP_TRANSPORT_NCCL 1
+int fw_moe_ep_set_transport(fw_moe* handle, int32_t transport);
 int fw_ep_unique_id(uint8_t id[128]);
 int fw_moe_ep_init(fw_moe* handle, int32_t rank, int32_t world, const uint8_t id[128]);
 
@@ -245,12 +264,30 @@ int fw_moe_last_union(fw_moe* handle, int32_t* distinct_experts, uint64_t* weigh
 /* Wait for `stream`, then report and clear device-side status. */
 int fw_moe_sync(fw_moe* handle, void* stream);
 
+/* Bound of the handle's device-side waits on other CTAs' work and on
+ * expert-parallel peers, in nanoseconds (1 ms .. 60 s; default 2 s).  A wait
+ * that runs out ends its kernel early with FW_ETIMEOUT reported by
+ * fw_moe_sync, instead of hanging the device.  No reference counterpart: the
+ * reference's device transactions fail closed on a command buffer error
+ * (src/metal_moe.rs:259-264, 353-358). */
+int fw_moe_set_wait_limit(fw_moe* handle, uint64_t nanoseconds);
+
+/* Test hook (no reference counterpart): the next forward on the handle makes
+ * the expert kernel's wait for its gate/up units unreachable, so that wait
+ * runs out after the wait limit and the forward reports FW_ETIMEOUT; the
+ * forward after it is normal again. */
+int fw_moe_test_stall(fw_moe* handle);
+
 /* Per-stage timing, for roofline measurement (the reference times its phases
  * with host intervals, src/metal_moe.rs:473-477, 590-606).  While enabled,
- * every forward records CUDA events around its four kernels (router logits,
- * route + permute, experts: gate_up + SwiGLU and down + scale, combine),
- * which serialises them; fw_moe_profile_read waits for the last forward and
- * returns the four durations in milliseconds (n >= 4). */
+ * every forward records CUDA events around its five stages, which
+ * serialises them; fw_moe_profile_read waits for the last forward and
+ * returns the five durations in milliseconds (n >= 5):
+ *   router logits; route (and, under expert parallelism, publishing this
+ *   rank's tokens); dispatch (grouping pairs by expert, and under expert
+ *   parallelism bringing every rank's selections and the needed rows);
+ *   experts (gate_up + SwiGLU, down + scale); combine (under expert
+ *   parallelism including the wait for the slowest peer's rows). */
 int fw_moe_profile(fw_moe* handle, int32_t enable);
 int fw_moe_profile_read(fw_moe* handle, float* stage_ms, int32_t n);
 
