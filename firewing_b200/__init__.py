@@ -7,9 +7,14 @@ runner).  There is no CPU fallback: every call runs the CUDA kernels, and
 importing the binding fails loudly when the library has not been built.
 """
 from .moe import (  # noqa: F401
+    EP_TRANSPORT_NCCL,
+    EP_TRANSPORT_P2P,
+    FW_ECUDA,
     FW_EINVAL,
     FW_ENAN,
     FW_ENCCL,
+    FW_ENOMEM,
+    FW_ETIMEOUT,
     FW_OK,
     FwError,
     MoeBlock,
