@@ -845,6 +845,8 @@ def main() -> None:
     ap.add_argument("--no-cfg4", action="store_true", help="skip the config-4 prefill line item")
     ap.add_argument("--only-prefill", action="store_true",
                     help="run only the config-2 prefill measurement and print it (for ncu captures)")
+    ap.add_argument("--only-cfg4", action="store_true",
+                    help="run only the config-4 measurement on one GPU and print it (for sweeps and ncu captures)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--minimal", action="store_true",
                     help="timed steps only (no T=4 pass, e2e, stage profile or CPU leg); "
@@ -867,6 +869,18 @@ def main() -> None:
             pass
         pre = measure_prefill(args, rank, 1, local_rank, peaks, torch.cuda.Stream(), lambda v: v, lambda: None)
         print(json.dumps({"only_prefill": True, "prefill": pre}), flush=True)
+        return
+    if args.only_cfg4:
+        import torch
+
+        torch.cuda.set_device(local_rank)
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except Exception:
+            pass
+        c4 = measure_cfg4(args, rank, 1, local_rank, peaks, torch.cuda.Stream(), lambda v: v, lambda: None, None)
+        print(json.dumps({"only_cfg4": True, "cfg4": c4}), flush=True)
         return
     if world > 1:
         import datetime

@@ -259,8 +259,10 @@ __global__ void __launch_bounds__(kRouterRows * 32) k_router(RouterArgs a) {
 
 // The router on the partial-major copy of the router rows (element
 // (row, j, i) = row[j + 32 i]; row E the shared gate vector), for H a
-// multiple of 256 (launched for single-token forwards).  A CTA of 4 warps
-// covers 16 rows x TT tokens; warp w rows 4w..4w+3 of the tile.  The CTA's rows are copied into
+// multiple of 256 (launched for forwards of up to four tokens).  A CTA of 4
+// warps covers 4 * RW rows x TT tokens; warp w rows RW*w..RW*w+RW-1 of the
+// tile.  With RW = 1 the E + 1 rows spread over ~130 CTAs, so each SM
+// copies and reduces only 16 KB of router weights.  The CTA's rows are copied into
 // shared memory with cp.async before the grid-dependency wait (they do not
 // depend on the previous kernel), the tokens after it; both tiles are laid
 // out partial-major with lane blocks padded to an odd number of 16-byte
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(kRouterRows * 32) k_router(RouterArgs a) {
 // partial j: its columns j, j+32, ... come as chunks of 8 in column order,
 // each added with 8 sequential mixed-precision FMAs -- the reference
 // schedule exactly -- then its tree.
-constexpr int kPmRows = 16, kPmWarps = 4;
+constexpr int kPmWarps = 4;
 
 __host__ __device__ inline int pm_stride(int H) {
   const int nch = H / 256;
@@ -279,8 +281,9 @@ __device__ __forceinline__ void cp_async16_dec(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
-template <int TT>
+template <int TT, int RW>
 __global__ void __launch_bounds__(kPmWarps * 32) k_router_pm(RouterArgs a) {
+  constexpr int kPmRows = kPmWarps * RW;
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = a.H >> 8, S = pm_stride(a.H), per = a.H >> 5;
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(kPmWarps * 32) k_router_pm(RouterArgs a) {
   uint4* xs = ws + kPmRows * 32 * S;            // [TT][32 lane blocks][S chunks]
   const int rbase = blockIdx.x * kPmRows;
   const int nrows = min(kPmRows, a.E + 1 - rbase);
-  const int row0 = rbase + warp * 4;
+  const int row0 = rbase + warp * RW;
   const int t0 = blockIdx.y * TT;
   const int nt = min(TT, a.T - t0);
   for (int g = threadIdx.x; g < nrows * 32 * nch; g += blockDim.x) {
@@ -313,26 +316,26 @@ __global__ void __launch_bounds__(kPmWarps * 32) k_router_pm(RouterArgs a) {
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  const uint4* wr[4];
+  const uint4* wr[RW];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int lr = min(warp * 4 + r, nrows - 1);  // rows past E repeat the last and are not stored
+  for (int r = 0; r < RW; ++r) {
+    const int lr = min(warp * RW + r, nrows - 1);  // rows past E repeat the last and are not stored
     wr[r] = ws + (lr * 32 + lane) * S;
   }
-  float acc[4][TT];
+  float acc[RW][TT];
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+  for (int r = 0; r < RW; ++r)
 #pragma unroll
     for (int t = 0; t < TT; ++t) acc[r][t] = 0.0f;
   for (int q = 0; q < nch; ++q) {
-    uint4 w[4];
+    uint4 w[RW];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) w[r] = wr[r][q];
+    for (int r = 0; r < RW; ++r) w[r] = wr[r][q];
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
       const uint4 xv = xs[(t * 32 + lane) * S + q];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
+      for (int r = 0; r < RW; ++r) {
         acc[r][t] = fma_seq2(w[r].x, xv.x, acc[r][t]);
         acc[r][t] = fma_seq2(w[r].y, xv.y, acc[r][t]);
         acc[r][t] = fma_seq2(w[r].z, xv.z, acc[r][t]);
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(kPmWarps * 32) k_router_pm(RouterArgs a) {
     }
   }
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < RW; ++r) {
     const int row = row0 + r;
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
@@ -900,13 +903,16 @@ cudaError_t launch_synth(uint64_t key, uint32_t /*tensor*/, uint64_t start, uint
 cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& sc, const uint16_t* x, int T,
                           cudaStream_t st) {
   RouterArgs a{w.router_pm, w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T, sc.err};
-  // One token: the partial-major router (T = 1 decode measured 18.5 k ->
-  // 19.4 k token-layers/s).  At T = 4 it measured 3 % slower than k_router
-  // and at T = 64 no faster, so wider forwards keep k_router.
-  if (T == 1 && w.router_pm != nullptr && s.H % 256 == 0) {
-    const int rows = (s.E + 1 + kPmRows - 1) / kPmRows;
-    const size_t smem = static_cast<size_t>(kPmRows + 1) * 32 * pm_stride(s.H) * 16;
-    return launch_pdl(k_router_pm<1>, dim3(rows, 1), dim3(kPmWarps * 32), smem, st, a);
+  // Up to four tokens: the partial-major router, one row per warp (T = 1
+  // decode with 16 rows per CTA measured 18.5 k -> 19.4 k token-layers/s
+  // against k_router).  Wider forwards keep k_router.
+  if (T <= 4 && w.router_pm != nullptr && s.H % 256 == 0) {
+    constexpr int kRows = kPmWarps;  // RW = 1
+    const int rows = (s.E + 1 + kRows - 1) / kRows;
+    const int tt = T == 1 ? 1 : 4;
+    const size_t smem = static_cast<size_t>(kRows + tt) * 32 * pm_stride(s.H) * 16;
+    return T == 1 ? launch_pdl(k_router_pm<1, 1>, dim3(rows, 1), dim3(kPmWarps * 32), smem, st, a)
+                  : launch_pdl(k_router_pm<4, 1>, dim3(rows, 1), dim3(kPmWarps * 32), smem, st, a);
   }
   const size_t smem = static_cast<size_t>(kRouterRows + kRouterTokens) * s.H * 2 + 16;
   const dim3 grid((s.E + 1 + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);

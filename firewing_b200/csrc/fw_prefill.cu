@@ -65,11 +65,23 @@
 namespace fw {
 namespace {
 
+// Ring depths and the token chunk are build-time settings (defaults below),
+// so tile and pipeline sweeps can build variants without editing the code.
+#ifndef FW_PF_RING_A
+#define FW_PF_RING_A 4
+#endif
+#ifndef FW_PF_RING_B
+#define FW_PF_RING_B 4
+#endif
+#ifndef FW_PF_BN
+#define FW_PF_BN 256
+#endif
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kBK = 64;         // columns per ring stage (one 128-byte swizzle atom)
-constexpr int kBN = 256;        // tokens per work unit (MMA N, max)
-constexpr int kRingA = 4;       // weight-tile ring stages
-constexpr int kRingB = 4;       // token-tile ring stages
+constexpr int kBN = FW_PF_BN;   // tokens per work unit (MMA N, max; 128 or 256)
+constexpr int kRingA = FW_PF_RING_A;  // weight-tile ring stages
+constexpr int kRingB = FW_PF_RING_B;  // token-tile ring stages
+static_assert(kBN == 128 || kBN == 256, "token chunk of 128 or 256");
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kStageBytes = 32 * kBM * 2;  // epilogue staging per set: 32 tokens x 128 rows, bf16
