@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kRouterRows * 32) k_router(RouterArgs a) {
 
 // The router on the partial-major copy of the router rows (element
 // (row, j, i) = row[j + 32 i]; row E the shared gate vector), for H a
-// multiple of 256 (launched for forwards of up to four tokens).  A CTA of 4
+// multiple of 256 (launched for single-token forwards).  A CTA of 4
 // warps covers 4 * RW rows x TT tokens; warp w rows RW*w..RW*w+RW-1 of the
 // tile.  With RW = 1 the E + 1 rows spread over ~130 CTAs, so each SM
 // copies and reduces only 16 KB of router weights.  The CTA's rows are copied into
@@ -903,16 +903,15 @@ cudaError_t launch_synth(uint64_t key, uint32_t /*tensor*/, uint64_t start, uint
 cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& sc, const uint16_t* x, int T,
                           cudaStream_t st) {
   RouterArgs a{w.router_pm, w.router, w.sh_gate_w, w.bias, x, sc.logits, sc.sh_logit, s.E, s.H, T, sc.err};
-  // Up to four tokens: the partial-major router, one row per warp (T = 1
-  // decode with 16 rows per CTA measured 18.5 k -> 19.4 k token-layers/s
-  // against k_router).  Wider forwards keep k_router.
-  if (T <= 4 && w.router_pm != nullptr && s.H % 256 == 0) {
+  // One token: the partial-major router, one row per warp on ~130 CTAs
+  // (with 16 rows per CTA it measured 18.5 k -> 19.4 k token-layers/s against
+  // k_router).  At T = 4 the same kernel measured 5 % slower than k_router,
+  // so wider forwards keep k_router.
+  if (T == 1 && w.router_pm != nullptr && s.H % 256 == 0) {
     constexpr int kRows = kPmWarps;  // RW = 1
     const int rows = (s.E + 1 + kRows - 1) / kRows;
-    const int tt = T == 1 ? 1 : 4;
-    const size_t smem = static_cast<size_t>(kRows + tt) * 32 * pm_stride(s.H) * 16;
-    return T == 1 ? launch_pdl(k_router_pm<1, 1>, dim3(rows, 1), dim3(kPmWarps * 32), smem, st, a)
-                  : launch_pdl(k_router_pm<4, 1>, dim3(rows, 1), dim3(kPmWarps * 32), smem, st, a);
+    const size_t smem = static_cast<size_t>(kRows + 1) * 32 * pm_stride(s.H) * 16;
+    return launch_pdl(k_router_pm<1, 1>, dim3(rows, 1), dim3(kPmWarps * 32), smem, st, a);
   }
   const size_t smem = static_cast<size_t>(kRouterRows + kRouterTokens) * s.H * 2 + 16;
   const dim3 grid((s.E + 1 + kRouterRows - 1) / kRouterRows, (T + kRouterTokens - 1) / kRouterTokens);
