@@ -78,12 +78,20 @@ namespace {
 #endif
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kBK = 64;         // columns per ring stage (one 128-byte swizzle atom)
-constexpr int kBN = FW_PF_BN;   // tokens per work unit (MMA N, max; 128 or 256)
+constexpr int kBN = FW_PF_BN;   // tokens per work unit (MMA N, max)
 constexpr int kRingA = FW_PF_RING_A;  // weight-tile ring stages
 constexpr int kRingB = FW_PF_RING_B;  // token-tile ring stages
-static_assert(kBN == 128 || kBN == 256, "token chunk of 128 or 256");
+static_assert(kBN == 256, "token chunk of 256 (pairs need the upper half of the token slot)");
+// The two rings advance together, one weight tile and one token tile per
+// stage, so they share their barriers: a stage is full when both producers
+// have posted it and both copies have landed, and one commit frees both.
+static_assert(kRingA == kRingB, "the weight and token rings share their barriers");
+constexpr int kRing = kRingA;
 constexpr int kABytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kPairTileOff = kBBytes / 2;  // second weight tile of a pair: upper half of the token slot
+constexpr int kPairCols = 128;             // its accumulator: TMEM columns 128.. of the buffer
+static_assert(kBBytes / 2 >= kABytes, "a pair's second weight tile fits beside a half-width token tile");
 constexpr int kStageBytes = 32 * kBM * 2;  // epilogue staging per set: 32 tokens x 128 rows, bf16
 constexpr int kEpiSets = 2;                // epilogue warp sets (4 warps each, alternate column groups)
 constexpr int kEpiWarp0 = 3;               // warps 0, 1: producers; 2: MMA; 3..: epilogue
@@ -235,8 +243,27 @@ struct GemmArgs {
   EpPeers ep;
 };
 
+// Token chunks of at most kPairMax tokens (every expert with few tokens,
+// and the last chunk of a busy one) take their weight tiles two at a time:
+// one unit streams the chunk's token tile once against two 128-row weight
+// tiles (the second lands in the unused upper half of the stage's token
+// slot) and accumulates into two TMEM column ranges, so each stage carries
+// twice the tensor work for one token load and one commit.
+constexpr int kPairMax = kBN / 2;
+
+// Work units of one phase for a slot of `count` token rows and `mt` 128-row
+// tiles: full chunks take one unit per tile, a last chunk of at most
+// kPairMax tokens one per pair of tiles.
+__host__ __device__ inline int slot_units(int count, int mt) {
+  if (count <= 0) return 0;
+  const int chunks = (count + kBN - 1) / kBN;
+  const int last = count - (chunks - 1) * kBN;
+  return (chunks - 1) * mt + (last <= kPairMax ? (mt + 1) / 2 : mt);
+}
+
 struct Unit {
   int slot, m, n0, nvalid, bn, kblocks;
+  int np;  // weight tiles of the unit: m and, when 2, m + 1
   bool routed;
 };
 
@@ -253,9 +280,25 @@ __device__ __forceinline__ Unit decode_unit(const GemmArgs& a, const int* s_pref
   w.routed = lo < a.E;
   const int mt = w.routed ? a.mt_r : a.mt_s;
   const int local = u - s_prefix[lo];
-  const int chunk = local / mt;
-  w.m = local - chunk * mt;
   const int count = w.routed ? s_offset[lo + 1] - s_offset[lo] : a.T;
+  const int chunks = (count + kBN - 1) / kBN;
+  const int full = (chunks - 1) * mt;  // units of the chunks before the last
+  int chunk;
+  if (local < full) {
+    chunk = local / mt;
+    w.m = local - chunk * mt;
+    w.np = 1;
+  } else {
+    chunk = chunks - 1;
+    const int i = local - full;
+    if (count - chunk * kBN <= kPairMax) {
+      w.m = 2 * i;
+      w.np = min(2, mt - w.m);
+    } else {
+      w.m = i;
+      w.np = 1;
+    }
+  }
   w.n0 = (w.routed ? s_offset[lo] : 0) + chunk * kBN;
   w.nvalid = min(kBN, count - chunk * kBN);
   w.bn = (w.nvalid + 15) & ~15;
@@ -264,10 +307,8 @@ __device__ __forceinline__ Unit decode_unit(const GemmArgs& a, const int* s_pref
 }
 
 struct __align__(8) GemmSmemTail {
-  uint64_t full_a[kRingA];
-  uint64_t empty_a[kRingA];
-  uint64_t full_b[kRingB];
-  uint64_t empty_b[kRingB];
+  uint64_t full[kRing];   // both producers arrive (with their bytes)
+  uint64_t empty[kRing];  // one tcgen05.commit frees the weight and the token slot
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t mma_done;
@@ -339,13 +380,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRingA; ++i) {
-      mbar_init(&tail->full_a[i], 1);
-      mbar_init(&tail->empty_a[i], 1);
-    }
-    for (int i = 0; i < kRingB; ++i) {
-      mbar_init(&tail->full_b[i], 1);
-      mbar_init(&tail->empty_b[i], 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&tail->full[i], 2);
+      mbar_init(&tail->empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tail->acc_full[i], 1);
@@ -377,16 +414,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- weight-tile producer ----------------
     const uint64_t policy = l2_evict_first_policy();
     produce(
-        a, s_prefix, s_offset, total, tail, tail->full_a, tail->empty_a, kRingA, lane,
-        [&](const Unit&, int) { return static_cast<uint32_t>(kABytes); },
+        a, s_prefix, s_offset, total, tail, tail->full, tail->empty, kRing, lane,
+        [&](const Unit& w, int) { return static_cast<uint32_t>(w.np * kABytes); },
         [&](const Unit& w, int kb, int st, uint64_t* bar) {
           const int grp0 = (w.routed ? w.slot * a.groups_r : 0) + w.m * (kBM / 8);
-          if (lane == 0) tma_load_4d(ring_a + st * kABytes, w.routed ? &map_a_r : &map_a_s, 0, 0, kb, grp0, bar, policy);
+          const CUtensorMap* ma = w.routed ? &map_a_r : &map_a_s;
+          if (lane == 0) {
+            tma_load_4d(ring_a + st * kABytes, ma, 0, 0, kb, grp0, bar, policy);
+            // second tile of a pair: the upper half of the stage's token slot
+            if (w.np == 2) tma_load_4d(ring_b + st * kBBytes + kPairTileOff, ma, 0, 0, kb, grp0 + kBM / 8, bar, policy);
+          }
         });
   } else if (warp == 1) {
     // ---------------- token-tile producer ----------------
     produce(
-        a, s_prefix, s_offset, total, tail, tail->full_b, tail->empty_b, kRingB, lane,
+        a, s_prefix, s_offset, total, tail, tail->full, tail->empty, kRing, lane,
         [&](const Unit& w, int) { return static_cast<uint32_t>(w.bn * kBK * 2); },
         [&](const Unit& w, int kb, int st, uint64_t* bar) {
           unsigned char* sb = ring_b + st * kBBytes;
@@ -409,7 +451,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 2) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      int ia = 0, ib = 0, ai = 0;
+      int ia = 0, ai = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total; u += gridDim.x, ++ai) {
         if (aborted(tail)) break;
@@ -423,10 +465,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + buf * kAccCols;
         const uint32_t idesc = idesc_bf16(kBM, w.bn);
-        for (int kb = 0; kb < w.kblocks; ++kb, ++ia, ++ib) {
-          const int sa_i = ia % kRingA, sb_i = ib % kRingB;
-          if (!mbar_wait_bounded(&tail->full_a[sa_i], (ia / kRingA) & 1, kWaitNs) ||
-              !mbar_wait_bounded(&tail->full_b[sb_i], (ib / kRingB) & 1, kWaitNs)) {
+        const bool pair = w.np == 2;
+        for (int kb = 0; kb < w.kblocks; ++kb, ++ia) {
+          const int sa_i = ia % kRing, sb_i = sa_i;
+          if (!mbar_wait_bounded(&tail->full[sa_i], (ia / kRing) & 1, kWaitNs)) {
             raise_abort(tail, a.err);
             ok = false;
             break;
@@ -435,10 +477,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t sa = smem_u32(ring_a + sa_i * kABytes);
           const uint32_t sb = smem_u32(ring_b + sb_i * kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
+          for (int k = 0; k < kBK / 16; ++k) {
             umma_bf16(d, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&tail->empty_a[sa_i]);
-          umma_commit(&tail->empty_b[sb_i]);
+            if (pair)
+              umma_bf16(d + kPairCols, sw128_desc(sb + kPairTileOff + k * 32), sw128_desc(sb + k * 32), idesc,
+                        (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&tail->empty[sa_i]);
         }
         if (ok) umma_commit(&tail->acc_full[buf]);
       }
@@ -489,9 +534,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * kAccCols;
+      // A pair's second tile sits kPairCols columns further in the buffer.
+      for (int jt = 0; jt < w.np; ++jt) {
+      const int mo = w.m + jt;  // the 128-row tile these columns belong to
       for (int c0 = 32 * set; c0 < w.bn; c0 += 32 * kEpiSets) {
         uint32_t v[32];
-        tmem_ld32(tbase + c0, v);
+        tmem_ld32(tbase + jt * kPairCols + c0, v);
         if (a.phase == 0) {
           // Rows alternate 4 gate / 4 up per 8-row group; lanes with
           // (row & 7) < 4 own a gate row and take the matching up value
@@ -535,7 +583,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // [32 tokens][64 intermediates] = rows of K-block m of act
           // ([I/64][rows][64]): 8 chunks of 16 bytes per token.
           uint16_t* dst = (w.routed ? a.act : a.act_sh) +
-                          static_cast<size_t>(w.m) * (w.routed ? a.rows_r : a.rows_s) * 64;
+                          static_cast<size_t>(mo) * (w.routed ? a.rows_r : a.rows_s) * 64;
           for (int ch = et; ch < rows_here * 8; ch += 128) {
             const int r = ch >> 3, c = ch & 7;
             *reinterpret_cast<uint4*>(dst + static_cast<size_t>(w.n0 + c0 + r) * 64 + c * 8) =
@@ -546,11 +594,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // (under expert parallelism, routed rows go over NVLink).
           for (int ch = et; ch < rows_here * 16; ch += 128) {
             const int r = ch >> 4, c = ch & 15;
-            *reinterpret_cast<uint4*>(s_col_dst[c0 + r] + w.m * kBM + c * 8) =
+            *reinterpret_cast<uint4*>(s_col_dst[c0 + r] + mo * kBM + c * 8) =
                 *reinterpret_cast<const uint4*>(stage + r * 128 + c * 8);
           }
         }
         epi_sync(set);
+      }
       }
       tc_fence_before();
       __syncwarp();
@@ -938,8 +987,7 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
   const int e = threadIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = (blockDim.x + 31) >> 5;
   const int c = e < a.E ? a.count[e] : 0;
-  const int chunks = (c + kBN - 1) / kBN;
-  int v[3] = {c, chunks * a.mt_up_r, chunks * a.mt_dn};
+  int v[3] = {c, slot_units(c, a.mt_up_r), slot_units(c, a.mt_dn)};
   int incl[3];
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
@@ -978,12 +1026,11 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
   }
   if (e == 0) {
     const int pairs = wsum[0][nw - 1], up = wsum[1][nw - 1], dn = wsum[2][nw - 1];
-    const int sh_chunks = (a.T + kBN - 1) / kBN;
     a.offset[a.E] = pairs;
     a.prefix[a.E] = up;
-    a.prefix[a.E + 1] = up + sh_chunks * a.mt_up_s;
+    a.prefix[a.E + 1] = up + slot_units(a.T, a.mt_up_s);
     a.prefix[a.E + 2 + a.E] = dn;
-    a.prefix[a.E + 2 + a.E + 1] = dn + sh_chunks * a.mt_dn;
+    a.prefix[a.E + 2 + a.E + 1] = dn + slot_units(a.T, a.mt_dn);
   }
 }
 
