@@ -662,7 +662,7 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
     if ((rc = alloc(h, &s.pair_count, E, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.pair_fill, E, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.pair_offset, static_cast<size_t>(E) + 1, o)) != FW_OK) break;
-    if ((rc = alloc(h, &s.unit_prefix, 2 * (static_cast<size_t>(E) + 2), o)) != FW_OK) break;
+    if ((rc = alloc(h, &s.unit_prefix, 4 * (static_cast<size_t>(E) + 2), o)) != FW_OK) break;
     if ((rc = alloc(h, &s.pair_tk, static_cast<size_t>(M) * K, o)) != FW_OK) break;
     if ((rc = alloc(h, &s.xg, static_cast<size_t>(M) * K * H, o)) != FW_OK) break;
     s.pair_cap = static_cast<long long>(M) * K;

@@ -141,7 +141,7 @@ struct Scratch {
   int* pair_count = nullptr;     // [E] pairs per expert (zeroed per forward)
   int* pair_fill = nullptr;      // [E] scatter cursors
   int* pair_offset = nullptr;    // [E+1] first pair of each expert in grouped order
-  int* unit_prefix = nullptr;    // [2][E+2] GEMM work-unit prefix per slot, up and down phases
+  int* unit_prefix = nullptr;    // [2 phases][2 classes][E+2] GEMM work-unit prefixes per slot (see fw_prefill.cu)
   int32_t* pair_tk = nullptr;    // [T*K] grouped pairs: t*K + top-k position
   uint16_t* xg = nullptr;        // input rows in grouped pair order, K-blocked: [H/64][pair_cap][64]
   long long pair_cap = 0;        // pair rows of xg / act / pair_tk (max_T * K; more under expert parallelism)

@@ -226,7 +226,10 @@ struct GemmArgs {
   // the packed send buffer (null: row t*K+k of `weighted`).
   const int32_t* send_pos;
   const int* offset;       // [E+1] grouped pair offsets
-  const int* prefix;       // [E+2] unit prefix of this phase (slot E = shared)
+  // [2][E+2] unit prefixes of this phase (slot E = shared): compute-heavy
+  // slots (more than kPairMax tokens), then weight-streaming ones; the two
+  // classes are interleaved in the unit order (decode_unit)
+  const int* prefix;
   const int32_t* pair_tk;  // [pairs] t*K + k
   const uint16_t* score;   // [T*K] route weights (bf16)
   const uint16_t* sh_sig;  // [T] shared gate (bf16)
@@ -267,19 +270,35 @@ struct Unit {
   bool routed;
 };
 
-// Unit u of this phase; s_prefix / s_offset are the shared-memory copies.
+// Unit u of this phase; s_prefix ([2][E+2]) / s_offset are the
+// shared-memory copies.  The units of compute-heavy slots (more than
+// kPairMax tokens: full 256-token chunks, tensor-bound) and of
+// weight-streaming slots (HBM-bound) are interleaved in proportion to their
+// counts, so that at any time some SMs stream weights while others compute:
+// with a skewed router the busy experts have the low ids, and slot order
+// alone would run all the tensor-bound units first and all the HBM-bound
+// ones after them.  Unit u is compute-heavy unit floor(u * Uh / U) when that
+// value steps at u, else weight-streaming unit u - floor(u * Uh / U).
 __device__ __forceinline__ Unit decode_unit(const GemmArgs& a, const int* s_prefix, const int* s_offset, int u) {
-  int lo = 0, hi = a.E;  // largest slot s with prefix[s] <= u
+  const int* ph = s_prefix;
+  const int* pt = s_prefix + a.E + 2;
+  const long long uh = ph[a.E + 1], ut = pt[a.E + 1];
+  const int hk = static_cast<int>(static_cast<long long>(u) * uh / (uh + ut));
+  const int hk1 = static_cast<int>(static_cast<long long>(u + 1) * uh / (uh + ut));
+  const bool heavy = hk1 > hk;
+  const int idx = heavy ? hk : u - hk;
+  const int* pre = heavy ? ph : pt;
+  int lo = 0, hi = a.E;  // largest slot s with pre[s] <= idx (it has units of this class)
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (s_prefix[mid] <= u) lo = mid;
+    if (pre[mid] <= idx) lo = mid;
     else hi = mid - 1;
   }
   Unit w;
   w.slot = lo;
   w.routed = lo < a.E;
   const int mt = w.routed ? a.mt_r : a.mt_s;
-  const int local = u - s_prefix[lo];
+  const int local = idx - pre[lo];
   const int count = w.routed ? s_offset[lo + 1] - s_offset[lo] : a.T;
   const int chunks = (count + kBN - 1) / kBN;
   const int full = (chunks - 1) * mt;  // units of the chunks before the last
@@ -372,8 +391,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   unsigned char* ring_b = smem + kRingA * kABytes;      // [kRingB][32 KB]
   uint16_t* s_stage = reinterpret_cast<uint16_t*>(ring_b + kRingB * kBBytes);  // [sets][32][128] epilogue staging
   GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(ring_b + kRingB * kBBytes + kEpiSets * kStageBytes);
-  int* s_prefix = reinterpret_cast<int*>(tail + 1);     // [E+2]
-  int* s_offset = s_prefix + a.E + 2;                   // [E+1]
+  int* s_prefix = reinterpret_cast<int*>(tail + 1);     // [2][E+2]
+  int* s_offset = s_prefix + 2 * (a.E + 2);             // [E+1]
   // [kBN] epilogue: destination row per column (8-byte aligned)
   uint16_t** s_col_dst = reinterpret_cast<uint16_t**>((reinterpret_cast<uintptr_t>(s_offset + a.E + 1) + 7) & ~uintptr_t(7));
   float* s_col_scale = reinterpret_cast<float*>(s_col_dst + kBN);  // [kBN] epilogue: scale per column
@@ -402,13 +421,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  for (int i = threadIdx.x; i < a.E + 2; i += blockDim.x) s_prefix[i] = a.prefix[i];
+  for (int i = threadIdx.x; i < 2 * (a.E + 2); i += blockDim.x) s_prefix[i] = a.prefix[i];
   for (int i = threadIdx.x; i < a.E + 1; i += blockDim.x) s_offset[i] = a.offset[i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tail->tmem_base;
-  const int total = (a.ep.world > 0 && ld_volatile_int(a.err) != 0) ? 0 : s_prefix[a.E + 1];
+  const int total =
+      (a.ep.world > 0 && ld_volatile_int(a.err) != 0) ? 0 : s_prefix[a.E + 1] + s_prefix[2 * (a.E + 2) - 1];
 
   if (warp == 0) {
     // ---------------- weight-tile producer ----------------
@@ -976,21 +996,26 @@ struct OffsetsArgs {
   int* count;    // [E], zeroed here for the next forward
   int* fill;     // [E], zeroed here
   int* offset;   // [E+1]
-  int* prefix;   // [2][E+2]
+  int* prefix;   // [2 phases][2 classes][E+2], see GemmArgs::prefix
 };
 
-// One CTA of blockDim.x >= E threads (thread e = expert e).
+// One CTA of blockDim.x >= E threads (thread e = expert e): exclusive scans
+// of the pair counts and, per phase, of the units of compute-heavy slots and
+// of weight-streaming slots.
 __global__ void k_pf_offsets(OffsetsArgs a) {
-  __shared__ int wsum[3][32];
+  constexpr int kScans = 5;  // pairs, up heavy, up streaming, down heavy, down streaming
+  __shared__ int wsum[kScans][32];
   pdl_wait();
   pdl_launch_dependents();
   const int e = threadIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nw = (blockDim.x + 31) >> 5;
   const int c = e < a.E ? a.count[e] : 0;
-  int v[3] = {c, slot_units(c, a.mt_up_r), slot_units(c, a.mt_dn)};
-  int incl[3];
+  const bool heavy = c > kPairMax;
+  const int up = slot_units(c, a.mt_up_r), dn = slot_units(c, a.mt_dn);
+  int v[kScans] = {c, heavy ? up : 0, heavy ? 0 : up, heavy ? dn : 0, heavy ? 0 : dn};
+  int incl[kScans];
 #pragma unroll
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < kScans; ++i) {
     int x = v[i];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -1003,7 +1028,7 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
   __syncthreads();
   if (warp == 0) {
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < kScans; ++i) {
       int x = lane < nw ? wsum[i][lane] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -1014,23 +1039,26 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
     }
   }
   __syncthreads();
-  int excl[3];
-#pragma unroll
-  for (int i = 0; i < 3; ++i) excl[i] = incl[i] - v[i] + (warp > 0 ? wsum[i][warp - 1] : 0);
+  const int P = a.E + 2;
   if (e < a.E) {
-    a.offset[e] = excl[0];
-    a.prefix[e] = excl[1];
-    a.prefix[a.E + 2 + e] = excl[2];
+    a.offset[e] = incl[0] - v[0] + (warp > 0 ? wsum[0][warp - 1] : 0);
+#pragma unroll
+    for (int i = 1; i < kScans; ++i) a.prefix[(i - 1) * P + e] = incl[i] - v[i] + (warp > 0 ? wsum[i][warp - 1] : 0);
     a.count[e] = 0;
     a.fill[e] = 0;
   }
   if (e == 0) {
-    const int pairs = wsum[0][nw - 1], up = wsum[1][nw - 1], dn = wsum[2][nw - 1];
-    a.offset[a.E] = pairs;
-    a.prefix[a.E] = up;
-    a.prefix[a.E + 1] = up + slot_units(a.T, a.mt_up_s);
-    a.prefix[a.E + 2 + a.E] = dn;
-    a.prefix[a.E + 2 + a.E + 1] = dn + slot_units(a.T, a.mt_dn);
+    // slot E: the shared expert over T tokens
+    const bool sh_heavy = a.T > kPairMax;
+    const int sh[4] = {sh_heavy ? slot_units(a.T, a.mt_up_s) : 0, sh_heavy ? 0 : slot_units(a.T, a.mt_up_s),
+                       sh_heavy ? slot_units(a.T, a.mt_dn) : 0, sh_heavy ? 0 : slot_units(a.T, a.mt_dn)};
+    a.offset[a.E] = wsum[0][nw - 1];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tot = wsum[i + 1][nw - 1];
+      a.prefix[i * P + a.E] = tot;
+      a.prefix[i * P + a.E + 1] = tot + sh[i];
+    }
   }
 }
 
@@ -1175,7 +1203,7 @@ cudaError_t launch_pdl_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStr
 
 size_t gemm_smem_bytes(int E) {
   return 1024 + static_cast<size_t>(kRingA) * kABytes + static_cast<size_t>(kRingB) * kBBytes +
-         kEpiSets * kStageBytes + sizeof(GemmSmemTail) + sizeof(int) * (2 * static_cast<size_t>(E) + 3) + 8 +
+         kEpiSets * kStageBytes + sizeof(GemmSmemTail) + sizeof(int) * (3 * static_cast<size_t>(E) + 5) + 8 +
          (sizeof(uint16_t*) + sizeof(float)) * kBN;
 }
 
@@ -1380,7 +1408,7 @@ cudaError_t launch_prefill_gemms(const Shape& s, const PrefillWeightMaps& wm, co
   g.mt_s = s.H / kBM;
   g.groups_r = s.H / 8;
   g.b_blocked_s = 1;  // shared down: K-blocked act_sh
-  g.prefix = sc.unit_prefix + ecount + 2;
+  g.prefix = sc.unit_prefix + 2 * (ecount + 2);
   return launch(wm.down, wm.sh_down, smaps.act, smaps.act_sh);
 }
 
