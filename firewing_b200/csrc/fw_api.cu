@@ -703,8 +703,13 @@ int fw_moe_get_config(const fw_moe* h, fw_moe_config* out) {
 int fw_moe_destroy(fw_moe* h) {
   if (h == nullptr) return FW_OK;
   cudaSetDevice(h->device);
-  if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->ep != nullptr && h->stream) {
+    // a collective a peer never joined must not hold the teardown
+    cudaError_t ce = cudaSuccess;
+    fw::ep_bounded_sync(h->ep, h->stream, 2 * h->sc.wait_ns, &ce);
+  }
   fw::ep_comm_destroy(h->ep);
+  if (h->stream) cudaStreamSynchronize(h->stream);
   fw::p2p_destroy(h->p2p);
   if (h->ep_counts_host) cudaFreeHost(h->ep_counts_host);
   if (h->ep_counts_ev) cudaEventDestroy(h->ep_counts_ev);
@@ -998,6 +1003,7 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
   cudaEvent_t* ev = h->profile ? h->stage_ev : nullptr;
   if (h->ep != nullptr || h->p2p != nullptr) {
+    if (fw::ep_comm_aborted(h->ep)) return fail(FW_ENCCL, "the communicator was aborted after a failure");
     bool ep_prefill = false;
     const int rc = ep_block(h, L, x, tokens, y, idx, sc, cs, ev, nullptr, &ep_prefill);
     if (rc == FW_OK) note_forward(h, ep_prefill, cs);
@@ -1048,6 +1054,18 @@ int fw_moe_set_prefill_min_tokens(fw_moe* h, int32_t min_tokens) {
 int fw_moe_sync(fw_moe* h, void* stream) {
   if (h == nullptr) return fail(FW_EINVAL, "handle is null");
   FW_CUDA(cudaSetDevice(h->device));
+  if (h->ep != nullptr) {
+    // Over NCCL a missing peer would hold the stream forever: wait at most
+    // the handle's wait limit (twice: the kernels' own waits come first).
+    cudaError_t ce = cudaSuccess;
+    switch (fw::ep_bounded_sync(h->ep, static_cast<cudaStream_t>(stream), 2 * h->sc.wait_ns, &ce)) {
+      case 0: break;
+      case 1: return fail(FW_ETIMEOUT, "an expert-parallel collective did not complete within the wait limit "
+                                       "(communicator aborted; destroy the handle)");
+      case 2: return fail(FW_ENCCL, "the NCCL communicator reported an error (aborted; destroy the handle)");
+      default: return fail(FW_ECUDA, "stream", cudaGetErrorString(ce));
+    }
+  }
   FW_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
   int code = 0;
   FW_CUDA(cudaMemcpy(&code, h->sc.err, sizeof(int), cudaMemcpyDeviceToHost));

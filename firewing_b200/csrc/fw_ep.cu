@@ -14,6 +14,8 @@
 // framework may already have loaded), so the single-GPU library carries no
 // NCCL dependency.
 #include <dlfcn.h>
+#include <time.h>
+#include <unistd.h>
 
 #include <cstdio>
 #include <cstring>
@@ -88,6 +90,7 @@ const char* nccl_fail(const char* what, ncclResult_t r) {
 struct EpComm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  bool aborted = false;  // ncclCommAbort ran: every later call fails
 };
 
 const char* ep_unique_id(unsigned char out[128]) {
@@ -118,11 +121,55 @@ const char* ep_comm_init(int rank, int world, const unsigned char id_bytes[128],
   return nullptr;
 }
 
+// Teardown never waits on the peers (a peer may be gone): the communicator
+// is aborted rather than destroyed, which releases it locally.
 void ep_comm_destroy(EpComm* c) {
   if (c == nullptr) return;
-  if (c->comm != nullptr && api().ok) api().comm_destroy(c->comm);
+  if (c->comm != nullptr && !c->aborted && api().ok) api().comm_abort(c->comm);
   delete c;
 }
+
+// Wait for `st` (the handle's forwards, NCCL kernels included) for at most
+// `limit_ns`, watching the communicator's asynchronous error.  When a peer
+// never joins a collective, NCCL's kernel keeps waiting for it: the
+// communicator is then aborted, which ends that kernel, and every later
+// forward on the handle fails.  Returns 0, 1 (timeout, aborted), 2 (NCCL
+// error, aborted) or 3 (a CUDA error, in *cuda_err).
+int ep_bounded_sync(EpComm* c, cudaStream_t st, unsigned long long limit_ns, cudaError_t* cuda_err) {
+  const NcclApi& a = api();
+  timespec t0;
+  clock_gettime(CLOCK_MONOTONIC, &t0);
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) return 0;
+    if (q != cudaErrorNotReady) {
+      *cuda_err = q;
+      return 3;
+    }
+    if (c != nullptr && !c->aborted && a.ok) {
+      ncclResult_t ae = ncclSuccess;
+      if (a.async_error(c->comm, &ae) == ncclSuccess && ae != ncclSuccess && ae != ncclInProgress) {
+        a.comm_abort(c->comm);
+        c->aborted = true;
+        return 2;
+      }
+    }
+    timespec t;
+    clock_gettime(CLOCK_MONOTONIC, &t);
+    const unsigned long long el = static_cast<unsigned long long>(t.tv_sec - t0.tv_sec) * 1000000000ull +
+                                  static_cast<unsigned long long>(t.tv_nsec) - static_cast<unsigned long long>(t0.tv_nsec);
+    if (el > limit_ns) {
+      if (c != nullptr && !c->aborted && a.ok) {
+        a.comm_abort(c->comm);
+        c->aborted = true;
+      }
+      return 1;
+    }
+    usleep(50);
+  }
+}
+
+bool ep_comm_aborted(const EpComm* c) { return c != nullptr && c->aborted; }
 
 const char* ep_dispatch(EpComm* c, const uint16_t* x, uint16_t* x_all, size_t x_elems, const int32_t* idx,
                         int32_t* idx_all, const uint16_t* score, uint16_t* score_all, size_t k_elems,

@@ -346,6 +346,11 @@ const char* ep_dispatch(EpComm* c, const uint16_t* x, uint16_t* x_all, size_t x_
 const char* ep_combine_exchange(EpComm* c, const uint16_t* send, uint16_t* recv, size_t block_elems,
                                 cudaStream_t st);
 const char* ep_async_error(EpComm* c);
+// Bounded wait for the stream with NCCL failure handling (see fw_ep.cu):
+// 0 done, 1 timeout (communicator aborted), 2 NCCL error (aborted),
+// 3 CUDA error (*cuda_err).
+int ep_bounded_sync(EpComm* c, cudaStream_t st, unsigned long long limit_ns, cudaError_t* cuda_err);
+bool ep_comm_aborted(const EpComm* c);
 // Row-sized exchange: rows_send[p] rows of `row_elems` bf16 from send at
 // row off_send[p] to rank p; rows_recv[p] rows from rank p into recv at
 // row off_recv[p] (counts on the host).
