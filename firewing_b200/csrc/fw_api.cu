@@ -310,6 +310,23 @@ struct Marks {
   cudaError_t operator()(int i) const { return ev != nullptr ? cudaEventRecord(ev[i], st) : cudaSuccess; }
 };
 
+// The next layer's weights that do not depend on its input (router rows in
+// the partial-major copy its router reads, shared expert tiles), for the
+// decode expert kernel to prefetch into L2 when its work is done: decode
+// forwards usually run the layers in order.
+void prefetch_next(const fw_moe* h, int layer, fw::Scratch* sc) {
+  if (layer + 1 >= h->cfg.layers) return;
+  const OwnedLayer& n = h->layers[layer + 1];
+  if (!n.loaded || !n.w.tiled) return;
+  const unsigned long long H = h->cfg.hidden, E = h->cfg.experts, Is = h->cfg.shared_intermediate;
+  sc->prefetch[0] = n.w.router_pm != nullptr ? static_cast<const void*>(n.w.router_pm) : n.w.router;
+  sc->prefetch_bytes[0] = (n.w.router_pm != nullptr ? E + 1 : E) * H * 2;
+  sc->prefetch[1] = n.w.sh_gate;  // tiled gate/up
+  sc->prefetch_bytes[1] = 2 * Is * H * 2;
+  sc->prefetch[2] = n.w.sh_down;
+  sc->prefetch_bytes[2] = H * Is * 2;
+}
+
 // The expert kernel's stall count for this forward (fw_moe_test_stall).
 int take_stall(fw_moe* h) {
   const int v = h->stall_next;
@@ -1013,6 +1030,7 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
   fw::Scratch scr = h->sc;
   scr.stall = take_stall(h);
+  if (!prefill) prefetch_next(h, layer, &scr);
   const cudaError_t e =
       prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, scr, x, tokens, y, idx, sc, cs, ev)
               : fw::launch_block(h->shape, L.w, h->luts, scr, x, tokens, y, idx, sc, cs, ev);

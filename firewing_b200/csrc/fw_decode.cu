@@ -624,6 +624,43 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
     }
   }
   if (a.sched == nullptr) return;
+  if (a.T == 1 && a.ep_world == 1) {
+    // One token on one GPU: the schedule follows from the K selected ids
+    // alone (each slot holds one pair), so warp 0 writes the same words
+    // build_schedule would, without its block-wide scans over E experts:
+    // slot = rank of the id among the selection, pair = its top-k position,
+    // every slot (and the shared expert's) costing one 1-token pass.
+    if (warp == 0) {
+      const int Kk = a.K;
+      int32_t* active = a.sched + 1;
+      int32_t* offsets = a.sched + 1 + E;
+      int32_t* pairs = a.sched + 2 + 2 * E;
+      int32_t* up_pref = pairs + Kk;
+      int32_t* dn_pref = up_pref + E + 2;
+      const int my = lane < Kk ? a.idx[lane] : 0;  // this lane's own write above
+      int rank = 0;
+      for (int k = 0; k < Kk; ++k) rank += (__shfl_sync(0xffffffffu, my, k) < my) ? 1 : 0;
+      // a 1-token pass: 4 + pad(1) up, 4 + 4 pad(1) down (as build_schedule)
+      const int cu = 5 * a.qpr, cd = 8 * a.ops;
+      if (lane < Kk) {
+        active[rank] = my;
+        offsets[rank] = rank;
+        pairs[rank] = lane;
+        up_pref[rank] = rank * cu;
+        dn_pref[rank] = rank * cd;
+      }
+      if (lane == 0) {
+        a.sched[0] = Kk;
+        offsets[Kk] = Kk;
+        up_pref[Kk] = Kk * cu;
+        up_pref[Kk + 1] = Kk * cu + 5 * a.qps;
+        dn_pref[Kk] = Kk * cd;
+        dn_pref[Kk + 1] = Kk * cd + cd;
+      }
+      for (int i = lane; i <= Kk; i += 32) a.up_done[i] = 0;
+    }
+    return;
+  }
   // The last CTA to finish builds the schedule from every token's selection
   // (a single-token launch is its own last CTA: no ticket).
   __syncthreads();

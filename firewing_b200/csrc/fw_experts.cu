@@ -81,7 +81,25 @@ struct ExpertsArgs {
   // their owner's window (ep_recv_row) instead of `weighted`, and the
   // kernel's last CTA sets this rank's done flag in every window.
   EpPeers ep;
+  // L2 prefetch once a CTA's units are done (see Scratch::prefetch)
+  const void* pf[3];
+  unsigned long long pf_bytes[3];
 };
+
+// This CTA's share of the prefetch ranges (thread 0; 16-byte aligned
+// ranges of 16-byte multiples), in pieces of at most 64 KB.
+__device__ __forceinline__ void prefetch_share(const ExpertsArgs& a) {
+  if (threadIdx.x != 0) return;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (a.pf[i] == nullptr || a.pf_bytes[i] == 0) continue;
+    const unsigned long long share = ((a.pf_bytes[i] + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+    const unsigned long long b0 = share * blockIdx.x;
+    const unsigned long long end = min(b0 + share, a.pf_bytes[i]);
+    for (unsigned long long o = b0; o < end; o += 65536)
+      bulk_prefetch_l2(static_cast<const unsigned char*>(a.pf[i]) + o, static_cast<uint32_t>(min(65536ull, end - o)));
+  }
+}
 
 // Destination of pair `pair`'s weighted row.
 __device__ __forceinline__ uint16_t* routed_row(const ExpertsArgs& a, long long pair) {
@@ -591,6 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
       if (!mbar_wait_bounded(&my_bars[kk % kRing], (kk / kRing) & 1, kDrainNs)) break;
     }
   }
+  prefetch_share(a);
   if (a.ep.world > 0) ep_signal(a.ep, kEpFlagDone, a.ep.ticket + 1, a.err);
 }
 
@@ -1018,6 +1037,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1) k_experts_small(const __grid
       if (!mbar_wait_bounded(&full[i % kSmallFull], (i / kSmallFull) & 1, kDrainNs)) break;
     }
   }
+  prefetch_share(a);
 }
 
 }  // namespace
@@ -1051,7 +1071,9 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
   ExpertsArgs a{s.H, s.I, s.Is, s.E, s.K, T, tgp, x, w.gate_up, w.down, w.sh_gate,
                 w.sh_up, w.sh_down, w.ep_world, luts.silu, sc.sched, topk_score, sc.sh_sig, sc.act,
                 sc.act_sh, sc.weighted, sc.gated_sh, sc.up_done, sc.err, sh_x, sh_T,
-                sc.wait_ns, sc.stall, ep != nullptr ? *ep : EpPeers{}};
+                sc.wait_ns, sc.stall, ep != nullptr ? *ep : EpPeers{},
+                {sc.prefetch[0], sc.prefetch[1], sc.prefetch[2]},
+                {sc.prefetch_bytes[0], sc.prefetch_bytes[1], sc.prefetch_bytes[2]}};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -151,6 +151,11 @@ struct Scratch {
   // to make that bounded wait expire).
   unsigned long long wait_ns = 2000000000ull;
   int stall = 0;
+  // Decode forwards: device ranges the expert kernel's CTAs prefetch into L2
+  // when their work is done (the next layer's router rows and shared expert,
+  // which do not depend on its input); null / 0 for none.
+  const void* prefetch[3] = {};
+  unsigned long long prefetch_bytes[3] = {};
 };
 
 // Schedule layout inside Scratch::sched (int32 words), written by the route
