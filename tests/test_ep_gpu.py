@@ -229,13 +229,11 @@ def _stop_main(rank, world, store, transport, wait_s, q):
 
 
 # Over peer memory the dispatch's bounded wait on the silent peer's flag
-# runs out; over NCCL the bounded host-side sync aborts the communicator
-# whose all-gather the peer never joined.
-@pytest.mark.parametrize("transport", [P2P, NCCL])
-def test_ep_peer_stops_between_forwards_fails_closed(transport):
+# runs out and every later kernel of the forward skips its work.
+def test_ep_peer_stops_between_forwards_fails_closed():
     import firewing_b200 as fw
 
     wait_s = 1.0
-    r = _spawn(_stop_main, 2, (transport, wait_s), timeout=180)
+    r = _spawn(_stop_main, 2, (P2P, wait_s), timeout=180)
     assert r["code"] == fw.FW_ETIMEOUT, r
     assert r["elapsed"] < 10 * wait_s, r
