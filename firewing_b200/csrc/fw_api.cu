@@ -1030,7 +1030,8 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   if (prefill && !L.prefill) return fail(FW_EINVAL, "this layer has no prefill tensor maps");
   fw::Scratch scr = h->sc;
   scr.stall = take_stall(h);
-  if (!prefill) prefetch_next(h, layer, &scr);
+  // measured: +1 % at T = 64, neutral at T = 1, -2 % at T = 4
+  if (!prefill && tokens > 4) prefetch_next(h, layer, &scr);
   const cudaError_t e =
       prefill ? fw::launch_prefill(h->shape, L.w, L.maps, h->pf_maps, h->luts, scr, x, tokens, y, idx, sc, cs, ev)
               : fw::launch_block(h->shape, L.w, h->luts, scr, x, tokens, y, idx, sc, cs, ev);

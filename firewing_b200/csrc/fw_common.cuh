@@ -285,12 +285,13 @@ __device__ __forceinline__ unsigned* ep_flag(const EpPeers& p, int owner, int ki
 // Where the weighted row of pair g*K + k goes: row t*K + k of the receive
 // area of the rank that owns token g (rank g / t_local, its token t), in
 // that rank's window.
-__device__ __forceinline__ uint16_t* ep_recv_row(const EpPeers& p, long long pair) {
-  const long long g = pair / p.K;
-  const long long k = pair - g * p.K;
-  const int owner = static_cast<int>(g / p.t_local);
-  const long long t = g - static_cast<long long>(owner) * p.t_local;
-  return reinterpret_cast<uint16_t*>(p.win[owner] + p.off_recv) + (t * p.K + k) * p.H;
+// (pair < world * t_local * K <= 8 * 16384 * 32: 32-bit arithmetic.)
+__device__ __forceinline__ uint16_t* ep_recv_row(const EpPeers& p, int pair) {
+  const int g = pair / p.K;
+  const int k = pair - g * p.K;
+  const int owner = g / p.t_local;
+  const int t = g - owner * p.t_local;
+  return reinterpret_cast<uint16_t*>(p.win[owner] + p.off_recv) + static_cast<size_t>(t * p.K + k) * p.H;
 }
 
 // Called by one thread: wait (bounded by p.wait_ns) until every rank has set

@@ -101,9 +101,12 @@ __device__ __forceinline__ void prefetch_share(const ExpertsArgs& a) {
   }
 }
 
-// Destination of pair `pair`'s weighted row.
-__device__ __forceinline__ uint16_t* routed_row(const ExpertsArgs& a, long long pair) {
-  return a.ep.world > 0 ? ep_recv_row(a.ep, pair) : a.weighted + pair * a.H;
+// Destination of pair `pair`'s weighted row: `weighted`, or under expert
+// parallelism over peer memory (kEp) the owner's window.
+template <bool kEp>
+__device__ __forceinline__ uint16_t* routed_row(const ExpertsArgs& a, int pair) {
+  if constexpr (kEp) return ep_recv_row(a.ep, pair);
+  return a.weighted + static_cast<size_t>(pair) * a.H;
 }
 
 // Per-launch constants, identical in every thread of a CTA.
@@ -328,7 +331,7 @@ __device__ __forceinline__ void stage_fma(const unsigned char* buf, int cols, co
 // Per-pass token table in shared memory: tok_row[t] is the pair id (routed)
 // or token id (shared) of the pass's token t; tok_scale[t] its route weight
 // (routed) or sigmoid gate (shared) as f32.
-template <int NT>
+template <int NT, bool kEp>
 __device__ __forceinline__ void epilogue(const Ctx& c, const Pass& p, int item, int nt, float (&acc)[kMaxTGP][8],
                                          int lane, const int* tok_row, const float* tok_scale) {
   const ExpertsArgs& a = *c.a;
@@ -356,14 +359,14 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const Pass& p, int item, 
         const float d = bf16_to_f32(f32_to_bf16(val[t]));
         // routed: bf16(down * route weight) (src/expert.rs:748-751);
         // shared: bf16(sigmoid * down) (src/expert.rs:1144-1147)
-        uint16_t* dst = routed ? routed_row(a, tok_row[t]) : a.gated_sh + static_cast<size_t>(tok_row[t]) * a.H;
+        uint16_t* dst = routed ? routed_row<kEp>(a, tok_row[t]) : a.gated_sh + static_cast<size_t>(tok_row[t]) * a.H;
         dst[h] = f32_to_bf16(d * tok_scale[t]);
       }
     }
   }
 }
 
-template <int NT, bool kTiled>
+template <int NT, bool kTiled, bool kEp>
 __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, const uint16_t* xs, int xstride,
                                           unsigned char* my_ring, uint64_t* my_bars, Cursor& k, int& consumed,
                                           uint64_t policy, int warp, int lane, int* s_abort, const int* tok_row,
@@ -393,12 +396,12 @@ __device__ __forceinline__ bool run_items(const Ctx& c, const Pass& p, int nt, c
         cursor_next(k, c, warp);
       }
     }
-    epilogue<NT>(c, p, item, nt, acc, lane, tok_row, tok_scale);
+    epilogue<NT, kEp>(c, p, item, nt, acc, lane, tok_row, tok_scale);
   }
   return true;
 }
 
-template <bool kTiled>
+template <bool kTiled, bool kEp>
 __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__ ExpertsArgs a) {
   constexpr int kRing = RingCfg<kTiled>::kRing, kStageBytes = RingCfg<kTiled>::kStageBytes;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -421,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
   pdl_launch_dependents();
   // Under expert parallelism a failed dispatch leaves the schedule stale:
   // compute nothing, but still signal (with the failure) so peers stop waiting.
-  const bool skip = a.ep.world > 0 && ld_volatile_int(a.err) != 0;
+  const bool skip = kEp && ld_volatile_int(a.err) != 0;
 
   Ctx c;
   c.a = &a;
@@ -576,16 +579,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
       __syncthreads();
       bool good;
       if (nt_pad == 1)
-        good = run_items<1, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<1, kTiled, kEp>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       else if (nt_pad == 2)
-        good = run_items<2, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<2, kTiled, kEp>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       else if (nt_pad == 4)
-        good = run_items<4, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<4, kTiled, kEp>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       else
-        good = run_items<8, kTiled>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
+        good = run_items<8, kTiled, kEp>(c, p, nt, xs, kd, my_ring, my_bars, k, consumed, policy, warp, lane, s_abort,
                                tok_row, tok_scale);
       if (!good) {
         aborted = true;
@@ -610,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_experts(const __grid_constant__
     }
   }
   prefetch_share(a);
-  if (a.ep.world > 0) ep_signal(a.ep, kEpFlagDone, a.ep.ticket + 1, a.err);
+  if constexpr (kEp) ep_signal(a.ep, kEpFlagDone, a.ep.ticket + 1, a.err);
 }
 
 // ---- small widths: one producer warp, a CTA-wide ring ----------------------
@@ -751,7 +754,7 @@ __device__ __forceinline__ bool small_unit(const Ctx& c, const Pass& p, int item
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
-  epilogue<NT>(c, p, item, nt, acc, lane, tok_row, tok_scale);
+  epilogue<NT, false>(c, p, item, nt, acc, lane, tok_row, tok_scale);
   return true;
 }
 
@@ -1098,7 +1101,9 @@ cudaError_t launch_experts(const Shape& s, const LayerWeights& w, const Luts& lu
     return cudaLaunchKernelEx(&cfg, k_experts_small, a, R);
   }
   const size_t smem = experts_smem_bytes(s, w.tiled);
-  auto kern = w.tiled ? k_experts<true> : k_experts<false>;
+  const bool ep_peers = ep != nullptr && ep->world > 0;
+  auto kern = w.tiled ? (ep_peers ? k_experts<true, true> : k_experts<true, false>)
+                      : (ep_peers ? k_experts<false, true> : k_experts<false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   cfg.blockDim = dim3(kThreads);
