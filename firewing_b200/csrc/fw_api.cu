@@ -485,8 +485,8 @@ int ep_prefill_forward_p2p(fw_moe* h, const OwnedLayer& L, const uint16_t* x, in
       (e = fw::launch_ep_ids(P, s.E, h->ep_idx_all, h->ep_score_all, h->sc.pair_count, h->sc.err, cs)) !=
           cudaSuccess ||
       (e = fw::launch_prefill_offsets(s, h->sc, count, T_l, cs)) != cudaSuccess ||
-      (e = fw::launch_ep_scatter(P, h->ep_idx_all, h->sc.pair_offset, h->sc.pair_fill, h->sc.pair_tk, h->sc.xg,
-                                 h->sc.pair_cap, h->sc.err, cs)) != cudaSuccess)
+      (e = fw::launch_ep_scatter(P, count, h->ep_idx_all, h->sc.pair_offset, h->sc.pair_fill, h->sc.pair_tk,
+                                 h->sc.xg, h->sc.pair_cap, h->sc.err, cs)) != cudaSuccess)
     return cuda_failed("dispatch launch");
   if ((e = mark(3)) != cudaSuccess) return cuda_failed("event");
   if ((e = fw::launch_prefill_gemms(s, L.maps, h->pf_maps, h->luts, h->sc, x, T_l, count, h->ep_score_all, nullptr,

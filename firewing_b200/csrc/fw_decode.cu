@@ -679,6 +679,111 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
   if (gridDim.x > 1 && threadIdx.x == 0) *a.ticket = 0;  // ready for the next forward
 }
 
+// Route for prefill widths (thousands of tokens): one warp per token, the
+// arithmetic of k_route in the same order -- top-k by (f32 total-order key
+// of the bf16 logit, lower index first), exp in f64 rounded to f32 with the
+// maximum subtracted, the index-order sum of all E terms by one lane from
+// shared memory, selected_sum in top-k order, scores bf16(p / sum) -- so
+// selections and scores are bit-identical to k_route's.  16 tokens per CTA
+// (64 per SM) instead of one CTA per token, and the pair counts are summed
+// per CTA before one global atomic per expert (a hot expert's counter would
+// otherwise take one atomic per token).
+constexpr int kRouteWarps = 16;
+template <int NS>
+__global__ void __launch_bounds__(kRouteWarps * 32) k_route_warp(RouteArgs a) {
+  extern __shared__ __align__(16) float rw_smem[];
+  const int E = a.E, K = a.K, ne = E >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* ex = rw_smem + static_cast<size_t>(warp) * E;                         // [E] this warp's exp terms
+  int* cnt = reinterpret_cast<int*>(rw_smem + static_cast<size_t>(kRouteWarps) * E);  // [E] this CTA's pair counts
+  pdl_wait();
+  pdl_launch_dependents();
+  if (a.pair_count != nullptr)
+    for (int i = threadIdx.x; i < E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int t = blockIdx.x * kRouteWarps + warp;
+  if (t < a.T) {
+    const uint16_t* lr = a.logits + static_cast<size_t>(t) * E;
+    uint32_t key[NS];
+    bool nan = false;
+#pragma unroll
+    for (int i = 0; i < NS; ++i) {
+      key[i] = 0u;
+      if (i < ne) {
+        const int e = lane + 32 * i;
+        const uint32_t b = lr[e];
+        nan |= ((b & 0x7f80u) == 0x7f80u) && ((b & 0x007fu) != 0u);
+        key[i] = (total_key(b) << 16) | static_cast<uint32_t>(0xffff - e);
+      }
+    }
+    if (__any_sync(0xffffffffu, nan)) {
+      // src/decoder_layer.rs:279-281 rejects NaN logits (see k_route)
+      if (lane == 0) set_error(a.err, kErrNanLogits);
+      if (lane < K) {
+        a.idx[static_cast<size_t>(t) * K + lane] = lane;
+        a.score[static_cast<size_t>(t) * K + lane] = 0;
+        if (a.sorted_slot) a.sorted_slot[static_cast<size_t>(t) * K + lane] = lane;
+        if (a.pair_count) atomicAdd(&cnt[lane], 1);
+      }
+      if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = 0;
+    } else {
+      if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = a.sig_lut[a.sh_logit[t]];
+      // top-K: K rounds of a warp max over each lane's best untaken key
+      uint32_t taken = 0u, top = 0u;
+      int mysel = 0;
+      for (int k = 0; k < K; ++k) {
+        uint32_t best = 0u;
+        int bi = -1;
+#pragma unroll
+        for (int i = 0; i < NS; ++i)
+          if (i < ne && !((taken >> i) & 1u) && key[i] > best) {
+            best = key[i];
+            bi = i;
+          }
+        const uint32_t m = __reduce_max_sync(0xffffffffu, best);
+        if (best == m && bi >= 0) taken |= 1u << bi;  // keys are unique: one lane
+        if (k == 0) top = m;
+        if (lane == k) mysel = 0xffff - static_cast<int>(m & 0xffffu);
+      }
+      // softmax with the maximum subtracted (src/decoder_layer.rs:289-297);
+      // exp correctly rounded (f64, then f32)
+      const float maximum = key_value(top);
+#pragma unroll
+      for (int i = 0; i < NS; ++i)
+        if (i < ne) ex[lane + 32 * i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(key_value(key[i]), maximum))));
+      __syncwarp();
+      float den = -0.0f;  // Rust's f32 Sum: -0.0, then index order
+      if (lane == 0) {
+        const float4* ex4 = reinterpret_cast<const float4*>(ex);
+        for (int i = 0; i < (E >> 2); ++i) {
+          const float4 v = ex4[i];
+          den = __fadd_rn(den, v.x);
+          den = __fadd_rn(den, v.y);
+          den = __fadd_rn(den, v.z);
+          den = __fadd_rn(den, v.w);
+        }
+      }
+      den = __shfl_sync(0xffffffffu, den, 0);
+      const float pk = lane < K ? __fdiv_rn(ex[mysel], den) : 0.0f;
+      float ssum = -0.0f;  // selected_sum in top-k order
+      for (int k = 0; k < K; ++k) ssum = __fadd_rn(ssum, __shfl_sync(0xffffffffu, pk, k));
+      int rank = 0;  // slot order by ascending expert id (src/decoder_layer.rs:428-429)
+      for (int k = 0; k < K; ++k) rank += (__shfl_sync(0xffffffffu, mysel, k) < mysel) ? 1 : 0;
+      if (lane < K) {
+        a.idx[static_cast<size_t>(t) * K + lane] = mysel;
+        a.score[static_cast<size_t>(t) * K + lane] = f32_to_bf16(__fdiv_rn(pk, ssum));
+        if (a.sorted_slot != nullptr) a.sorted_slot[static_cast<size_t>(t) * K + rank] = lane;
+        if (a.pair_count != nullptr) atomicAdd(&cnt[mysel], 1);
+      }
+    }
+  }
+  if (a.pair_count == nullptr) return;
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += blockDim.x)
+    if (cnt[i] != 0) atomicAdd(&a.pair_count[i], cnt[i]);
+}
+
+
 // Expert parallelism: the schedule of this GPU's experts over every rank's
 // tokens (a.idx holds the gathered selections), built by one CTA.
 __global__ void __launch_bounds__(1024) k_schedule(RouteArgs a) {
@@ -961,6 +1066,17 @@ cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& 
               sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, schedule ? sc.sched : nullptr, sc.up_done,
               experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket, pair_count, 0, 1, T};
   return launch_route_kernel(a, st);
+}
+
+cudaError_t launch_route_prefill(const Shape& s, const Luts& luts, const Scratch& sc, int T, int32_t* topk_idx,
+                                 uint16_t* topk_score, int* pair_count, cudaStream_t st) {
+  RouteArgs a{sc.logits, T, s.E, s.K, topk_idx, topk_score, sc.err,
+              sc.sh_logit, luts.sigmoid, sc.sh_sig, sc.sorted_slot, nullptr, sc.up_done,
+              experts_tokens_per_pass(s), s.I / 4, s.Is / 4, s.H / 8, sc.ticket, pair_count, 0, 1, T};
+  const size_t smem = sizeof(float) * static_cast<size_t>(kRouteWarps + 1) * s.E;
+  const dim3 grid((T + kRouteWarps - 1) / kRouteWarps), block(kRouteWarps * 32);
+  return s.E <= 512 ? launch_pdl(k_route_warp<16>, grid, block, smem, st, a)
+                    : launch_pdl(k_route_warp<32>, grid, block, smem, st, a);
 }
 
 cudaError_t launch_ep_schedule(const Shape& s, const Scratch& sc, const int32_t* idx_all, int T, int ep_rank,

@@ -320,6 +320,11 @@ cudaError_t launch_router(const Shape& s, const LayerWeights& w, const Scratch& 
                           cudaStream_t st);
 cudaError_t launch_route_block(const Shape& s, const Luts& luts, const Scratch& sc, int T, int32_t* topk_idx,
                                uint16_t* topk_score, bool schedule, int* pair_count, cudaStream_t st);
+// Route of a prefill-width forward: one warp per token, selections and
+// scores bit-identical to launch_route_block's, pair counts added into
+// pair_count (or null); no schedule.
+cudaError_t launch_route_prefill(const Shape& s, const Luts& luts, const Scratch& sc, int T, int32_t* topk_idx,
+                                 uint16_t* topk_score, int* pair_count, cudaStream_t st);
 // ep_idx / ep_world / ep_rows: expert parallelism (rows per source GPU,
 // see CombineArgs); null / 0 / null on one GPU.
 // row_of: explicit row of every (t, k) in ep_rows (expert-parallel prefill).
@@ -389,8 +394,8 @@ cudaError_t launch_ep_ids(const EpPeers& p, int E, int32_t* idx_all, uint16_t* s
                           cudaStream_t st);
 // ... then, after the pair offsets, the grouped input rows, each token row
 // read once from its owner's window.
-cudaError_t launch_ep_scatter(const EpPeers& p, const int32_t* idx_all, const int* offset, int* fill, int32_t* pair_tk,
-                              uint16_t* xg, long long xg_rows, int* err, cudaStream_t st);
+cudaError_t launch_ep_scatter(const EpPeers& p, int banks, const int32_t* idx_all, const int* offset, int* fill,
+                              int32_t* pair_tk, uint16_t* xg, long long xg_rows, int* err, cudaStream_t st);
 
 // Store a failure message for fw_last_error() (fixed buffer, no allocation);
 // returns `code`.

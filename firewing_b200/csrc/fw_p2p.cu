@@ -456,26 +456,44 @@ __global__ void __launch_bounds__(256) k_ep_ids(EpPeers p, int E, int32_t* idx_a
 // the gathered index space, gives each of its pairs with one of this rank's
 // experts a slot in that expert's group, and copies the token's row once
 // from its owner's window into every slot's row of the grouped input xg
-// (K-blocked, [H/64][xg_rows][64]).
-__global__ void __launch_bounds__(256) k_ep_scatter(EpPeers p, const int32_t* idx_all, const int* offset, int* fill,
-                                                    int32_t* pair_tk, uint16_t* xg, long long xg_rows, int* err) {
+// (K-blocked, [H/64][xg_rows][64]).  Slots are counted per CTA in shared
+// memory and each expert's range reserved with one global atomic per CTA
+// (a hot expert draws pairs from every rank's tokens).
+__global__ void __launch_bounds__(256) k_ep_scatter(EpPeers p, int banks, const int32_t* idx_all, const int* offset,
+                                                    int* fill, int32_t* pair_tk, uint16_t* xg, long long xg_rows,
+                                                    int* err) {
+  extern __shared__ int s_cnt[];  // [banks]: this CTA's pairs per bank, then their base in the group
   pdl_wait();
   pdl_launch_dependents();
-  if (ld_volatile_int(err) != 0) return;
+  __shared__ int s_bad;
   const int lane = threadIdx.x & 31;
   const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (g >= p.world * p.t_local) return;
-  int slot = -1;
-  if (lane < p.K) {
+  const bool live = g < p.world * p.t_local;
+  if (threadIdx.x == 0) s_bad = ld_volatile_int(err);
+  for (int i = threadIdx.x; i < banks; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  if (s_bad != 0) return;  // one read per CTA: the whole CTA leaves together
+  int bank = -1, lr = 0;
+  if (live && lane < p.K) {
     const int e = idx_all[static_cast<size_t>(g) * p.K + lane];
     if (e % p.world == p.rank) {
-      const int b = e / p.world;
-      slot = offset[b] + atomicAdd(&fill[b], 1);
-      pair_tk[slot] = g * p.K + lane;
+      bank = e / p.world;
+      lr = atomicAdd(&s_cnt[bank], 1);
     }
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < banks; i += blockDim.x) {
+    const int c = s_cnt[i];
+    if (c > 0) s_cnt[i] = atomicAdd(&fill[i], c);
+  }
+  __syncthreads();
+  int slot = -1;
+  if (bank >= 0) {
+    slot = offset[bank] + s_cnt[bank] + lr;
+    pair_tk[slot] = g * p.K + lane;
+  }
   const unsigned have = __ballot_sync(0xffffffffu, slot >= 0);
-  if (have == 0) return;
+  if (!live || have == 0) return;
   const int src = g / p.t_local, t = g - src * p.t_local;
   const uint4* sx = reinterpret_cast<const uint4*>(p.win[src] + p.off_x) + static_cast<size_t>(t) * (p.H / 8);
   const int nch = p.H / 8;
@@ -539,11 +557,20 @@ cudaError_t launch_ep_ids(const EpPeers& p, int E, int32_t* idx_all, uint16_t* s
   return launch_pdl(k_ep_ids, dim3(grid_for(n, 256, 8 * 148)), dim3(256), st, p, E, idx_all, score_all, count, err);
 }
 
-cudaError_t launch_ep_scatter(const EpPeers& p, const int32_t* idx_all, const int* offset, int* fill, int32_t* pair_tk,
-                              uint16_t* xg, long long xg_rows, int* err, cudaStream_t st) {
+cudaError_t launch_ep_scatter(const EpPeers& p, int banks, const int32_t* idx_all, const int* offset, int* fill,
+                              int32_t* pair_tk, uint16_t* xg, long long xg_rows, int* err, cudaStream_t st) {
   const int tokens = p.world * p.t_local;
-  return launch_pdl(k_ep_scatter, dim3((tokens + 7) / 8), dim3(256), st, p, idx_all, offset, fill, pair_tk, xg,
-                    xg_rows, err);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((tokens + 7) / 8);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = sizeof(int) * static_cast<size_t>(banks);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_ep_scatter, p, banks, idx_all, offset, fill, pair_tk, xg, xg_rows, err);
 }
 
 }  // namespace fw

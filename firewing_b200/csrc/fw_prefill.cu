@@ -1062,40 +1062,77 @@ __global__ void k_pf_offsets(OffsetsArgs a) {
   }
 }
 
-// One warp per (token, top-k position): its slot in its expert's group, and
-// a copy of the token's input row into the grouped input (so the gate/up
-// GEMM reads each expert's token rows of a 64-column block as one
-// contiguous run).
-// Only pairs whose expert e has e % world == rank are grouped (this GPU's
-// experts under expert parallelism; all of them otherwise); the slot is the
-// bank index e / world.
-__global__ void k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H, int rank, int world,
-                             const int* offset, int* fill, int32_t* pair_tk, const uint16_t* x, uint16_t* xg,
-                             long long xg_rows, int* err) {
+// Pairs grouped by expert: every (token, top-k position) whose expert e has
+// e % world == rank (this GPU's experts under expert parallelism; all of
+// them otherwise) gets a slot in its expert's group (bank e / world), and the
+// token's input row is copied to that slot of the grouped input, so the
+// gate/up GEMM reads each expert's token rows of a 64-column block as one
+// contiguous run.  One warp per token: lane k takes top-k position k, and
+// the row is read once and stored to each of the token's slots.  A CTA
+// counts its pairs per expert in shared memory and reserves each expert's
+// range with one global atomic (under a skewed router thousands of pairs
+// select one expert).
+constexpr int kScatterTokens = 8;
+size_t scatter_smem(int banks) { return sizeof(int) * static_cast<size_t>(banks); }
+
+__global__ void __launch_bounds__(kScatterTokens * 32) k_pf_scatter(const int32_t* idx, int TK, int K, int E, int H,
+                                                                    int rank, int world, const int* offset, int* fill,
+                                                                    int32_t* pair_tk, const uint16_t* x, uint16_t* xg,
+                                                                    long long xg_rows, int* err) {
+  extern __shared__ int s_cnt[];  // [E / world]: this CTA's pairs per bank, then their base in the group
+  const int nb = E / world;
   pdl_wait();
   pdl_launch_dependents();
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (i >= TK) return;
-  int p = 0;
-  if (lane == 0) {
-    const int e = idx[i];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kScatterTokens + warp;
+  const bool live = t < TK / K;
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  int bank = -1, lr = 0;
+  if (live && lane < K) {
+    const int e = idx[t * K + lane];
     if (e < 0 || e >= E) {
       set_error(err, kErrBadIndex);
-      p = -1;
-    } else if (e % world != rank) {
-      p = -1;  // another GPU's expert
-    } else {
-      p = offset[e / world] + atomicAdd(&fill[e / world], 1);
-      pair_tk[p] = i;
+    } else if (e % world == rank) {
+      bank = e / world;
+      lr = atomicAdd(&s_cnt[bank], 1);
     }
   }
-  p = __shfl_sync(0xffffffffu, p, 0);
-  if (p < 0) return;
+  __syncthreads();
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    const int c = s_cnt[i];
+    if (c > 0) s_cnt[i] = atomicAdd(&fill[i], c);
+  }
+  __syncthreads();
+  int slot = -1;
+  if (bank >= 0) {
+    slot = offset[bank] + s_cnt[bank] + lr;
+    pair_tk[slot] = t * K + lane;
+  }
+  const unsigned have = __ballot_sync(0xffffffffu, slot >= 0);
+  if (!live || have == 0) return;
   // xg is K-blocked, [H/64][xg_rows][64]: 16-byte chunk c of the row goes
-  // to block c / 8, row p, chunk c % 8.
-  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(i / K) * H);
-  for (int c = lane; c < H / 8; c += 32)
-    *reinterpret_cast<uint4*>(xg + ((static_cast<size_t>(c >> 3) * xg_rows + p) * 64 + (c & 7) * 8)) = src[c];
+  // to block c / 8, row slot, chunk c % 8.  Eight chunks in flight per lane.
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H);
+  const int nch = H / 8;
+  for (int c0 = lane; c0 < nch; c0 += 8 * 32) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (c0 + 32 * u < nch) v[u] = src[c0 + 32 * u];
+    unsigned rest = have;
+    while (rest != 0) {
+      const int k = __ffs(rest) - 1;
+      rest &= rest - 1;
+      const long long row = __shfl_sync(0xffffffffu, slot, k);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + 32 * u;
+        if (c < nch)
+          *reinterpret_cast<uint4*>(xg + ((static_cast<long long>(c >> 3) * xg_rows + row) * 64 + (c & 7) * 8)) = v[u];
+      }
+    }
+  }
 }
 
 // Expert parallelism: per-expert pair counts of this GPU's experts over
@@ -1329,7 +1366,7 @@ cudaError_t launch_prefill_front(const Shape& s, const LayerWeights& w, const Pr
                          s.E, s.H, T, s.K};
   if ((e = launch_router_fix(fa, st)) != cudaSuccess) return e;
   if (mid != nullptr && (e = cudaEventRecord(mid, st)) != cudaSuccess) return e;
-  return launch_route_block(s, luts, sc, T, topk_idx, topk_score, false, count_pairs ? sc.pair_count : nullptr, st);
+  return launch_route_prefill(s, luts, sc, T, topk_idx, topk_score, count_pairs ? sc.pair_count : nullptr, st);
 }
 
 cudaError_t launch_prefill_offsets(const Shape& s, const Scratch& sc, int ecount, int sh_T, cudaStream_t st) {
@@ -1351,7 +1388,10 @@ cudaError_t launch_prefill_group(const Shape& s, const Scratch& sc, const int32_
       return e;
   }
   if ((e = launch_prefill_offsets(s, sc, ecount, sh_T, st)) != cudaSuccess) return e;
-  return launch_pdl_ex(k_pf_scatter, dim3((n_pairs + 7) / 8), dim3(256), 0, st, idx, n_pairs, s.K, s.E, s.H, ep_rank,
+  if (s.K > 32) return cudaErrorInvalidValue;
+  const int tokens = (n_pairs + s.K - 1) / s.K;
+  return launch_pdl_ex(k_pf_scatter, dim3((tokens + kScatterTokens - 1) / kScatterTokens), dim3(kScatterTokens * 32),
+                       scatter_smem(ecount), st, idx, n_pairs, s.K, s.E, s.H, ep_rank,
                        ep_world, static_cast<const int*>(sc.pair_offset), sc.pair_fill, sc.pair_tk, x_src, sc.xg,
                        static_cast<long long>(sc.pair_cap), sc.err);
 }
