@@ -14,6 +14,7 @@
 // 4 lanes, each walking the 32-column blocks in order, then reduced with the
 // reference tree (fw::reduce_partials).  Rows are streamed once per CTA with
 // 16-byte read-only loads; activations sit in shared memory as f32.
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 
@@ -282,7 +283,7 @@ __device__ __forceinline__ void cp_async16_dec(void* dst, const void* src) {
 }
 
 template <int TT, int RW>
-__global__ void __launch_bounds__(kPmWarps * 32) k_router_pm(RouterArgs a) {
+__device__ __forceinline__ void router_pm_body(const RouterArgs& a) {
   constexpr int kPmRows = kPmWarps * RW;
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -361,6 +362,11 @@ __global__ void __launch_bounds__(kPmWarps * 32) k_router_pm(RouterArgs a) {
       }
     }
   }
+}
+
+template <int TT, int RW>
+__global__ void __launch_bounds__(kPmWarps * 32) k_router_pm(RouterArgs a) {
+  router_pm_body<TT, RW>(a);
 }
 
 // ---------------------------------------------------------------------------
@@ -528,6 +534,41 @@ __device__ void build_schedule(const RouteArgs& a, unsigned char* smem) {
   }
 }
 
+// One token on one GPU: the schedule follows from the K selected ids alone
+// (each slot holds one pair), so one warp writes the same words
+// build_schedule would, without its block-wide scans over E experts: slot =
+// rank of the id among the selection, pair = its top-k position, every slot
+// (and the shared expert's) costing one 1-token pass.  `my` is lane k's
+// selected id (k < K).
+__device__ void single_token_schedule(const RouteArgs& a, int my, int lane) {
+  const int E = a.E, Kk = a.K;
+  int32_t* active = a.sched + 1;
+  int32_t* offsets = a.sched + 1 + E;
+  int32_t* pairs = a.sched + 2 + 2 * E;
+  int32_t* up_pref = pairs + Kk;
+  int32_t* dn_pref = up_pref + E + 2;
+  int rank = 0;
+  for (int k = 0; k < Kk; ++k) rank += (__shfl_sync(0xffffffffu, my, k) < my) ? 1 : 0;
+  // a 1-token pass: 4 + pad(1) up, 4 + 4 pad(1) down (as build_schedule)
+  const int cu = 5 * a.qpr, cd = 8 * a.ops;
+  if (lane < Kk) {
+    active[rank] = my;
+    offsets[rank] = rank;
+    pairs[rank] = lane;
+    up_pref[rank] = rank * cu;
+    dn_pref[rank] = rank * cd;
+  }
+  if (lane == 0) {
+    a.sched[0] = Kk;
+    offsets[Kk] = Kk;
+    up_pref[Kk] = Kk * cu;
+    up_pref[Kk + 1] = Kk * cu + 5 * a.qps;
+    dn_pref[Kk] = Kk * cd;
+    dn_pref[Kk + 1] = Kk * cd + cd;
+  }
+  for (int i = lane; i <= Kk; i += 32) a.up_done[i] = 0;
+}
+
 __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int E = a.E, K = a.K;
@@ -625,40 +666,7 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
   }
   if (a.sched == nullptr) return;
   if (a.T == 1 && a.ep_world == 1) {
-    // One token on one GPU: the schedule follows from the K selected ids
-    // alone (each slot holds one pair), so warp 0 writes the same words
-    // build_schedule would, without its block-wide scans over E experts:
-    // slot = rank of the id among the selection, pair = its top-k position,
-    // every slot (and the shared expert's) costing one 1-token pass.
-    if (warp == 0) {
-      const int Kk = a.K;
-      int32_t* active = a.sched + 1;
-      int32_t* offsets = a.sched + 1 + E;
-      int32_t* pairs = a.sched + 2 + 2 * E;
-      int32_t* up_pref = pairs + Kk;
-      int32_t* dn_pref = up_pref + E + 2;
-      const int my = lane < Kk ? a.idx[lane] : 0;  // this lane's own write above
-      int rank = 0;
-      for (int k = 0; k < Kk; ++k) rank += (__shfl_sync(0xffffffffu, my, k) < my) ? 1 : 0;
-      // a 1-token pass: 4 + pad(1) up, 4 + 4 pad(1) down (as build_schedule)
-      const int cu = 5 * a.qpr, cd = 8 * a.ops;
-      if (lane < Kk) {
-        active[rank] = my;
-        offsets[rank] = rank;
-        pairs[rank] = lane;
-        up_pref[rank] = rank * cu;
-        dn_pref[rank] = rank * cd;
-      }
-      if (lane == 0) {
-        a.sched[0] = Kk;
-        offsets[Kk] = Kk;
-        up_pref[Kk] = Kk * cu;
-        up_pref[Kk + 1] = Kk * cu + 5 * a.qps;
-        dn_pref[Kk] = Kk * cd;
-        dn_pref[Kk + 1] = Kk * cd + cd;
-      }
-      for (int i = lane; i <= Kk; i += 32) a.up_done[i] = 0;
-    }
+    if (warp == 0) single_token_schedule(a, lane < a.K ? a.idx[lane] : 0, lane);  // this lane's own write above
     return;
   }
   // The last CTA to finish builds the schedule from every token's selection
@@ -679,22 +687,103 @@ __global__ void __launch_bounds__(1024) k_route(RouteArgs a) {
   if (gridDim.x > 1 && threadIdx.x == 0) *a.ticket = 0;  // ready for the next forward
 }
 
-// Route for prefill widths (thousands of tokens): one warp per token, the
-// arithmetic of k_route in the same order -- top-k by (f32 total-order key
-// of the bf16 logit, lower index first), exp in f64 rounded to f32 with the
-// maximum subtracted, the index-order sum of all E terms by one lane from
-// shared memory, selected_sum in top-k order, scores bf16(p / sum) -- so
-// selections and scores are bit-identical to k_route's.  16 tokens per CTA
-// (64 per SM) instead of one CTA per token, and the pair counts are summed
-// per CTA before one global atomic per expert (a hot expert's counter would
-// otherwise take one atomic per token).
 constexpr int kRouteWarps = 16;
+
+// Route of token t by one warp (the arithmetic of k_route, in its order):
+// writes idx / score / sorted_slot / sh_sig for t, adds its selections into
+// cnt (shared memory, or null), and returns lane k's selected id (k < K).
+// ex: E floats of this warp's shared memory.  Logit loads bypass L1 (the
+// fused router writes them from other SMs).
+template <int NS>
+__device__ __forceinline__ int route_warp_token(const RouteArgs& a, int t, float* ex, int* cnt, int lane) {
+  const int E = a.E, K = a.K, ne = E >> 5;
+  const uint16_t* lr = a.logits + static_cast<size_t>(t) * E;
+  uint32_t key[NS];
+  bool nan = false;
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    key[i] = 0u;
+    if (i < ne) {
+      const int e = lane + 32 * i;
+      const uint32_t b = __ldcg(lr + e);
+      nan |= ((b & 0x7f80u) == 0x7f80u) && ((b & 0x007fu) != 0u);
+      key[i] = (total_key(b) << 16) | static_cast<uint32_t>(0xffff - e);
+    }
+  }
+  if (__any_sync(0xffffffffu, nan)) {
+    // src/decoder_layer.rs:279-281 rejects NaN logits (see k_route)
+    if (lane == 0) set_error(a.err, kErrNanLogits);
+    if (lane < K) {
+      a.idx[static_cast<size_t>(t) * K + lane] = lane;
+      a.score[static_cast<size_t>(t) * K + lane] = 0;
+      if (a.sorted_slot) a.sorted_slot[static_cast<size_t>(t) * K + lane] = lane;
+      if (cnt != nullptr) atomicAdd(&cnt[lane], 1);
+    }
+    if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = 0;
+    return lane < K ? lane : 0;
+  }
+  if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = a.sig_lut[__ldcg(a.sh_logit + t)];
+  // top-K: K rounds of a warp max over each lane's best untaken key
+  uint32_t taken = 0u, top = 0u;
+  int mysel = 0;
+  for (int k = 0; k < K; ++k) {
+    uint32_t best = 0u;
+    int bi = -1;
+#pragma unroll
+    for (int i = 0; i < NS; ++i)
+      if (i < ne && !((taken >> i) & 1u) && key[i] > best) {
+        best = key[i];
+        bi = i;
+      }
+    const uint32_t m = __reduce_max_sync(0xffffffffu, best);
+    if (best == m && bi >= 0) taken |= 1u << bi;  // keys are unique: one lane
+    if (k == 0) top = m;
+    if (lane == k) mysel = 0xffff - static_cast<int>(m & 0xffffu);
+  }
+  // softmax with the maximum subtracted (src/decoder_layer.rs:289-297);
+  // exp correctly rounded (f64, then f32)
+  const float maximum = key_value(top);
+#pragma unroll
+  for (int i = 0; i < NS; ++i)
+    if (i < ne) ex[lane + 32 * i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(key_value(key[i]), maximum))));
+  __syncwarp();
+  float den = -0.0f;  // Rust's f32 Sum: -0.0, then index order
+  if (lane == 0) {
+    const float4* ex4 = reinterpret_cast<const float4*>(ex);
+    for (int i = 0; i < (E >> 2); ++i) {
+      const float4 v = ex4[i];
+      den = __fadd_rn(den, v.x);
+      den = __fadd_rn(den, v.y);
+      den = __fadd_rn(den, v.z);
+      den = __fadd_rn(den, v.w);
+    }
+  }
+  den = __shfl_sync(0xffffffffu, den, 0);
+  const float pk = lane < K ? __fdiv_rn(ex[mysel], den) : 0.0f;
+  float ssum = -0.0f;  // selected_sum in top-k order
+  for (int k = 0; k < K; ++k) ssum = __fadd_rn(ssum, __shfl_sync(0xffffffffu, pk, k));
+  int rank = 0;  // slot order by ascending expert id (src/decoder_layer.rs:428-429)
+  for (int k = 0; k < K; ++k) rank += (__shfl_sync(0xffffffffu, mysel, k) < mysel) ? 1 : 0;
+  if (lane < K) {
+    a.idx[static_cast<size_t>(t) * K + lane] = mysel;
+    a.score[static_cast<size_t>(t) * K + lane] = f32_to_bf16(__fdiv_rn(pk, ssum));
+    if (a.sorted_slot != nullptr) a.sorted_slot[static_cast<size_t>(t) * K + rank] = lane;
+    if (cnt != nullptr) atomicAdd(&cnt[mysel], 1);
+  }
+  return mysel;
+}
+
+// Route for prefill widths (thousands of tokens): one warp per token
+// (route_warp_token), so selections and scores are bit-identical to
+// k_route's.  16 tokens per CTA instead of one CTA per token, and the pair
+// counts are summed per CTA before one global atomic per expert (a hot
+// expert's counter would otherwise take one atomic per token).
 template <int NS>
 __global__ void __launch_bounds__(kRouteWarps * 32) k_route_warp(RouteArgs a) {
   extern __shared__ __align__(16) float rw_smem[];
-  const int E = a.E, K = a.K, ne = E >> 5;
+  const int E = a.E;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* ex = rw_smem + static_cast<size_t>(warp) * E;                         // [E] this warp's exp terms
+  float* ex = rw_smem + static_cast<size_t>(warp) * E;                                // [E] this warp's exp terms
   int* cnt = reinterpret_cast<int*>(rw_smem + static_cast<size_t>(kRouteWarps) * E);  // [E] this CTA's pair counts
   pdl_wait();
   pdl_launch_dependents();
@@ -702,86 +791,13 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_warp(RouteArgs a) {
     for (int i = threadIdx.x; i < E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
   const int t = blockIdx.x * kRouteWarps + warp;
-  if (t < a.T) {
-    const uint16_t* lr = a.logits + static_cast<size_t>(t) * E;
-    uint32_t key[NS];
-    bool nan = false;
-#pragma unroll
-    for (int i = 0; i < NS; ++i) {
-      key[i] = 0u;
-      if (i < ne) {
-        const int e = lane + 32 * i;
-        const uint32_t b = lr[e];
-        nan |= ((b & 0x7f80u) == 0x7f80u) && ((b & 0x007fu) != 0u);
-        key[i] = (total_key(b) << 16) | static_cast<uint32_t>(0xffff - e);
-      }
-    }
-    if (__any_sync(0xffffffffu, nan)) {
-      // src/decoder_layer.rs:279-281 rejects NaN logits (see k_route)
-      if (lane == 0) set_error(a.err, kErrNanLogits);
-      if (lane < K) {
-        a.idx[static_cast<size_t>(t) * K + lane] = lane;
-        a.score[static_cast<size_t>(t) * K + lane] = 0;
-        if (a.sorted_slot) a.sorted_slot[static_cast<size_t>(t) * K + lane] = lane;
-        if (a.pair_count) atomicAdd(&cnt[lane], 1);
-      }
-      if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = 0;
-    } else {
-      if (a.sh_sig != nullptr && lane == 0) a.sh_sig[t] = a.sig_lut[a.sh_logit[t]];
-      // top-K: K rounds of a warp max over each lane's best untaken key
-      uint32_t taken = 0u, top = 0u;
-      int mysel = 0;
-      for (int k = 0; k < K; ++k) {
-        uint32_t best = 0u;
-        int bi = -1;
-#pragma unroll
-        for (int i = 0; i < NS; ++i)
-          if (i < ne && !((taken >> i) & 1u) && key[i] > best) {
-            best = key[i];
-            bi = i;
-          }
-        const uint32_t m = __reduce_max_sync(0xffffffffu, best);
-        if (best == m && bi >= 0) taken |= 1u << bi;  // keys are unique: one lane
-        if (k == 0) top = m;
-        if (lane == k) mysel = 0xffff - static_cast<int>(m & 0xffffu);
-      }
-      // softmax with the maximum subtracted (src/decoder_layer.rs:289-297);
-      // exp correctly rounded (f64, then f32)
-      const float maximum = key_value(top);
-#pragma unroll
-      for (int i = 0; i < NS; ++i)
-        if (i < ne) ex[lane + 32 * i] = static_cast<float>(exp(static_cast<double>(__fsub_rn(key_value(key[i]), maximum))));
-      __syncwarp();
-      float den = -0.0f;  // Rust's f32 Sum: -0.0, then index order
-      if (lane == 0) {
-        const float4* ex4 = reinterpret_cast<const float4*>(ex);
-        for (int i = 0; i < (E >> 2); ++i) {
-          const float4 v = ex4[i];
-          den = __fadd_rn(den, v.x);
-          den = __fadd_rn(den, v.y);
-          den = __fadd_rn(den, v.z);
-          den = __fadd_rn(den, v.w);
-        }
-      }
-      den = __shfl_sync(0xffffffffu, den, 0);
-      const float pk = lane < K ? __fdiv_rn(ex[mysel], den) : 0.0f;
-      float ssum = -0.0f;  // selected_sum in top-k order
-      for (int k = 0; k < K; ++k) ssum = __fadd_rn(ssum, __shfl_sync(0xffffffffu, pk, k));
-      int rank = 0;  // slot order by ascending expert id (src/decoder_layer.rs:428-429)
-      for (int k = 0; k < K; ++k) rank += (__shfl_sync(0xffffffffu, mysel, k) < mysel) ? 1 : 0;
-      if (lane < K) {
-        a.idx[static_cast<size_t>(t) * K + lane] = mysel;
-        a.score[static_cast<size_t>(t) * K + lane] = f32_to_bf16(__fdiv_rn(pk, ssum));
-        if (a.sorted_slot != nullptr) a.sorted_slot[static_cast<size_t>(t) * K + rank] = lane;
-        if (a.pair_count != nullptr) atomicAdd(&cnt[mysel], 1);
-      }
-    }
-  }
+  if (t < a.T) route_warp_token<NS>(a, t, ex, a.pair_count != nullptr ? cnt : nullptr, lane);
   if (a.pair_count == nullptr) return;
   __syncthreads();
   for (int i = threadIdx.x; i < E; i += blockDim.x)
     if (cnt[i] != 0) atomicAdd(&a.pair_count[i], cnt[i]);
 }
+
 
 
 // Expert parallelism: the schedule of this GPU's experts over every rank's
