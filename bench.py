@@ -397,6 +397,10 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     sampler = ClockSampler(local_rank)
     el = timed(T, bufs, args.steps, args.warmup, sampler)
     clocks = sampler.summary()
+    # decode (bit-exact CUDA-core path) or prefill (tensor cores): at N > 1
+    # the width that decides is the total over the ranks (N x T)
+    path_T = blk.last_path()
+    decode_path = path_T == fw.PATH_DECODE
     if args.minimal:
         if rank == 0:
             print(json.dumps({"metric": METRIC, "value": world * T * L * args.steps / el,
@@ -447,7 +451,8 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
     stage_ranks = gather_to_rank0(dist, world, stage_ms)
     roofline = {"bound": "hbm", "achieved": up_gbs, "peak": hbm_peak, "unit": "GB/s",
                 "frac": up_gbs / hbm_peak, "traffic": traffic,
-                "kernel": "k_experts (gate_up + SwiGLU and down + scale, persistent)",
+                "kernel": "k_experts (gate_up + SwiGLU and down + scale, persistent)" if decode_path else
+                          "k_gemm (tcgen05 grouped GEMMs: gate/up + SwiGLU, down + route weight; weight-streaming)",
                 "peak_source": f"{peak_src} hbm_gbs",
                 "stage_ms_per_layer": stage_ms}
     if world > 1 and rank == 0:
@@ -519,7 +524,8 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
             ys = np.concatenate([everyone[r][j][2] for r in range(world)])
             ids = np.concatenate([everyone[r][j][3] for r in range(world)])
             scs = np.concatenate([everyone[r][j][4] for r in range(world)])
-            parity["layers"][str(l)] = parity_rows(w, layer_seed(l), w["zipf"], xs, ys, ids, scs, exact=True)
+            parity["layers"][str(l)] = parity_rows(w, layer_seed(l), w["zipf"], xs, ys, ids, scs,
+                                                   exact=decode_path)
         parity["pass"] = all(v["pass"] for v in parity["layers"].values())
         parity["tokens_per_rank"] = int(rows.size)
     barrier()
@@ -538,7 +544,12 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
         cpu = cpu_baseline(w, os.cpu_count() or 1, budget_s=args.cpu_budget, rank=rank)
 
     if rank == 0:
-        launches = (4 if world == 1 else 5) * L * args.steps
+        # this library's kernels per layer: decode router, route, experts,
+        # combine (+ the peer publish at N > 1); prefill router logits,
+        # repair, route, offsets, scatter, two GEMMs, combine (+ publish,
+        # gathered ids and the done wait at N > 1)
+        per_layer = (4 if world == 1 else 5) if decode_path else (8 if world == 1 else 11)
+        launches = per_layer * L * args.steps
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
@@ -550,6 +561,8 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
                        "experts": E, "top_k": K, "intermediate": w["intermediate"],
                        "shared_intermediate": w["shared_intermediate"],
                        "parallelism": f"ep{world}" if world > 1 else "single",
+                       "path": "decode (CUDA-core dot products in the reference's order, bit-exact)" if decode_path
+                               else "prefill (tcgen05 grouped GEMMs: N x T tokens over the ranks >= 192)",
                        "l2": "no flush: every layer streams >126 MB of distinct weights",
                        "distinct_experts_per_layer_mean_this_gpu": float(np.mean(unique))},
             "stack_tokens_per_s": world * T * args.steps / el,
@@ -766,6 +779,7 @@ def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, bar
     e1.synchronize()
     blk.sync(stream)
     el = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    decode_path = blk.last_path() == fw.PATH_DECODE
     # this rank's distinct local experts per layer (from every rank's picks)
     ids = idx.cpu().numpy()
     t_ids = torch.from_numpy(ids.astype(np.int32)).cuda()
@@ -786,7 +800,7 @@ def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, bar
     parity = None
     if rank == 0 and not args.no_cpu:
         parity = parity_rows(p, layer_seed(0), False, *[np.concatenate([e[i] for e in everyone]) for i in range(4)],
-                             exact=True)
+                             exact=decode_path)
         parity["layer"] = 0
     barrier()
     return {
@@ -795,6 +809,7 @@ def measure_ep(args, rank, world, local_rank, peaks, stream, max_over_ranks, bar
         "value": T_l * world * L * steps / el, "unit": UNIT, "ms_per_step": el / steps * 1e3,
         "per_gpu_gbs_min": gbs, "per_gpu_frac_hbm_min": gbs / hbm_peak,
         "parallelism": f"ep{world} (experts {E // world} per GPU) + dp tokens",
+        "path": "decode (bit-exact)" if decode_path else "prefill (tcgen05 grouped GEMMs)",
         "stage_ms_per_layer_by_rank": stages,
         "parity_sample": parity,
         "exchange": "NVLink peer memory: rows pulled once per destination GPU, weighted rows stored by the expert kernel into the owner's window, bounded flag waits",

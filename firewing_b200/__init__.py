@@ -16,6 +16,8 @@ from .moe import (  # noqa: F401
     FW_ENOMEM,
     FW_ETIMEOUT,
     FW_OK,
+    PATH_DECODE,
+    PATH_PREFILL,
     FwError,
     MoeBlock,
     MoeConfig,

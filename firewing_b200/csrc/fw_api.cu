@@ -158,6 +158,17 @@ int record_error(int code, const char* msg) { return fail(code, msg); }
 
 // Widest forward the decode kernels take; wider ones use the prefill path.
 constexpr int kDecodeMaxTokens = 256;
+// Default width from which a shape with a prefill path takes it.  Measured on
+// one B200 at config 0 (8 layers, uniform router, token-layers/s decode ->
+// tensor-core path): T = 64: 165 k -> 154 k; T = 96: 199 k -> 205 k;
+// T = 128: 221 k -> 254 k; T = 192: 250 k -> 360 k; T = 256: 272 k -> 468 k.
+// Two tokens per expert (T * K / E) is where the CUDA-core dot products stop
+// hiding under the weight stream.
+constexpr int kPrefillDefaultMin = 96;
+// Under expert parallelism the default counts every rank's tokens and starts
+// at 192 in total (about four tokens per held expert, +44 % on one GPU at
+// T = 192): the prefill exchange takes more launches than the decode one.
+constexpr int kEpPrefillDefaultMin = 192;
 constexpr int kMaxTokens = 16384;
 
 struct fw_moe {
@@ -181,6 +192,7 @@ struct fw_moe {
   bool prefill_ok = false;            // shape supported and scratch maps built
   fw::PrefillScratchMaps pf_maps{};
   int prefill_min_tokens = kDecodeMaxTokens + 1;  // forwards this wide or wider take the prefill path
+  bool prefill_min_set = false;                   // set by fw_moe_set_prefill_min_tokens
   // The last forward (fw_moe_last_union): 0 none, 1 decode (expert schedule),
   // 2 prefill (grouped pair offsets over `last_experts` bank experts).
   int last_path = 0, last_experts = 0;
@@ -503,7 +515,11 @@ int ep_prefill_forward_p2p(fw_moe* h, const OwnedLayer& L, const uint16_t* x, in
 // Whole block under expert parallelism (either transport, either path).
 int ep_block(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_t* y, int32_t* idx, uint16_t* score,
              cudaStream_t cs, cudaEvent_t* ev, const fw::HcPost* hc, bool* prefill) {
-  *prefill = T_l > h->ep_decode_max || T_l >= h->prefill_min_tokens;
+  // The experts of a rank see every rank's tokens: the width that decides
+  // the path is the total over the ranks.
+  const int min_total =
+      h->prefill_min_set || !h->prefill_ok ? h->prefill_min_tokens : kEpPrefillDefaultMin;
+  *prefill = T_l > h->ep_decode_max || (L.prefill && static_cast<int64_t>(T_l) * h->ep_world >= min_total);
   if (*prefill && !L.prefill) return fail(FW_EINVAL, "this many tokens need the prefill path, which this handle's shape lacks");
   if (h->p2p != nullptr)
     return *prefill ? ep_prefill_forward_p2p(h, L, x, T_l, y, idx, score, cs, ev, hc)
@@ -698,6 +714,7 @@ int fw_moe_create(const fw_moe_config* config, int device, fw_moe** out) {
       break;
     }
     h->prefill_ok = fw::prefill_supported(h->shape) && fw::make_prefill_scratch_maps(h->shape, s, &h->pf_maps);
+    if (h->prefill_ok) h->prefill_min_tokens = kPrefillDefaultMin;
     if (M > kDecodeMaxTokens && !h->prefill_ok) {
       rc = fail(FW_ECUDA, "prefill tensor maps could not be encoded");
       break;
@@ -1040,6 +1057,13 @@ int fw_moe_forward_async(fw_moe* h, int32_t layer, const uint16_t* x, int32_t to
   return FW_OK;
 }
 
+int fw_moe_last_path(fw_moe* h, int32_t* path) {
+  if (h == nullptr || path == nullptr) return fail(FW_EINVAL, "null argument");
+  if (h->last_path == 0) return fail(FW_EINVAL, "no forward has run on this handle");
+  *path = h->last_path == 2 ? FW_PATH_PREFILL : FW_PATH_DECODE;
+  return FW_OK;
+}
+
 int fw_moe_last_union(fw_moe* h, int32_t* distinct_experts, uint64_t* weight_bytes) {
   if (h == nullptr || distinct_experts == nullptr || weight_bytes == nullptr)
     return fail(FW_EINVAL, "null argument");
@@ -1067,6 +1091,7 @@ int fw_moe_set_prefill_min_tokens(fw_moe* h, int32_t min_tokens) {
   if (min_tokens <= kDecodeMaxTokens && !h->prefill_ok)
     return fail(FW_EINVAL, "this block shape has no prefill path");
   h->prefill_min_tokens = min_tokens;
+  h->prefill_min_set = true;
   return FW_OK;
 }
 

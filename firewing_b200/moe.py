@@ -34,6 +34,10 @@ FW_ENAN = -6
 EP_TRANSPORT_P2P = 0
 EP_TRANSPORT_NCCL = 1
 
+# paths a forward takes (fw_moe_last_path)
+PATH_DECODE = 1
+PATH_PREFILL = 2
+
 _HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -107,6 +111,7 @@ def library() -> ctypes.CDLL:
                                              ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
     L.fw_moe_get_config.argtypes = [vp, ctypes.POINTER(_Config)]
     L.fw_moe_last_union.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_uint64)]
+    L.fw_moe_last_path.argtypes = [vp, ctypes.POINTER(ctypes.c_int32)]
     L.fw_moe_load_expert.argtypes = [vp, ctypes.c_int32, ctypes.c_int32, vp, vp]
     L.fw_moe_load_expert_container.argtypes = [vp, ctypes.c_int32, ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32,
                                                ctypes.POINTER(ctypes.c_int32)]
@@ -129,7 +134,7 @@ def library() -> ctypes.CDLL:
                  "fw_moe_profile", "fw_moe_profile_read", "fw_moe_set_prefill_min_tokens",
                  "fw_ep_unique_id", "fw_moe_ep_init", "fw_moe_load_hc", "fw_moe_forward_hc",
                  "fw_moe_forward_hc_async", "fw_moe_load_layer_safetensors", "fw_moe_load_hc_safetensors",
-                 "fw_safetensors_tensor_info", "fw_moe_get_config", "fw_moe_last_union", "fw_moe_load_expert",
+                 "fw_safetensors_tensor_info", "fw_moe_get_config", "fw_moe_last_union", "fw_moe_last_path", "fw_moe_load_expert",
                  "fw_moe_load_expert_container", "fw_codec_container_check",
                  "fw_linear_bf16", "fw_swiglu_bf16", "fw_add_bf16", "fw_route_bf16", "fw_moe_forward_noalloc",
                  "fw_moe_ep_set_transport", "fw_moe_set_wait_limit", "fw_moe_test_stall"):
@@ -276,6 +281,12 @@ class MoeBlock:
         _check(library().fw_moe_last_union(self._h, ctypes.byref(n), ctypes.byref(b)))
         return {"distinct_experts": int(n.value), "weight_bytes": int(b.value)}
 
+    def last_path(self) -> int:
+        """PATH_DECODE or PATH_PREFILL: the path of this handle's last forward."""
+        v = ctypes.c_int32()
+        _check(library().fw_moe_last_path(self._h, ctypes.byref(v)))
+        return int(v.value)
+
     def load_expert(self, layer: int, expert: int, gate_up, down) -> None:
         """Replace one routed expert of a loaded layer: gate_up [2I][H] and
         down [H][I] (reference layout), host arrays or device tensors."""
@@ -316,7 +327,10 @@ class MoeBlock:
 
     def set_prefill_min_tokens(self, min_tokens: int) -> None:
         """Forwards of at least min_tokens tokens (and all above 256) take the
-        tensor-core prefill path; narrower ones the bit-exact decode path."""
+        tensor-core prefill path; narrower ones the bit-exact decode path.
+        Under expert parallelism the width is tokens x world.  Defaults for
+        shapes with a prefill path: 96 on one GPU, 192 in total under
+        expert parallelism."""
         _check(library().fw_moe_set_prefill_min_tokens(self._h, int(min_tokens)))
 
     def profile(self, enable: bool) -> None:

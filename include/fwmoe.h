@@ -143,10 +143,24 @@ int fw_moe_forward_hc_async(fw_moe* handle, int32_t layer, const uint16_t* post,
  * the tensor cores (f32 accumulation in the tensor core's own order, outputs
  * within the block tolerance of the reference, selection exact).  Narrower
  * forwards run the decode path, which reproduces the reference's dot
- * schedule bit for bit.  Default 257.  No reference counterpart: the
- * reference has one path for every width (src/decoder_layer.rs:460-586).
- * FW_EINVAL when min_tokens <= 256 and the shape has no prefill path. */
+ * schedule bit for bit.  Under expert parallelism the width compared is the
+ * total over the ranks (tokens x world), since each rank's experts see every
+ * rank's tokens.  Default, for a shape with a prefill path, 96 on one GPU
+ * (from about two tokens per expert the tensor cores are faster; measured at
+ * config 0: 205 k against 199 k token-layers/s at T = 96, 468 k against
+ * 272 k at T = 256) and 192 in total under expert parallelism (the prefill
+ * exchange takes more launches); 257 for a shape without one.  A value set
+ * here applies to both.  No reference counterpart: the reference has one path
+ * for every width (src/decoder_layer.rs:460-586).  FW_EINVAL when
+ * min_tokens <= 256 and the shape has no prefill path. */
 int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);
+
+/* Which path the handle's last forward took: FW_PATH_DECODE (bit-exact
+ * dot schedule) or FW_PATH_PREFILL (tensor cores, block tolerance).
+ * FW_EINVAL before the first forward.  No reference counterpart. */
+#define FW_PATH_DECODE 1
+#define FW_PATH_PREFILL 2
+int fw_moe_last_path(fw_moe* handle, int32_t* path);
 
 /* Expert parallelism over the GPUs of one node (no reference counterpart:
  * the reference runs the block on one device).  Rank r of `world` holds the

@@ -32,6 +32,7 @@ CFG0 = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512,
 CFG4 = dict(hidden=3072, intermediate=768, shared_intermediate=768, experts=512, top_k=10)
 
 P2P, NCCL = 0, 1
+PATH_DECODE, PATH_PREFILL = 1, 2  # fw_moe_last_path
 
 
 def _rendezvous() -> str:
@@ -78,11 +79,12 @@ def _rank_main(rank, world, store, shape, t_local, layers, zipf, q, min_tokens, 
             x = x_all[rank * t_local:(rank + 1) * t_local].copy()
             fwd = blk.forward_hc if hc_lowrank else blk.forward
             y1, i1, s1 = fwd(l, x)
+            path = blk.last_path()
             y2, i2, s2 = fwd(l, x)  # repeatable
-            results.append((l, x_all, y1, i1, s1, bool(np.array_equal(y1, y2) and np.array_equal(i1, i2))))
+            results.append((l, x_all, y1, i1, s1, bool(np.array_equal(y1, y2) and np.array_equal(i1, i2)), path))
         blk.close()
         gathered = [None] * world
-        dist.all_gather_object(gathered, [(l, y, i, s, rep) for (l, _, y, i, s, rep) in results])
+        dist.all_gather_object(gathered, [(l, y, i, s, rep) for (l, _, y, i, s, rep, _) in results])
         if rank == 0:
             bshape = O.BlockShape(**shape)
             report = []
@@ -101,7 +103,7 @@ def _rank_main(rank, world, store, shape, t_local, layers, zipf, q, min_tokens, 
                     ry, ridx, rsc = O.block(bshape, layer, x_all, threads=os.cpu_count() or 1)
                 exact = np.all(s == rsc, axis=1)
                 yf, rf = O.bf16_to_f32(y).astype(np.float64), O.bf16_to_f32(ry).astype(np.float64)
-                report.append(dict(idx=bool(np.array_equal(i, ridx)),
+                report.append(dict(path=results[l][6], idx=bool(np.array_equal(i, ridx)),
                                    score_ulp=int(np.abs(s.astype(np.int32) - rsc.astype(np.int32)).max()),
                                    exact_tokens_equal=bool(np.array_equal(y[exact], ry[exact])),
                                    n_exact=int(exact.sum()), repeat=rep,
@@ -140,11 +142,13 @@ def _rank_entry(rank, world, store, shape, t_local, layers, zipf, min_tokens, tr
 
 
 def _decode_ok(r):
-    return r["idx"] and r["score_ulp"] <= 1 and r["exact_tokens_equal"] and r["repeat"]
+    return (r["path"] == PATH_DECODE and r["idx"] and r["score_ulp"] <= 1 and r["exact_tokens_equal"]
+            and r["repeat"])
 
 
 def _prefill_ok(r):
-    return r["idx"] and r["score_ulp"] <= 1 and r["repeat"] and r["max_abs"] <= 2e-2 and r["rel_l2"] <= 1e-3
+    return (r["path"] == PATH_PREFILL and r["idx"] and r["score_ulp"] <= 1 and r["repeat"]
+            and r["max_abs"] <= 2e-2 and r["rel_l2"] <= 1e-3)
 
 
 @pytest.mark.parametrize("transport", [P2P, NCCL])
@@ -173,8 +177,19 @@ def test_ep_two_gpus_prefill(shape, t_local, min_tokens, zipf, transport):
 # Config 0's block at 2, 4 and 8 GPUs on both paths (peer-memory transport).
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_ep_config0_decode(world):
-    for r in _run(CFG0, 16, 2, False, world=world):
+    # 16 tokens per rank, the decode path pinned (a set threshold counts
+    # every rank's tokens too)
+    for r in _run(CFG0, 16, 2, False, min_tokens=1 << 20, world=world):
         assert _decode_ok(r), r
+
+
+# The default path threshold under expert parallelism (192 tokens) counts
+# every rank's tokens: 2 x 96 take the tensor-core path, 2 x 95 the decode
+# path.
+@pytest.mark.parametrize("t_local", [95, 96])
+def test_ep_default_path_counts_all_ranks(t_local):
+    for r in _run(CFG0, t_local, 1, False):
+        assert (_prefill_ok(r) if t_local == 96 else _decode_ok(r)), r
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])

@@ -147,6 +147,9 @@ CFG0 = dict(hidden=2048, intermediate=512, shared_intermediate=512, experts=512,
 def run_pair(shape: dict, seed: int, T: int, zipf: bool = False, x=None, max_tokens=None):
     cfg = fw.MoeConfig(**shape, max_tokens=max_tokens or max(T, 1), layers=1)
     blk = fw.MoeBlock(cfg)
+    # this file checks the bit-exact decode path: pinned up to its 256-token
+    # limit (shapes with a prefill path take it from 96 tokens by default)
+    blk.set_prefill_min_tokens(1 << 20)
     blk.synth_layer(0, seed, 0.02, zipf)
     bshape = O.BlockShape(**shape)
     layer = O.SynthLayer(bshape, seed, 0.02, zipf)

@@ -112,6 +112,29 @@ def test_prefill_and_decode_agree_on_selection():
     assert all(np.array_equal(u, v) for u, v in zip(dec, again))
 
 
+def test_default_path_threshold():
+    # Shapes with a prefill path take it from 96 tokens by default; narrower
+    # forwards keep the bit-exact decode path.
+    cfg = fw.MoeConfig(**CFG0, max_tokens=96, layers=1)
+    blk = fw.MoeBlock(cfg)
+    blk.synth_layer(0, 6, 0.02, False)
+    with pytest.raises(fw.FwError) as e:
+        blk.last_path()
+    assert e.value.code == fw.FW_EINVAL
+    x = O.synth_input(98, 96, CFG0["hidden"])
+    narrow = blk.forward(0, x[:95])
+    assert blk.last_path() == fw.PATH_DECODE
+    wide = blk.forward(0, x)
+    assert blk.last_path() == fw.PATH_PREFILL
+    bshape = O.BlockShape(**CFG0)
+    ref = O.block(bshape, O.SynthLayer(bshape, 6, 0.02, False), x, threads=16, taps=True)
+    assert_prefill_close(wide, ref)
+    ry, ridx, rsc = ref[0][:95], ref[1][:95], ref[2][:95]
+    assert np.array_equal(narrow[1], ridx)
+    exact = np.all(narrow[2] == rsc, axis=1)
+    assert np.array_equal(narrow[0][exact], ry[exact]), "decode path: bit-exact where the scores match"
+
+
 def test_prefill_repeatable_and_nan_rejected():
     blk, x, got, _ = run(SMALL, 13, 300)
     again = blk.forward(0, x)
