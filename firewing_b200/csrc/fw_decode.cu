@@ -846,14 +846,16 @@ __global__ void k_ep_wait_done(EpWaitArgs a) {
 }
 
 // One CTA per token, 8 columns per thread: the slot order, then the
-// weighted rows in groups of 8 (all loads of a group in flight before its
+// weighted rows in groups of G (all loads of a group in flight before its
 // adds), then the shared row.  The adds run in ascending expert id, as the
 // reference accumulates.  Row indices are 32-bit: with 64-bit ones the
-// kernel needed more than 64 registers, and one load group of all ten rows
-// (96 registers, fewer CTAs per SM) measured 0.100 ms at config 2 against
-// 0.088 ms for this form.
-__global__ void __launch_bounds__(512, 2) k_combine(CombineArgs a) {
-  constexpr int G = 8;
+// kernel needed more than 64 registers.  G = 8 for wide forwards; with
+// G = K every row and the shared row travel together (two memory latencies
+// per thread instead of four), which needs 96 registers: at config 2 it
+// measured 0.100 ms against 0.088 ms for G = 8 (fewer CTAs per SM), so it
+// is kept for the narrow forwards whose CTAs all fit on the GPU at once.
+template <int G>
+__global__ void __launch_bounds__(512, G > 8 ? 1 : 2) k_combine(CombineArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   if (a.err != nullptr && ld_volatile_int(a.err) != 0) return;
@@ -864,6 +866,7 @@ __global__ void __launch_bounds__(512, 2) k_combine(CombineArgs a) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] = 0;  // bf16(0.0) pairs
   const int32_t* ss = a.sorted_slot + static_cast<size_t>(t) * a.K;
+  uint4 sv = make_uint4(0u, 0u, 0u, 0u);
   for (int n0 = 0; n0 < a.K; n0 += G) {
     int sl[G];
 #pragma unroll
@@ -880,6 +883,8 @@ __global__ void __launch_bounds__(512, 2) k_combine(CombineArgs a) {
 #pragma unroll
     for (int i = 0; i < G; ++i)
       if (n0 + i < a.K) v[i] = *reinterpret_cast<const uint4*>(a.weighted + static_cast<size_t>(row[i]) * a.H + c);
+    if constexpr (G > 8)  // one group: the shared row travels with it
+      if (n0 + G >= a.K) sv = *reinterpret_cast<const uint4*>(a.gated_sh + static_cast<size_t>(t) * a.H + c);
 #pragma unroll
     for (int i = 0; i < G; ++i) {
       if (n0 + i < a.K) {
@@ -890,7 +895,7 @@ __global__ void __launch_bounds__(512, 2) k_combine(CombineArgs a) {
       }
     }
   }
-  const uint4 sv = *reinterpret_cast<const uint4*>(a.gated_sh + static_cast<size_t>(t) * a.H + c);
+  if constexpr (G <= 8) sv = *reinterpret_cast<const uint4*>(a.gated_sh + static_cast<size_t>(t) * a.H + c);
   const uint32_t o[4] = {add_bf16x2(acc[0], sv.x), add_bf16x2(acc[1], sv.y), add_bf16x2(acc[2], sv.z),
                          add_bf16x2(acc[3], sv.w)};
   *reinterpret_cast<uint4*>(a.y + static_cast<size_t>(t) * a.H + c) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -1119,7 +1124,12 @@ cudaError_t launch_combine(const Shape& s, const Scratch& sc, int T, uint16_t* y
     const cudaError_t e = launch_pdl(k_ep_wait_done, dim3(1), dim3(32), 0, st, EpWaitArgs{*wait, sc.err});
     if (e != cudaSuccess) return e;
   }
-  return launch_pdl(k_combine, dim3(T), dim3(s.H / 8), 0, st, a);
+  // top-10 forwards of at most two CTAs per SM: every row in one load group
+  DeviceAttrs da;
+  const int sms = current_device_attrs(&da) == cudaSuccess ? da.sms : 148;
+  if (s.K == 10 && T <= 2 * sms)
+    return launch_pdl(k_combine<10>, dim3(T), dim3(s.H / 8), 0, st, a);
+  return launch_pdl(k_combine<8>, dim3(T), dim3(s.H / 8), 0, st, a);
 }
 
 cudaError_t launch_block(const Shape& s, const LayerWeights& w, const Luts& luts, const Scratch& sc,
