@@ -562,7 +562,7 @@ def run_ours(args, w: dict, rank: int, world: int, local_rank: int) -> None:
                        "shared_intermediate": w["shared_intermediate"],
                        "parallelism": f"ep{world}" if world > 1 else "single",
                        "path": "decode (CUDA-core dot products in the reference's order, bit-exact)" if decode_path
-                               else "prefill (tcgen05 grouped GEMMs: N x T tokens over the ranks >= 192)",
+                               else "prefill (tcgen05 grouped GEMMs: N x T tokens over the ranks >= 96)",
                        "l2": "no flush: every layer streams >126 MB of distinct weights",
                        "distinct_experts_per_layer_mean_this_gpu": float(np.mean(unique))},
             "stack_tokens_per_s": world * T * args.steps / el,

@@ -164,11 +164,10 @@ constexpr int kDecodeMaxTokens = 256;
 // T = 128: 221 k -> 254 k; T = 192: 250 k -> 360 k; T = 256: 272 k -> 468 k.
 // Two tokens per expert (T * K / E) is where the CUDA-core dot products stop
 // hiding under the weight stream.
+// Under expert parallelism the same default applies to the total over the
+// ranks: the config-1 stack at 2 x 64 tokens measured 314 k token-layers/s
+// on the decode path and 380 k on the tensor-core path.
 constexpr int kPrefillDefaultMin = 96;
-// Under expert parallelism the default counts every rank's tokens and starts
-// at 192 in total (about four tokens per held expert, +44 % on one GPU at
-// T = 192): the prefill exchange takes more launches than the decode one.
-constexpr int kEpPrefillDefaultMin = 192;
 constexpr int kMaxTokens = 16384;
 
 struct fw_moe {
@@ -192,7 +191,6 @@ struct fw_moe {
   bool prefill_ok = false;            // shape supported and scratch maps built
   fw::PrefillScratchMaps pf_maps{};
   int prefill_min_tokens = kDecodeMaxTokens + 1;  // forwards this wide or wider take the prefill path
-  bool prefill_min_set = false;                   // set by fw_moe_set_prefill_min_tokens
   // The last forward (fw_moe_last_union): 0 none, 1 decode (expert schedule),
   // 2 prefill (grouped pair offsets over `last_experts` bank experts).
   int last_path = 0, last_experts = 0;
@@ -517,9 +515,8 @@ int ep_block(fw_moe* h, const OwnedLayer& L, const uint16_t* x, int T_l, uint16_
              cudaStream_t cs, cudaEvent_t* ev, const fw::HcPost* hc, bool* prefill) {
   // The experts of a rank see every rank's tokens: the width that decides
   // the path is the total over the ranks.
-  const int min_total =
-      h->prefill_min_set || !h->prefill_ok ? h->prefill_min_tokens : kEpPrefillDefaultMin;
-  *prefill = T_l > h->ep_decode_max || (L.prefill && static_cast<int64_t>(T_l) * h->ep_world >= min_total);
+  *prefill = T_l > h->ep_decode_max ||
+             (L.prefill && static_cast<int64_t>(T_l) * h->ep_world >= h->prefill_min_tokens);
   if (*prefill && !L.prefill) return fail(FW_EINVAL, "this many tokens need the prefill path, which this handle's shape lacks");
   if (h->p2p != nullptr)
     return *prefill ? ep_prefill_forward_p2p(h, L, x, T_l, y, idx, score, cs, ev, hc)
@@ -1091,7 +1088,6 @@ int fw_moe_set_prefill_min_tokens(fw_moe* h, int32_t min_tokens) {
   if (min_tokens <= kDecodeMaxTokens && !h->prefill_ok)
     return fail(FW_EINVAL, "this block shape has no prefill path");
   h->prefill_min_tokens = min_tokens;
-  h->prefill_min_set = true;
   return FW_OK;
 }
 

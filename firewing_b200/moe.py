@@ -328,9 +328,8 @@ class MoeBlock:
     def set_prefill_min_tokens(self, min_tokens: int) -> None:
         """Forwards of at least min_tokens tokens (and all above 256) take the
         tensor-core prefill path; narrower ones the bit-exact decode path.
-        Under expert parallelism the width is tokens x world.  Defaults for
-        shapes with a prefill path: 96 on one GPU, 192 in total under
-        expert parallelism."""
+        Under expert parallelism the width is tokens x world.  Default 96
+        for shapes with a prefill path."""
         _check(library().fw_moe_set_prefill_min_tokens(self._h, int(min_tokens)))
 
     def profile(self, enable: bool) -> None:

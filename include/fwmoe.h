@@ -145,12 +145,11 @@ int fw_moe_forward_hc_async(fw_moe* handle, int32_t layer, const uint16_t* post,
  * forwards run the decode path, which reproduces the reference's dot
  * schedule bit for bit.  Under expert parallelism the width compared is the
  * total over the ranks (tokens x world), since each rank's experts see every
- * rank's tokens.  Default, for a shape with a prefill path, 96 on one GPU
- * (from about two tokens per expert the tensor cores are faster; measured at
- * config 0: 205 k against 199 k token-layers/s at T = 96, 468 k against
- * 272 k at T = 256) and 192 in total under expert parallelism (the prefill
- * exchange takes more launches); 257 for a shape without one.  A value set
- * here applies to both.  No reference counterpart: the reference has one path
+ * rank's tokens.  Default 96 for a shape with a prefill path (from about
+ * two tokens per expert the tensor cores are faster; measured at config 0:
+ * 205 k against 199 k token-layers/s at T = 96, 468 k against 272 k at
+ * T = 256; two GPUs at 64 tokens each: 380 k against 314 k), 257 for a
+ * shape without one.  No reference counterpart: the reference has one path
  * for every width (src/decoder_layer.rs:460-586).  FW_EINVAL when
  * min_tokens <= 256 and the shape has no prefill path. */
 int fw_moe_set_prefill_min_tokens(fw_moe* handle, int32_t min_tokens);

@@ -183,13 +183,12 @@ def test_ep_config0_decode(world):
         assert _decode_ok(r), r
 
 
-# The default path threshold under expert parallelism (192 tokens) counts
-# every rank's tokens: 2 x 96 take the tensor-core path, 2 x 95 the decode
-# path.
-@pytest.mark.parametrize("t_local", [95, 96])
+# The default path threshold (96 tokens) counts every rank's tokens: 2 x 48
+# take the tensor-core path, 2 x 47 the decode path.
+@pytest.mark.parametrize("t_local", [47, 48])
 def test_ep_default_path_counts_all_ranks(t_local):
     for r in _run(CFG0, t_local, 1, False):
-        assert (_prefill_ok(r) if t_local == 96 else _decode_ok(r)), r
+        assert (_prefill_ok(r) if t_local == 48 else _decode_ok(r)), r
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
